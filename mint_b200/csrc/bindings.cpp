@@ -1,0 +1,68 @@
+// Python bindings of the mint_b200 sm_100a extension (module mint_b200._C).
+#include <torch/extension.h>
+
+#include "host_common.h"
+
+namespace mint {
+void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& D,
+               bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t);
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& scale, double eps, int64_t out_code);
+std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd,
+                                    const at::Tensor& scale, int64_t dx_code);
+std::vector<at::Tensor> add_rmsnorm_fwd(const at::Tensor& res, const at::Tensor& a, const at::Tensor& post,
+                                        const c10::optional<at::Tensor>& pre, double eps, int64_t y_code);
+std::vector<at::Tensor> add_rmsnorm_bwd(const c10::optional<at::Tensor>& dh, const c10::optional<at::Tensor>& dy,
+                                        const at::Tensor& a, const at::Tensor& h, const at::Tensor& rstd_a,
+                                        const at::Tensor& rstd_h, const at::Tensor& post,
+                                        const c10::optional<at::Tensor>& pre);
+std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, int64_t n_q, int64_t n_kv, int64_t Dh,
+                                         const at::Tensor& qs, const at::Tensor& ks, const at::Tensor& cos_t,
+                                         const at::Tensor& sin_t, int64_t start, double eps, bool use_rope);
+std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv,
+                                         const at::Tensor& qkv, const at::Tensor& rq, const at::Tensor& rk,
+                                         const at::Tensor& qs, const at::Tensor& ks, const at::Tensor& cos_t,
+                                         const at::Tensor& sin_t, int64_t n_q, int64_t n_kv, int64_t Dh,
+                                         int64_t start, bool use_rope);
+at::Tensor geglu_fwd(const at::Tensor& ab);
+at::Tensor geglu_bwd(const at::Tensor& dh, const at::Tensor& ab);
+at::Tensor embedding_fwd(const at::Tensor& ids, const at::Tensor& w, int64_t start);
+at::Tensor embedding_bwd(const at::Tensor& dout, const at::Tensor& ids, int64_t rows, int64_t start);
+at::Tensor ce_fused_fwd_bwd(at::Tensor& logits, const at::Tensor& targets, const at::Tensor& mask,
+                            const at::Tensor& denom, int64_t valid, int64_t vstart);
+std::vector<at::Tensor> ce_row_stats(const at::Tensor& logits, const at::Tensor& targets, int64_t valid,
+                                     int64_t vstart);
+void ce_grad_inplace(at::Tensor& logits, const at::Tensor& targets, const at::Tensor& mask, const at::Tensor& lse,
+                     const at::Tensor& denom, int64_t valid, int64_t vstart);
+void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1, double b2,
+                double eps, double wd, int64_t step);
+}  // namespace mint
+
+static int64_t read_status(bool reset) {
+  int dev = 0;
+  MINT_CUDA_CHECK(cudaGetDevice(&dev));
+  return static_cast<int64_t>(mint::read_status_word(dev, reset));
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "mint_b200 sm_100a kernels";
+  m.def("read_status", &read_status, "read (and optionally clear) this device's kernel status word",
+        py::arg("reset") = false);
+  m.def("gemm", &mint::gemm_bf16, "C = alpha * op(A) @ op(B) + beta * D (tcgen05)", py::arg("A"), py::arg("B"),
+        py::arg("C"), py::arg("D"), py::arg("a_kmajor"), py::arg("b_kmajor"), py::arg("alpha") = 1.0,
+        py::arg("beta") = 0.0, py::arg("alpha_t") = py::none());
+  m.def("launch_count", &mint::launch_count, "kernels launched by this extension so far");
+  m.def("rmsnorm_fwd", &mint::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &mint::rmsnorm_bwd);
+  m.def("add_rmsnorm_fwd", &mint::add_rmsnorm_fwd);
+  m.def("add_rmsnorm_bwd", &mint::add_rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &mint::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &mint::qk_norm_rope_bwd);
+  m.def("geglu_fwd", &mint::geglu_fwd);
+  m.def("geglu_bwd", &mint::geglu_bwd);
+  m.def("embedding_fwd", &mint::embedding_fwd);
+  m.def("embedding_bwd", &mint::embedding_bwd);
+  m.def("ce_fused_fwd_bwd", &mint::ce_fused_fwd_bwd);
+  m.def("ce_row_stats", &mint::ce_row_stats);
+  m.def("ce_grad_inplace", &mint::ce_grad_inplace);
+  m.def("adamw_step", &mint::adamw_step);
+}

@@ -1,0 +1,388 @@
+// Persistent, warp-specialized tcgen05 GEMM for sm_100a:  C = alpha * op(A) @ op(B) + beta * D.
+//
+// Layout: row-major with A [M,K] (K-major) or [K,M] (MN-major), B [N,K] (K-major) or [K,N]
+// (MN-major); no operand is ever transposed in memory: the TMA boxes and the UMMA shared-memory
+// descriptors describe either major-ness directly.
+//
+// One CTA per SM, 192 threads:
+//   warp 0      TMA producer: 128B-swizzled A/B tiles (BK = 64) into a kStages-deep ring
+//   warp 1      TMEM allocation + single-thread tcgen05.mma issue (M = 128, N = BN, K = 16)
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (32 lanes x 32 columns per load),
+//               alpha / beta*D, conversion and global stores
+// The fp32 accumulator is double-buffered in tensor memory (2 x BN columns) so the epilogue of
+// tile t overlaps the MMAs of tile t+1. Every mbarrier wait is bounded (common.cuh); on a
+// timeout the kernel records a status code, drains its in-flight MMAs, frees TMEM and exits.
+#include "common.cuh"
+#include "host_common.h"
+
+namespace mint {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+};
+
+struct Params {
+  void* C;
+  const void* D;
+  int M, N, K;
+  long long ldc, ldd;
+  float alpha, beta;
+  const float* alpha_ptr;
+  int c_fp32, d_fp32;
+  int tiles_m, tiles_n;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  constexpr int G = 8;  // groups of 8 M-tiles sweep all N-tiles: B tiles stay hot in L2
+  const int per_group = G * tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * G;
+  const int gsize = min(tiles_m - first_m, G);
+  const int r = tile % per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, Params p) {
+  using C_ = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C_::kStages * C_::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::kStages * C_::kStageBytes);
+  uint64_t* empty = full + C_::kStages;
+  uint64_t* tfull = empty + C_::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C_::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C_::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tma);
+      tma_prefetch_desc(&tmb);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C_::kStageBytes);
+          uint8_t* a_dst = sA + stage * C_::kABytes;
+          uint8_t* b_dst = sB + stage * C_::kBBytes;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tma, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BM / 64; ++i) tma_load_2d(a_dst + i * 8192, &tma, &full[stage], m0 + i * 64, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmb, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i) tma_load_2d(b_dst + i * 8192, &tmb, &full[stage], n0 + i * 64, k0);
+          }
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // let any TMA copy already in flight land before the CTA's shared memory goes away
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+        const int acc = t & 1;
+        const uint32_t acc_phase = (t >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, kStatusTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C_::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * C_::kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major SW128: step 16 elements = 32 bytes inside the swizzle atom (SBO = 8 rows x 128 B).
+            // MN-major SW128: step 16 K-rows = 2048 bytes; LBO = 8 KB between 64-wide MN atoms.
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a_addr + k * 2048, 8192, 1024)
+                                        : umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, 8192, 1024)
+                                        : umma_desc_sw128(b_addr + k * 32, 16, 1024);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+      // drain: every MMA issued by this thread completes before TMEM is released
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, kStatusTimeoutMma, nullptr);
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    float alpha = p.alpha;
+    if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+      const int acc = t & 1;
+      const uint32_t acc_phase = (t >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      const int row = tm * BM + row_in_tile;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = tn * BN + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
+        const bool full_chunk = col0 + 32 <= p.N;
+        if (p.D != nullptr && p.beta != 0.0f) {
+          if (p.d_fp32) {
+            const float* dp = static_cast<const float*>(p.D) + static_cast<long long>(row) * p.ldd + col0;
+            if (full_chunk) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 d4 = *reinterpret_cast<const float4*>(dp + j);
+                v[j] += p.beta * d4.x;
+                v[j + 1] += p.beta * d4.y;
+                v[j + 2] += p.beta * d4.z;
+                v[j + 3] += p.beta * d4.w;
+              }
+            } else {
+              for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * dp[j];
+            }
+          } else {
+            const __nv_bfloat16* dp =
+                static_cast<const __nv_bfloat16*>(p.D) + static_cast<long long>(row) * p.ldd + col0;
+            if (full_chunk) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                const uint4 u = *reinterpret_cast<const uint4*>(dp + j);
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __bfloat1622float2(h[e]);
+                  v[j + 2 * e] += p.beta * f.x;
+                  v[j + 2 * e + 1] += p.beta * f.y;
+                }
+              }
+            } else {
+              for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * __bfloat162float(dp[j]);
+            }
+          }
+        }
+        if (p.c_fp32) {
+          float* cp = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col0;
+          if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(cp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < p.N; ++j) cp[j] = v[j];
+          }
+        } else {
+          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col0;
+          if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 u;
+              u.x = pack_bf16x2(v[j], v[j + 1]);
+              u.y = pack_bf16x2(v[j + 2], v[j + 3]);
+              u.z = pack_bf16x2(v[j + 4], v[j + 5]);
+              u.w = pack_bf16x2(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4*>(cp + j) = u;
+            }
+          } else {
+            for (int j = 0; j < 32 && col0 + j < p.N; ++j) cp[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::kTmemCols);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int sms, cudaStream_t stream) {
+  using C_ = Cfg<BN>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  static bool configured = false;
+  if (!configured) {
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes));
+    configured = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, p);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace gemm
+
+// C = alpha * op(A) @ op(B) + beta * D.  a_kmajor: A stored [M,K]; else [K,M].  b_kmajor: B stored [N,K]; else [K,N].
+void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& D,
+               bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(C, "C");
+  MINT_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm expects 2-D tensors");
+  MINT_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
+  MINT_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm operands need unit inner stride");
+  MINT_CHECK(C.scalar_type() == at::kBFloat16 || C.scalar_type() == at::kFloat, "C must be bf16 or fp32");
+  const int64_t M = a_kmajor ? A.size(0) : A.size(1);
+  const int64_t K = a_kmajor ? A.size(1) : A.size(0);
+  const int64_t N = b_kmajor ? B.size(0) : B.size(1);
+  const int64_t KB = b_kmajor ? B.size(1) : B.size(0);
+  MINT_CHECK(K == KB, "gemm K mismatch ", K, " vs ", KB);
+  MINT_CHECK(C.size(0) == M && C.size(1) == N, "C has shape ", C.sizes(), ", expected [", M, ", ", N, "]");
+  MINT_CHECK(C.stride(0) % (C.scalar_type() == at::kFloat ? 4 : 8) == 0, "C row stride must be 16-byte aligned");
+  MINT_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm dims too large");
+  c10::cuda::CUDAGuard guard(A.device());
+  const int dev = A.get_device();
+  auto stream = at::cuda::getCurrentCUDAStream();
+
+  gemm::Params p{};
+  p.C = C.data_ptr();
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.ldc = C.stride(0);
+  p.alpha = static_cast<float>(alpha);
+  p.beta = static_cast<float>(beta);
+  p.c_fp32 = C.scalar_type() == at::kFloat;
+  p.status = status_ptr(dev);
+  if (D.has_value() && D->defined() && beta != 0.0) {
+    check_cuda(*D, "D");
+    MINT_CHECK(D->dim() == 2 && D->size(0) == M && D->size(1) == N && D->stride(1) == 1, "D must match C");
+    MINT_CHECK(D->scalar_type() == at::kFloat || D->scalar_type() == at::kBFloat16, "D must be bf16 or fp32");
+    MINT_CHECK(D->stride(0) % (D->scalar_type() == at::kFloat ? 4 : 8) == 0, "D row stride must be 16-byte aligned");
+    p.D = D->data_ptr();
+    p.ldd = D->stride(0);
+    p.d_fp32 = D->scalar_type() == at::kFloat;
+  }
+  if (alpha_t.has_value() && alpha_t->defined()) {
+    MINT_CHECK(alpha_t->scalar_type() == at::kFloat && alpha_t->numel() == 1 && alpha_t->is_cuda(),
+               "alpha tensor must be a 1-element fp32 CUDA tensor");
+    p.alpha_ptr = alpha_t->data_ptr<float>();
+  }
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    // empty contraction: C = beta * D
+    if (p.D != nullptr) {
+      C.copy_(D->to(C.scalar_type()).mul(beta));
+    } else {
+      C.zero_();
+    }
+    return;
+  }
+  const int sms = num_sms(dev);
+  const int64_t tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
+  const bool use256 = N > 128 && tiles256 >= sms;
+  const int BN = use256 ? 256 : 128;
+  p.tiles_m = static_cast<int>((M + 127) / 128);
+  p.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  const int64_t lda = A.stride(0), ldb = B.stride(0);
+  const CUtensorMap ta = a_kmajor ? make_tmap_2d_bf16(A.data_ptr(), M, K, lda, 128, 64, true)
+                                  : make_tmap_2d_bf16(A.data_ptr(), K, M, lda, 64, 64, true);
+  const CUtensorMap tb = b_kmajor ? make_tmap_2d_bf16(B.data_ptr(), N, K, ldb, BN, 64, true)
+                                  : make_tmap_2d_bf16(B.data_ptr(), K, N, ldb, 64, 64, true);
+  const bool a_mn = !a_kmajor, b_mn = !b_kmajor;
+#define MINT_GEMM_DISPATCH(BNV)                                                  \
+  if (!a_mn && !b_mn) gemm::launch<BNV, false, false>(ta, tb, p, sms, stream);   \
+  else if (!a_mn && b_mn) gemm::launch<BNV, false, true>(ta, tb, p, sms, stream); \
+  else if (a_mn && !b_mn) gemm::launch<BNV, true, false>(ta, tb, p, sms, stream); \
+  else gemm::launch<BNV, true, true>(ta, tb, p, sms, stream);
+  if (BN == 256) {
+    MINT_GEMM_DISPATCH(256)
+  } else {
+    MINT_GEMM_DISPATCH(128)
+  }
+#undef MINT_GEMM_DISPATCH
+}
+
+}  // namespace mint

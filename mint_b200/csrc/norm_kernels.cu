@@ -1,0 +1,517 @@
+// Row-wise normalization kernels (memory bound, one warp per row, fp32 math):
+//   rmsnorm           y = x * rsqrt(mean(x^2) + eps) * (1 + scale)
+//   add_rmsnorm       h = res + bf16(rmsnorm(a; post)),  y = rmsnorm(h; pre)   (sandwich-norm block update)
+//   qk_norm_rope      per-head RMSNorm of q and k + half-split rotary embedding, splitting the fused QKV output
+// Backward kernels reduce the scale gradients per CTA in shared memory, then one atomicAdd per
+// column per CTA into an fp32 accumulator.
+#include "common.cuh"
+#include "host_common.h"
+
+namespace mint {
+namespace {
+
+constexpr int kRowsPerBlock = 8;  // 8 warps
+constexpr int kMaxD = 4096;
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const Tin* __restrict__ x, const float* __restrict__ scale,
+                                                          Tout* __restrict__ y, float* __restrict__ rstd_out, int rows,
+                                                          int D, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerBlock + warp;
+  if (row >= rows) return;
+  const Tin* xr = x + static_cast<long long>(row) * D;
+  float ss = 0.f;
+  for (int j = lane; j < D; j += 32) {
+    const float v = to_f32(xr[j]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / D + eps);
+  Tout* yr = y + static_cast<long long>(row) * D;
+  for (int j = lane; j < D; j += 32) yr[j] = from_f32<Tout>(to_f32(xr[j]) * r * (1.f + scale[j]));
+  if (lane == 0) rstd_out[row] = r;
+}
+
+// dx = r * w * dy - x * r^3 * mean(dy * w * x);  dscale += dy * x * r
+template <typename Tin, typename Tdy, typename Tdx>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const Tdy* __restrict__ dy, const Tin* __restrict__ x,
+                                                          const float* __restrict__ rstd,
+                                                          const float* __restrict__ scale, Tdx* __restrict__ dx,
+                                                          float* __restrict__ dscale, int rows, int D) {
+  extern __shared__ float s_ds[];  // [nwarps][D], each lane owns distinct columns of its warp's row
+  const int nwarps = blockDim.x >> 5;
+  for (int j = threadIdx.x; j < nwarps * D; j += blockDim.x) s_ds[j] = 0.f;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* my = s_ds + warp * D;
+  for (int row = blockIdx.x * nwarps + warp; row < rows; row += gridDim.x * nwarps) {
+    const Tin* xr = x + static_cast<long long>(row) * D;
+    const Tdy* dyr = dy + static_cast<long long>(row) * D;
+    const float r = rstd[row];
+    float dot = 0.f;
+    for (int j = lane; j < D; j += 32) dot += to_f32(dyr[j]) * (1.f + scale[j]) * to_f32(xr[j]);
+    dot = warp_sum(dot) / D;
+    Tdx* dxr = dx + static_cast<long long>(row) * D;
+    for (int j = lane; j < D; j += 32) {
+      const float xv = to_f32(xr[j]), g = to_f32(dyr[j]);
+      dxr[j] = from_f32<Tdx>(r * (1.f + scale[j]) * g - xv * r * r * r * dot);
+      my[j] += g * xv * r;
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float t = 0.f;
+    for (int w = 0; w < nwarps; ++w) t += s_ds[w * D + j];
+    atomicAdd(&dscale[j], t);
+  }
+}
+
+// h = res + bf16(rms(a) * (1 + post));  y = rms(h) * (1 + pre)  (y optional)
+template <typename Ty>
+__global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const float* __restrict__ res,
+                                                              const __nv_bfloat16* __restrict__ a,
+                                                              const float* __restrict__ post,
+                                                              const float* __restrict__ pre, float* __restrict__ h,
+                                                              Ty* __restrict__ y, float* __restrict__ rstd_a,
+                                                              float* __restrict__ rstd_h, int rows, int D, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerBlock + warp;
+  if (row >= rows) return;
+  const long long off = static_cast<long long>(row) * D;
+  float ss = 0.f;
+  for (int j = lane; j < D; j += 32) {
+    const float v = __bfloat162float(a[off + j]);
+    ss += v * v;
+  }
+  const float ra = rsqrtf(warp_sum(ss) / D + eps);
+  float sh = 0.f;
+  for (int j = lane; j < D; j += 32) {
+    const float n = __bfloat162float(__float2bfloat16_rn(__bfloat162float(a[off + j]) * ra * (1.f + post[j])));
+    const float hv = res[off + j] + n;
+    h[off + j] = hv;
+    sh += hv * hv;
+  }
+  if (lane == 0) rstd_a[row] = ra;
+  if (pre != nullptr) {
+    const float rh = rsqrtf(warp_sum(sh) / D + eps);
+    __syncwarp();
+    for (int j = lane; j < D; j += 32) y[off + j] = from_f32<Ty>(h[off + j] * rh * (1.f + pre[j]));
+    if (lane == 0) rstd_h[row] = rh;
+  }
+}
+
+// dres = dh + rmsnorm_bwd(dy; h, pre);  da = rmsnorm_bwd(dres; a, post)
+template <typename Ty>
+__global__ void __launch_bounds__(256) add_rmsnorm_bwd_kernel(
+    const float* __restrict__ dh, const Ty* __restrict__ dy, const __nv_bfloat16* __restrict__ a,
+    const float* __restrict__ h, const float* __restrict__ rstd_a, const float* __restrict__ rstd_h,
+    const float* __restrict__ post, const float* __restrict__ pre, float* __restrict__ dres,
+    __nv_bfloat16* __restrict__ da, float* __restrict__ dpost, float* __restrict__ dpre, int rows, int D) {
+  extern __shared__ float s_acc[];  // [nwarps][2 * D]: dpost, dpre per warp
+  const int nwarps = blockDim.x >> 5;
+  for (int j = threadIdx.x; j < nwarps * 2 * D; j += blockDim.x) s_acc[j] = 0.f;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* my = s_acc + warp * 2 * D;
+  for (int row = blockIdx.x * nwarps + warp; row < rows; row += gridDim.x * nwarps) {
+    const long long off = static_cast<long long>(row) * D;
+    // 1) gradient into h: dh + d(y)/d(h)
+    if (dy != nullptr && pre != nullptr) {
+      const float rh = rstd_h[row];
+      float dot = 0.f;
+      for (int j = lane; j < D; j += 32) dot += to_f32(dy[off + j]) * (1.f + pre[j]) * h[off + j];
+      dot = warp_sum(dot) / D;
+      for (int j = lane; j < D; j += 32) {
+        const float g = to_f32(dy[off + j]), hv = h[off + j];
+        const float v = rh * (1.f + pre[j]) * g - hv * rh * rh * rh * dot + (dh != nullptr ? dh[off + j] : 0.f);
+        dres[off + j] = v;
+        my[D + j] += g * hv * rh;
+      }
+    } else {
+      for (int j = lane; j < D; j += 32) dres[off + j] = dh != nullptr ? dh[off + j] : 0.f;
+    }
+    __syncwarp();
+    // 2) gradient into a through the post norm (dn = dres)
+    const float ra = rstd_a[row];
+    float dot = 0.f;
+    for (int j = lane; j < D; j += 32) dot += dres[off + j] * (1.f + post[j]) * __bfloat162float(a[off + j]);
+    dot = warp_sum(dot) / D;
+    for (int j = lane; j < D; j += 32) {
+      const float g = dres[off + j], av = __bfloat162float(a[off + j]);
+      da[off + j] = __float2bfloat16_rn(ra * (1.f + post[j]) * g - av * ra * ra * ra * dot);
+      my[j] += g * av * ra;
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float tp = 0.f, tq = 0.f;
+    for (int w = 0; w < nwarps; ++w) {
+      tp += s_acc[w * 2 * D + j];
+      tq += s_acc[w * 2 * D + D + j];
+    }
+    atomicAdd(&dpost[j], tp);
+    if (dpre != nullptr) atomicAdd(&dpre[j], tq);
+  }
+}
+
+// One warp per (token, head) row of q or k; v heads are copied. Rows ordered token-major.
+// qkv [M, (Hq + 2 Hkv) * Dh]; q [M, Hq, Dh]; k, v [M, Hkv, Dh]. Position of token m = start + (m % T).
+__global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
+    const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ qs, const float* __restrict__ ks,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ q,
+    __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v, float* __restrict__ rq, float* __restrict__ rk,
+    int M, int T, int Hq, int Hkv, int Dh, int start, int use_rope, float eps) {
+  extern __shared__ float s_row[];  // [8][Dh]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = Hq + 2 * Hkv;
+  const long long item = static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp;
+  if (item >= static_cast<long long>(M) * H) return;
+  const int m = static_cast<int>(item / H);
+  const int hh = static_cast<int>(item % H);
+  const __nv_bfloat16* src = qkv + static_cast<long long>(m) * H * Dh + static_cast<long long>(hh) * Dh;
+  if (hh >= Hq + Hkv) {  // v: copy
+    __nv_bfloat16* dst = v + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh;
+    for (int j = lane; j < Dh; j += 32) dst[j] = src[j];
+    return;
+  }
+  const bool is_q = hh < Hq;
+  const float* sc = is_q ? qs : ks;
+  float* buf = s_row + warp * Dh;
+  float ss = 0.f;
+  for (int j = lane; j < Dh; j += 32) {
+    const float x = __bfloat162float(src[j]);
+    ss += x * x;
+  }
+  const float r = rsqrtf(warp_sum(ss) / Dh + eps);
+  for (int j = lane; j < Dh; j += 32) buf[j] = __bfloat162float(src[j]) * r * (1.f + sc[j]);
+  __syncwarp();
+  __nv_bfloat16* dst = is_q ? q + (static_cast<long long>(m) * Hq + hh) * Dh
+                            : k + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh;
+  const int half = Dh / 2;
+  const int pos = start + (m % T);
+  for (int j = lane; j < Dh; j += 32) {
+    float out = buf[j];
+    if (use_rope) {
+      const int i = j < half ? j : j - half;
+      const float c = cos_t[static_cast<long long>(pos) * half + i];
+      const float s = sin_t[static_cast<long long>(pos) * half + i];
+      out = j < half ? buf[j] * c - buf[j + half] * s : buf[j - half] * s + buf[j] * c;
+    }
+    dst[j] = __float2bfloat16_rn(out);
+  }
+  if (lane == 0) (is_q ? rq : rk)[static_cast<long long>(m) * (is_q ? Hq : Hkv) + (is_q ? hh : hh - Hq)] = r;
+}
+
+__global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(
+    const __nv_bfloat16* __restrict__ dq, const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv,
+    const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ rq, const float* __restrict__ rk,
+    const float* __restrict__ qs, const float* __restrict__ ks, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dqs,
+    float* __restrict__ dks, int M, int T, int Hq, int Hkv, int Dh, int start, int use_rope) {
+  extern __shared__ float smem[];  // [8][Dh] grads + [8][2][Dh] per-warp scale accumulators
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* s_acc = smem + kRowsPerBlock * Dh;
+  for (int j = threadIdx.x; j < kRowsPerBlock * 2 * Dh; j += blockDim.x) s_acc[j] = 0.f;
+  __syncthreads();
+  float* s_dq = s_acc + warp * 2 * Dh;
+  float* s_dk = s_dq + Dh;
+  const int H = Hq + 2 * Hkv;
+  const long long total = static_cast<long long>(M) * H;
+  const int half = Dh / 2;
+  float* buf = smem + warp * Dh;
+  for (long long item = static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp; item < total;
+       item += static_cast<long long>(gridDim.x) * kRowsPerBlock) {
+    const int m = static_cast<int>(item / H);
+    const int hh = static_cast<int>(item % H);
+    __nv_bfloat16* out = dqkv + static_cast<long long>(m) * H * Dh + static_cast<long long>(hh) * Dh;
+    if (hh >= Hq + Hkv) {
+      const __nv_bfloat16* g = dv + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh;
+      for (int j = lane; j < Dh; j += 32) out[j] = g[j];
+      continue;
+    }
+    const bool is_q = hh < Hq;
+    const __nv_bfloat16* g = is_q ? dq + (static_cast<long long>(m) * Hq + hh) * Dh
+                                  : dk + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh;
+    const float* sc = is_q ? qs : ks;
+    const float r = is_q ? rq[static_cast<long long>(m) * Hq + hh] : rk[static_cast<long long>(m) * Hkv + (hh - Hq)];
+    const int pos = start + (m % T);
+    // un-rotate the incoming gradient
+    __syncwarp();
+    for (int j = lane; j < Dh; j += 32) {
+      float gn = __bfloat162float(g[j]);
+      if (use_rope) {
+        const int i = j < half ? j : j - half;
+        const float c = cos_t[static_cast<long long>(pos) * half + i];
+        const float s = sin_t[static_cast<long long>(pos) * half + i];
+        gn = j < half ? __bfloat162float(g[j]) * c + __bfloat162float(g[j + half]) * s
+                      : -__bfloat162float(g[j - half]) * s + __bfloat162float(g[j]) * c;
+      }
+      buf[j] = gn;
+    }
+    __syncwarp();
+    const __nv_bfloat16* x = qkv + static_cast<long long>(m) * H * Dh + static_cast<long long>(hh) * Dh;
+    float dot = 0.f;
+    for (int j = lane; j < Dh; j += 32) dot += buf[j] * (1.f + sc[j]) * __bfloat162float(x[j]);
+    dot = warp_sum(dot) / Dh;
+    float* acc = is_q ? s_dq : s_dk;
+    for (int j = lane; j < Dh; j += 32) {
+      const float xv = __bfloat162float(x[j]);
+      out[j] = __float2bfloat16_rn(r * (1.f + sc[j]) * buf[j] - xv * r * r * r * dot);
+      acc[j] += buf[j] * xv * r;
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < Dh; j += blockDim.x) {
+    float tq = 0.f, tk = 0.f;
+    for (int w = 0; w < kRowsPerBlock; ++w) {
+      tq += s_acc[w * 2 * Dh + j];
+      tk += s_acc[w * 2 * Dh + Dh + j];
+    }
+    atomicAdd(&dqs[j], tq);
+    atomicAdd(&dks[j], tk);
+  }
+}
+
+int bwd_grid(int rows, int dev, int nwarps) {
+  const int want = (rows + nwarps - 1) / nwarps;
+  const int cap = num_sms(dev) * 4;
+  return want < cap ? want : cap;
+}
+
+// warps per CTA such that nwarps * floats_per_warp fp32 accumulators fit in ~192 KB of shared memory
+int bwd_warps(int floats_per_warp) {
+  int w = 8;
+  while (w > 1 && static_cast<long long>(w) * floats_per_warp * 4 > 192 * 1024) w >>= 1;
+  return w;
+}
+
+}  // namespace
+
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& scale, double eps, int64_t out_code) {
+  check_contig(x, "x");
+  check_contig(scale, "scale");
+  MINT_CHECK(scale.scalar_type() == at::kFloat, "RMSNorm scale must be fp32");
+  const int D = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / D);
+  MINT_CHECK(scale.numel() == D, "scale size mismatch");
+  const auto out_dt = out_code == 0 ? at::kFloat : (out_code == 1 ? at::kBFloat16 : at::kHalf);
+  auto y = at::empty(x.sizes(), x.options().dtype(out_dt));
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {y, rstd};
+  c10::cuda::CUDAGuard g(x.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+#define LAUNCH(TI, TO) \
+  rmsnorm_fwd_kernel<TI, TO><<<grid, 256, 0, st>>>(reinterpret_cast<const TI*>(x.data_ptr()), scale.data_ptr<float>(), \
+                                                  reinterpret_cast<TO*>(y.data_ptr()), rstd.data_ptr<float>(), rows, D, \
+                                                  static_cast<float>(eps))
+  if (x.scalar_type() == at::kFloat) {
+    if (out_dt == at::kFloat) LAUNCH(float, float);
+    else LAUNCH(float, __nv_bfloat16);
+  } else {
+    MINT_CHECK(x.scalar_type() == at::kBFloat16, "rmsnorm input must be fp32 or bf16");
+    if (out_dt == at::kFloat) LAUNCH(__nv_bfloat16, float);
+    else LAUNCH(__nv_bfloat16, __nv_bfloat16);
+  }
+#undef LAUNCH
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd,
+                                    const at::Tensor& scale, int64_t dx_code) {
+  check_contig(dy, "dy");
+  check_contig(x, "x");
+  const int D = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / D);
+  MINT_CHECK(D <= kMaxD, "rmsnorm D too large");
+  const auto dx_dt = dx_code == 0 ? at::kFloat : at::kBFloat16;
+  auto dx = at::empty(x.sizes(), x.options().dtype(dx_dt));
+  auto dscale = at::zeros({D}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {dx, dscale};
+  c10::cuda::CUDAGuard g(x.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int nw = bwd_warps(D);
+  const int grid = bwd_grid(rows, x.get_device(), nw);
+  const size_t sm = static_cast<size_t>(nw) * D * sizeof(float);
+  static bool attr_set = false;
+  if (!attr_set) {
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<float, float, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<float, __nv_bfloat16, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<__nv_bfloat16, float, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<float, __nv_bfloat16, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<__nv_bfloat16, __nv_bfloat16, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<float, float, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<__nv_bfloat16, float, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_set = true;
+  }
+#define LAUNCH(TI, TDY, TDX)                                                                                   \
+  rmsnorm_bwd_kernel<TI, TDY, TDX><<<grid, nw * 32, sm, st>>>(                                                     \
+      reinterpret_cast<const TDY*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), rstd.data_ptr<float>(), \
+      scale.data_ptr<float>(), reinterpret_cast<TDX*>(dx.data_ptr()), dscale.data_ptr<float>(), rows, D)
+  const bool xf = x.scalar_type() == at::kFloat, dyf = dy.scalar_type() == at::kFloat, dxf = dx_dt == at::kFloat;
+  if (xf && dyf && dxf) LAUNCH(float, float, float);
+  else if (xf && !dyf && dxf) LAUNCH(float, __nv_bfloat16, float);
+  else if (!xf && !dyf && !dxf) LAUNCH(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
+  else if (!xf && dyf && !dxf) LAUNCH(__nv_bfloat16, float, __nv_bfloat16);
+  else if (xf && !dyf && !dxf) LAUNCH(float, __nv_bfloat16, __nv_bfloat16);
+  else if (!xf && !dyf && dxf) LAUNCH(__nv_bfloat16, __nv_bfloat16, float);
+  else if (xf && dyf && !dxf) LAUNCH(float, float, __nv_bfloat16);
+  else LAUNCH(__nv_bfloat16, float, float);
+#undef LAUNCH
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {dx, dscale};
+}
+
+std::vector<at::Tensor> add_rmsnorm_fwd(const at::Tensor& res, const at::Tensor& a, const at::Tensor& post,
+                                        const c10::optional<at::Tensor>& pre, double eps, int64_t y_code) {
+  check_contig(res, "res");
+  check_contig(a, "a");
+  MINT_CHECK(res.scalar_type() == at::kFloat && a.scalar_type() == at::kBFloat16, "add_rmsnorm: res fp32, a bf16");
+  const int D = static_cast<int>(res.size(-1));
+  const int rows = static_cast<int>(res.numel() / D);
+  auto h = at::empty_like(res);
+  const bool has_pre = pre.has_value() && pre->defined();
+  const auto y_dt = y_code == 0 ? at::kFloat : at::kBFloat16;
+  auto y = has_pre ? at::empty(res.sizes(), res.options().dtype(y_dt)) : at::empty({0}, res.options());
+  auto ra = at::empty({rows}, res.options());
+  auto rh = at::empty({has_pre ? rows : 0}, res.options());
+  if (rows == 0) return {h, y, ra, rh};
+  c10::cuda::CUDAGuard g(res.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+  const float* pre_p = has_pre ? pre->data_ptr<float>() : nullptr;
+  if (y_dt == at::kFloat) {
+    add_rmsnorm_fwd_kernel<float><<<grid, 256, 0, st>>>(
+        res.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()), post.data_ptr<float>(), pre_p,
+        h.data_ptr<float>(), has_pre ? y.data_ptr<float>() : nullptr, ra.data_ptr<float>(),
+        has_pre ? rh.data_ptr<float>() : nullptr, rows, D, static_cast<float>(eps));
+  } else {
+    add_rmsnorm_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        res.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()), post.data_ptr<float>(), pre_p,
+        h.data_ptr<float>(), has_pre ? reinterpret_cast<__nv_bfloat16*>(y.data_ptr()) : nullptr, ra.data_ptr<float>(),
+        has_pre ? rh.data_ptr<float>() : nullptr, rows, D, static_cast<float>(eps));
+  }
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {h, y, ra, rh};
+}
+
+std::vector<at::Tensor> add_rmsnorm_bwd(const c10::optional<at::Tensor>& dh, const c10::optional<at::Tensor>& dy,
+                                        const at::Tensor& a, const at::Tensor& h, const at::Tensor& rstd_a,
+                                        const at::Tensor& rstd_h, const at::Tensor& post,
+                                        const c10::optional<at::Tensor>& pre) {
+  check_contig(a, "a");
+  check_contig(h, "h");
+  const int D = static_cast<int>(h.size(-1));
+  const int rows = static_cast<int>(h.numel() / D);
+  MINT_CHECK(D <= kMaxD, "add_rmsnorm D too large");
+  auto dres = at::empty_like(h);
+  auto da = at::empty_like(a);
+  auto dpost = at::zeros({D}, h.options());
+  const bool has_pre = pre.has_value() && pre->defined();
+  auto dpre = at::zeros({has_pre ? D : 0}, h.options());
+  if (rows == 0) return {dres, da, dpost, dpre};
+  c10::cuda::CUDAGuard g(h.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int nw = bwd_warps(2 * D);
+  const int grid = bwd_grid(rows, h.get_device(), nw);
+  const size_t sm = static_cast<size_t>(nw) * 2 * D * sizeof(float);
+  static bool attr_set = false;
+  if (!attr_set) {
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(add_rmsnorm_bwd_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(add_rmsnorm_bwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_set = true;
+  }
+  const float* dh_p = (dh.has_value() && dh->defined()) ? dh->data_ptr<float>() : nullptr;
+  const bool has_dy = dy.has_value() && dy->defined() && has_pre;
+  if (!has_dy || dy->scalar_type() == at::kBFloat16) {
+    add_rmsnorm_bwd_kernel<__nv_bfloat16><<<grid, nw * 32, sm, st>>>(
+        dh_p, has_dy ? reinterpret_cast<const __nv_bfloat16*>(dy->data_ptr()) : nullptr,
+        reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()), h.data_ptr<float>(), rstd_a.data_ptr<float>(),
+        has_pre ? rstd_h.data_ptr<float>() : nullptr, post.data_ptr<float>(), has_pre ? pre->data_ptr<float>() : nullptr,
+        dres.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(da.data_ptr()), dpost.data_ptr<float>(),
+        has_pre ? dpre.data_ptr<float>() : nullptr, rows, D);
+  } else {
+    add_rmsnorm_bwd_kernel<float><<<grid, nw * 32, sm, st>>>(
+        dh_p, dy->data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()), h.data_ptr<float>(),
+        rstd_a.data_ptr<float>(), rstd_h.data_ptr<float>(), post.data_ptr<float>(), pre->data_ptr<float>(),
+        dres.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(da.data_ptr()), dpost.data_ptr<float>(),
+        dpre.data_ptr<float>(), rows, D);
+  }
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {dres, da, dpost, dpre};
+}
+
+std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, int64_t n_q, int64_t n_kv, int64_t Dh,
+                                         const at::Tensor& qs, const at::Tensor& ks, const at::Tensor& cos_t,
+                                         const at::Tensor& sin_t, int64_t start, double eps, bool use_rope) {
+  check_contig(qkv, "qkv");
+  MINT_CHECK(qkv.dim() == 3 && qkv.scalar_type() == at::kBFloat16, "qkv must be [B, T, H*D] bf16");
+  const int B = static_cast<int>(qkv.size(0)), T = static_cast<int>(qkv.size(1));
+  MINT_CHECK(qkv.size(2) == (n_q + 2 * n_kv) * Dh, "qkv width mismatch");
+  MINT_CHECK(Dh % 2 == 0 && Dh <= 1024, "head_dim must be even and <= 1024");
+  if (use_rope) MINT_CHECK(cos_t.size(0) >= start + T && cos_t.size(1) == Dh / 2, "rope table too small");
+  const int M = B * T;
+  auto opts = qkv.options();
+  auto q = at::empty({B, T, n_q, Dh}, opts);
+  auto k = at::empty({B, T, n_kv, Dh}, opts);
+  auto v = at::empty({B, T, n_kv, Dh}, opts);
+  auto rq = at::empty({M, n_q}, opts.dtype(at::kFloat));
+  auto rk = at::empty({M, n_kv}, opts.dtype(at::kFloat));
+  const long long items = static_cast<long long>(M) * (n_q + 2 * n_kv);
+  if (items == 0) return {q, k, v, rq, rk};
+  c10::cuda::CUDAGuard g(qkv.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = static_cast<int>((items + kRowsPerBlock - 1) / kRowsPerBlock);
+  qk_norm_rope_fwd_kernel<<<grid, 256, kRowsPerBlock * Dh * sizeof(float), st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qs.data_ptr<float>(), ks.data_ptr<float>(),
+      cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(k.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v.data_ptr()),
+      rq.data_ptr<float>(), rk.data_ptr<float>(), M, T, static_cast<int>(n_q), static_cast<int>(n_kv),
+      static_cast<int>(Dh), static_cast<int>(start), use_rope ? 1 : 0, static_cast<float>(eps));
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {q, k, v, rq, rk};
+}
+
+std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv,
+                                         const at::Tensor& qkv, const at::Tensor& rq, const at::Tensor& rk,
+                                         const at::Tensor& qs, const at::Tensor& ks, const at::Tensor& cos_t,
+                                         const at::Tensor& sin_t, int64_t n_q, int64_t n_kv, int64_t Dh,
+                                         int64_t start, bool use_rope) {
+  check_contig(dq, "dq");
+  check_contig(dk, "dk");
+  check_contig(dv, "dv");
+  MINT_CHECK(dq.scalar_type() == at::kBFloat16 && dk.scalar_type() == at::kBFloat16 &&
+                 dv.scalar_type() == at::kBFloat16, "qk_norm_rope_bwd expects bf16 grads");
+  const int B = static_cast<int>(qkv.size(0)), T = static_cast<int>(qkv.size(1));
+  const int M = B * T;
+  auto dqkv = at::empty_like(qkv);
+  auto dqs = at::zeros({Dh}, qkv.options().dtype(at::kFloat));
+  auto dks = at::zeros({Dh}, qkv.options().dtype(at::kFloat));
+  const long long items = static_cast<long long>(M) * (n_q + 2 * n_kv);
+  if (items == 0) return {dqkv, dqs, dks};
+  c10::cuda::CUDAGuard g(qkv.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const long long want = (items + kRowsPerBlock - 1) / kRowsPerBlock;
+  const long long cap = static_cast<long long>(num_sms(qkv.get_device())) * 8;
+  const int grid = static_cast<int>(want < cap ? want : cap);
+  qk_norm_rope_bwd_kernel<<<grid, 256, 3 * kRowsPerBlock * Dh * sizeof(float), st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dq.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dk.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
+      rq.data_ptr<float>(), rk.data_ptr<float>(), qs.data_ptr<float>(), ks.data_ptr<float>(),
+      cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()),
+      dqs.data_ptr<float>(), dks.data_ptr<float>(), M, T, static_cast<int>(n_q), static_cast<int>(n_kv),
+      static_cast<int>(Dh), static_cast<int>(start), use_rope ? 1 : 0);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {dqkv, dqs, dks};
+}
+
+}  // namespace mint

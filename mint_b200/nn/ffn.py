@@ -1,0 +1,40 @@
+"""GeGLU feed-forward ``fc3(gelu_tanh(fc1 x) * fc2 x)`` (mint/nn/ffn.py:5-15).
+
+fc1 and fc2 run as one GEMM over ``[W1; W2]`` followed by the fused GeGLU kernel.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from mint_b200.nn.base import compute_dtype
+from mint_b200.ops.glu import geglu
+from mint_b200.ops.linear import linear
+from mint_b200.parallel import tp as tpc
+
+
+class GLU(nn.Module):
+    def __init__(self, embed_dim: int, hidden_dim: int, dtype: torch.dtype) -> None:
+        super().__init__()
+        self.fc1 = nn.Linear(embed_dim, hidden_dim, dtype=dtype, bias=False)
+        self.fc2 = nn.Linear(embed_dim, hidden_dim, dtype=dtype, bias=False)
+        self.fc3 = nn.Linear(hidden_dim, embed_dim, dtype=dtype, bias=False)
+        self.tp: tpc.TPInfo | None = None
+
+    def _fusable(self) -> bool:
+        return all(type(m) is nn.Linear for m in (self.fc1, self.fc2, self.fc3))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dt = compute_dtype(x)
+        x = tpc.enter_column_parallel(x, self.tp)
+        if self._fusable():
+            ab = linear(x, self.fc1.weight, self.fc2.weight, compute_dtype=dt)
+            h = geglu(ab)
+            out = linear(h, self.fc3.weight, compute_dtype=dt)
+        else:
+            a = self.fc1(x)
+            b = self.fc2(x)
+            h = geglu(torch.cat([a, b], dim=-1))
+            out = self.fc3(h)
+        return tpc.exit_row_parallel(out, self.tp)

@@ -1,0 +1,130 @@
+"""Scaled-dot-product attention with causal / sliding-window / document masking and GQA.
+
+Mask semantics follow the reference SDPA fallback (mint/nn/flashattn.py:218-279): a query at
+row ``i`` (aligned bottom-right when ``Tq < Tk``, i.e. with a KV cache) sees key ``j`` iff
+``j <= i`` (causal), ``i - j <= window_left`` (when ``window_left >= 0``), ``doc[i] == doc[j]``
+(when ``doc_ids`` is given) and ``attn_mask[.., i, j]`` (when given). GQA shares each KV head
+among ``Hq / Hkv`` query heads. CUDA tensors run the tcgen05 FlashAttention kernels in
+``mint_b200/csrc/attention_sm100.cu`` (causal + window + doc-id masking, GQA head packing);
+arbitrary boolean masks and ALiBi biases use the reference path.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F  # noqa: N812
+
+from mint_b200.ops import _ext
+
+
+def build_mask(
+    q_len: int,
+    k_len: int,
+    device: torch.device,
+    *,
+    causal: bool,
+    window_left: int,
+    doc_ids: torch.Tensor | None,
+    attn_mask: torch.Tensor | None,
+) -> torch.Tensor | None:
+    mask = None
+    if doc_ids is not None:
+        mask = doc_ids[:, None, :, None] == doc_ids[:, None, None, :]
+    if attn_mask is not None:
+        mask = attn_mask if mask is None else (mask & attn_mask)
+    if causal:
+        row = (k_len - q_len) + torch.arange(q_len, device=device)[:, None]
+        col = torch.arange(k_len, device=device)[None, :]
+        cm = col <= row
+        if 0 <= window_left < k_len:
+            cm = cm & ((row - col) <= window_left)
+        mask = cm if mask is None else (mask & cm)
+    return mask
+
+
+def attention_reference(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    causal: bool = True,
+    window_left: int = -1,
+    doc_ids: torch.Tensor | None = None,
+    attn_mask: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Math-mode attention in the input dtype via SDPA; q/k/v are ``[B, T, H, D]``."""
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    if qt.shape[1] != kt.shape[1]:
+        rep = qt.shape[1] // kt.shape[1]
+        kt = kt.repeat_interleave(rep, dim=1)
+        vt = vt.repeat_interleave(rep, dim=1)
+    mask = build_mask(qt.shape[2], kt.shape[2], q.device, causal=causal, window_left=window_left,
+                      doc_ids=doc_ids, attn_mask=attn_mask)
+    if bias is not None:
+        fmask = bias.to(qt.dtype)
+        if mask is not None:
+            fmask = fmask.masked_fill(~mask, float("-inf"))
+        mask = fmask
+    out = F.scaled_dot_product_attention(qt, kt, vt, attn_mask=mask, scale=scale)
+    return out.transpose(1, 2)
+
+
+class _FlashAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, window_left, doc_ids, scale):  # noqa: ANN001, ANN205
+        C = _ext.require()
+        o, lse = C.flash_attn_fwd(q, k, v, doc_ids, bool(causal), int(window_left), float(scale))
+        ctx.save_for_backward(q, k, v, o, lse, doc_ids)
+        ctx.meta = (bool(causal), int(window_left), float(scale))
+        return o
+
+    @staticmethod
+    def backward(ctx, do):  # noqa: ANN001, ANN205
+        C = _ext.require()
+        q, k, v, o, lse, doc_ids = ctx.saved_tensors
+        causal, window_left, scale = ctx.meta
+        dq, dk, dv = C.flash_attn_bwd(do.contiguous(), q, k, v, o, lse, doc_ids, causal, window_left, scale)
+        return dq, dk, dv, None, None, None, None
+
+
+def _kernel_supported(q: torch.Tensor, k: torch.Tensor) -> bool:
+    return (
+        q.dtype in (torch.bfloat16,)
+        and q.shape[-1] == 128
+        and k.shape[-1] == 128
+        and q.shape[2] % k.shape[2] == 0
+        and q.shape[1] == k.shape[1]
+        and hasattr(_ext.require(), "flash_attn_fwd")
+    )
+
+
+def attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    causal: bool = True,
+    window_left: int = -1,
+    doc_ids: torch.Tensor | None = None,
+    attn_mask: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Attention over ``[B, T, H, D]`` tensors; returns ``[B, Tq, Hq, D]``."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if (
+        _ext.use_cuda_kernels(q)
+        and attn_mask is None
+        and bias is None
+        and _kernel_supported(q, k)
+    ):
+        d = None if doc_ids is None else doc_ids.to(torch.int32).contiguous()
+        return _FlashAttnFn.apply(q.contiguous(), k.contiguous(), v.contiguous(), causal, window_left, d, scale)
+    return attention_reference(
+        q, k, v, causal=causal, window_left=window_left, doc_ids=doc_ids, attn_mask=attn_mask,
+        bias=bias, scale=scale,
+    )

@@ -1,0 +1,77 @@
+"""Bias-free linear layer ``y = x @ cat(weights)^T`` with fused multi-weight projections.
+
+The reference computes q/k/v (mint/nn/attn.py:49-53) and fc1/fc2 (mint/nn/ffn.py:13-14) as
+separate ``nn.Linear`` calls. Here several weights that read the same input run as ONE GEMM
+over their concatenation, and the weight gradient of each comes back as a slice of one fp32
+GEMM output. Master weights stay in their own dtype (fp32); the GEMMs run in ``compute_dtype``
+(bf16 under mixed precision) with fp32 accumulation; weight grads are produced in fp32 directly.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F  # noqa: N812
+
+from mint_b200.ops import _ext
+from mint_b200.ops.gemm import matmul
+
+
+def _cast_weight(weights: tuple[torch.Tensor, ...], dtype: torch.dtype) -> torch.Tensor:
+    if len(weights) == 1:
+        w = weights[0]
+        return w if w.dtype == dtype and w.is_contiguous() else w.to(dtype).contiguous()
+    return torch.cat([w.to(dtype) for w in weights], dim=0)
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dtype, *weights):  # noqa: ANN001, ANN205
+        k = x.shape[-1]
+        x2 = x.reshape(-1, k)
+        if x2.dtype != dtype or not x2.is_contiguous():
+            x2 = x2.to(dtype).contiguous()
+        w = _cast_weight(weights, dtype)
+        y = matmul(x2, w, trans_b=True, out_dtype=dtype)
+        # weights are kept as objects (not saved tensors) so ZeRO-3 can re-materialize them
+        ctx.weights = weights
+        ctx.x_shape = x.shape
+        ctx.x_dtype = x.dtype
+        ctx.dtype = dtype
+        ctx.save_for_backward(x2)
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        (x2,) = ctx.saved_tensors
+        weights = ctx.weights
+        n = dy.shape[-1]
+        dy2 = dy.reshape(-1, n)
+        if dy2.dtype != ctx.dtype or not dy2.is_contiguous():
+            dy2 = dy2.to(ctx.dtype).contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            w = _cast_weight(weights, ctx.dtype)
+            dx = matmul(dy2, w, out_dtype=ctx.dtype).view(ctx.x_shape)
+            if dx.dtype != ctx.x_dtype:
+                dx = dx.to(ctx.x_dtype)
+        grads: list[torch.Tensor | None] = [None] * len(weights)
+        want = [ctx.needs_input_grad[2 + i] for i in range(len(weights))]
+        if any(want):
+            gdtype = weights[0].dtype if weights[0].dtype in (torch.float32, torch.bfloat16) else torch.float32
+            dw = matmul(dy2, x2, trans_a=True, out_dtype=gdtype)
+            off = 0
+            for i, w in enumerate(weights):
+                rows = w.shape[0]
+                if want[i]:
+                    grads[i] = dw[off : off + rows]
+                off += rows
+        return (dx, None, *grads)
+
+
+def linear(x: torch.Tensor, *weights: torch.Tensor, compute_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``x @ cat(weights, 0)^T`` in ``compute_dtype`` (default: x's dtype)."""
+    dtype = compute_dtype or x.dtype
+    if _ext.use_cuda_kernels(x):
+        return _LinearFn.apply(x, dtype, *weights)
+    w = weights[0] if len(weights) == 1 else torch.cat(list(weights), dim=0)
+    return F.linear(x.to(dtype), w.to(dtype))

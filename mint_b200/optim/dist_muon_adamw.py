@@ -1,0 +1,267 @@
+"""DistMuonAdamW: AdamW / NorMuon over the gradient engine's shards (mint/optim/dist/muon_adamw.py).
+
+With a :class:`~mint_b200.parallel.zero.GradEngine` attached to the parameters:
+
+* AdamW groups update this rank's shard of every bucket with one fused kernel per bucket
+  (element-granular shards, same as the reference's flat slices);
+* NorMuon groups update whole matrices on their owner rank (owner buckets), so Polar-Express
+  runs on complete matrices. The reference flattens shards to 1-D and thereby degenerates
+  Muon to a plain normalization (mint/optim/dist/muon_adamw.py:250-254, 129-130);
+* after the step the engine all-gathers updated shards (ZeRO-1/2) or keeps them (ZeRO-3).
+
+``state_dict()`` is per parameter with full tensors (``step, exp_avg, exp_avg_sq`` or
+``momentum_buffer, second_momentum_buffer``) independent of the dp layout; on a ZeRO run it is
+a collective (every rank must call it) and ``load_state_dict`` re-shards for the current layout.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+from typing import Any
+
+import torch
+import torch.distributed as dist
+from torch.optim import Optimizer
+
+from mint_b200.optim.functional import POLAR_EXPRESS_COEFFS, adamw_update, normuon_update
+from mint_b200.optim.muon_adamw import AdamConfig, MuonAdamWConfig, MuonConfig
+
+
+class DistMuonAdamWConfig(MuonAdamWConfig):
+    pass
+
+
+class DistMuonAdamW(Optimizer):
+    def __init__(self, param_groups: list[dict], group: dist.ProcessGroup | None = None) -> None:
+        super().__init__(param_groups, defaults={})
+        self.process_group = group
+        self._engine = None
+        for g in self.param_groups:
+            for p in g["params"]:
+                eng = getattr(p, "_grad_engine", None)
+                if eng is not None:
+                    self._engine = eng
+                    break
+        # per-unit state, keyed by (param id, piece offset)
+        self._shard_state: dict[int, dict[str, Any]] = {}
+
+    @property
+    def engine(self):  # noqa: ANN201
+        return self._engine
+
+    def zero_grad(self, set_to_none: bool = True) -> None:  # noqa: ARG002
+        if self._engine is not None:
+            self._engine.zero_grad()
+            # params outside the engine (frozen or foreign) follow torch semantics
+            for g in self.param_groups:
+                for p in g["params"]:
+                    if id(p) not in self._engine.by_param:
+                        p.grad = None
+            return
+        super().zero_grad(set_to_none=True)
+
+    # ------------------------------------------------------------------ units
+    def _adamw_units(self, group: dict) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor, dict]]:
+        eng = self._engine
+        units = []
+        for p in group["params"]:
+            if eng is None or id(p) not in eng.by_param:
+                if p.grad is None:
+                    continue
+                units.append((p, p.data, p.grad, self.state[p]))
+                continue
+            for pv, gv, off, n in eng.segments(p):
+                st = self.state[p]
+                key = f"shard@{off}"
+                if key not in st:
+                    st[key] = {"step": 0, "exp_avg": torch.zeros_like(pv), "exp_avg_sq": torch.zeros_like(pv),
+                               "offset": off, "numel": n}
+                units.append((p, pv, gv, st[key]))
+        return units
+
+    def _step_adamw(self, group: dict) -> None:
+        beta1, beta2 = group["betas"]
+        for _p, pv, gv, st in self._adamw_units(group):
+            if "step" not in st:
+                st["step"] = 0
+                st["exp_avg"] = torch.zeros_like(pv)
+                st["exp_avg_sq"] = torch.zeros_like(pv)
+            st["step"] += 1
+            adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
+                         group["eps"], group["weight_decay"])
+
+    def _step_muon(self, group: dict) -> None:
+        eng = self._engine
+        for p in group["params"]:
+            if p.ndim != 2:
+                raise ValueError("NorMuon groups must hold 2-D matrices")
+            if eng is not None and id(p) in eng.by_param:
+                if not eng.owns_whole(p):
+                    continue
+                (pv, gv, off, n), = eng.segments(p)
+                assert off == 0 and n == p.numel(), "owner buckets hold whole matrices"
+                _b, slot = eng.slot(p)
+                pm, gm = pv.view(slot.shape), gv.view(slot.shape)
+            else:
+                if p.grad is None:
+                    continue
+                pm, gm = p.data, p.grad
+            st = self.state[p]
+            if "momentum_buffer" not in st:
+                rows, cols = pm.shape
+                st["momentum_buffer"] = torch.zeros(pm.shape, dtype=torch.float32, device=pm.device)
+                st["second_momentum_buffer"] = torch.zeros(
+                    (rows, 1) if rows >= cols else (1, cols), dtype=torch.float32, device=pm.device)
+            normuon_update(
+                pm, gm.float(), st["momentum_buffer"], st["second_momentum_buffer"],
+                lr=group["lr"], momentum=group["momentum"],
+                beta2=group["beta2"] if group.get("beta2") is not None else 0.0,
+                wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5),
+            )
+
+    @torch.no_grad()
+    def step(self, closure: Callable[[], float] | None = None) -> float | None:  # type: ignore[override]
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        eng = self._engine
+        if eng is not None and not getattr(eng, "_synced", False):
+            eng.finish_grad_sync()
+            eng.sync_tp_partial_grads()
+        for group in self.param_groups:
+            kind = group.get("kind", "adamw")
+            if kind == "adamw":
+                self._step_adamw(group)
+            elif kind == "muon":
+                self._step_muon(group)
+            else:
+                raise ValueError(f"Unknown optimizer kind: {kind}")
+        if eng is not None:
+            eng.after_step()
+            eng._synced = False
+        return loss
+
+    # ------------------------------------------------------------------ (de)serialization
+    def _full_state_tensor(self, p: torch.Tensor, st: dict, name: str) -> torch.Tensor:
+        """Assemble the full-shaped state ``name`` of ``p`` from this rank's pieces (collective when sharded)."""
+        eng = self._engine
+        if eng is None or id(p) not in eng.by_param or eng.level == 0 or eng.dp == 1:
+            for key, sub in st.items():
+                if key.startswith("shard@"):
+                    return sub[name].view(p.shape if p.numel() else eng.slot(p)[1].shape)
+            return st[name]
+        b, slot = eng.slot(p)
+        buf = torch.zeros(b.size, dtype=torch.float32, device=b.shard_data.device)
+        lo = eng.rank * b.shard
+        for key, sub in st.items():
+            if key.startswith("shard@"):
+                off = sub["offset"]
+                a = slot.start + off
+                buf[a : a + sub["numel"]].copy_(sub[name])
+        if name in st and isinstance(st[name], torch.Tensor) and st[name].shape == slot.shape:
+            buf[slot.start : slot.start + slot.numel].copy_(st[name].reshape(-1))
+        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=eng.group)
+        del lo
+        return buf[slot.start : slot.start + slot.numel].view(slot.shape)
+
+    def state_dict(self) -> dict[str, Any]:  # type: ignore[override]
+        groups = []
+        state: dict[int, dict[str, Any]] = {}
+        idx = 0
+        eng = self._engine
+        for g in self.param_groups:
+            ids = []
+            for p in g["params"]:
+                st = self.state.get(p, {})
+                full: dict[str, Any] = {}
+                kind = g.get("kind", "adamw")
+                if kind == "adamw":
+                    steps = [sub["step"] for k, sub in st.items() if k.startswith("shard@")]
+                    if not steps and "step" in st:
+                        steps = [st["step"]]
+                    step = max(steps) if steps else 0
+                    if eng is not None and eng.dp > 1 and eng.level > 0:
+                        t = torch.tensor([step], dtype=torch.float64, device=eng.buckets[0].shard_data.device)
+                        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=eng.group)
+                        step = int(t.item())
+                    if step > 0:
+                        full["step"] = step
+                        full["exp_avg"] = self._full_state_tensor(p, st, "exp_avg").detach().cpu().clone()
+                        full["exp_avg_sq"] = self._full_state_tensor(p, st, "exp_avg_sq").detach().cpu().clone()
+                else:
+                    have = "momentum_buffer" in st
+                    shape = p.shape if eng is None or id(p) not in eng.by_param else eng.slot(p)[1].shape
+                    mb = st["momentum_buffer"] if have else torch.zeros(shape, dtype=torch.float32,
+                                                                          device=self._device_of(p))
+                    rows, cols = shape
+                    sshape = (rows, 1) if rows >= cols else (1, cols)
+                    smb = st["second_momentum_buffer"] if have else torch.zeros(sshape, dtype=torch.float32,
+                                                                                 device=mb.device)
+                    if eng is not None and id(p) in eng.by_param and eng.dp > 1 and eng.level > 0:
+                        mb, smb = mb.clone(), smb.clone()
+                        if not eng.owns_whole(p):
+                            mb.zero_()
+                            smb.zero_()
+                        flag = torch.tensor([1.0 if have else 0.0], device=mb.device)
+                        dist.all_reduce(mb, group=eng.group)
+                        dist.all_reduce(smb, group=eng.group)
+                        dist.all_reduce(flag, group=eng.group)
+                        have = flag.item() > 0
+                    if have:
+                        full["momentum_buffer"] = mb.detach().cpu().clone()
+                        full["second_momentum_buffer"] = smb.detach().cpu().clone()
+                if full:
+                    state[idx] = full
+                ids.append(idx)
+                idx += 1
+            gcopy = {k: v for k, v in g.items() if k != "params"}
+            gcopy["params"] = ids
+            groups.append(gcopy)
+        return {"state": state, "param_groups": groups}
+
+    def _device_of(self, p: torch.Tensor) -> torch.device:
+        eng = self._engine
+        if eng is not None and id(p) in eng.by_param:
+            return eng.slot(p)[0].shard_data.device
+        return p.device
+
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:  # type: ignore[override]
+        saved_groups = state_dict["param_groups"]
+        if len(saved_groups) != len(self.param_groups):
+            raise ValueError("optimizer state has a different number of param groups")
+        eng = self._engine
+        self.state.clear()
+        for g, sg in zip(self.param_groups, saved_groups, strict=True):
+            for k, v in sg.items():
+                if k != "params":
+                    g[k] = v
+            for p, pid in zip(g["params"], sg["params"], strict=True):
+                st_saved = state_dict["state"].get(pid, state_dict["state"].get(str(pid)))
+                if not st_saved:
+                    continue
+                if g.get("kind", "adamw") == "adamw":
+                    if eng is None or id(p) not in eng.by_param:
+                        dev = p.device
+                        self.state[p] = {"step": int(st_saved["step"]),
+                                         "exp_avg": st_saved["exp_avg"].to(dev, torch.float32).view_as(p).clone(),
+                                         "exp_avg_sq": st_saved["exp_avg_sq"].to(dev, torch.float32).view_as(p).clone()}
+                        continue
+                    st = {}
+                    for pv, _gv, off, n in eng.segments(p):
+                        ea = st_saved["exp_avg"].reshape(-1)[off : off + n].to(pv.device, pv.dtype).clone()
+                        es = st_saved["exp_avg_sq"].reshape(-1)[off : off + n].to(pv.device, pv.dtype).clone()
+                        st[f"shard@{off}"] = {"step": int(st_saved["step"]), "exp_avg": ea, "exp_avg_sq": es,
+                                              "offset": off, "numel": n}
+                    self.state[p] = st
+                else:
+                    if eng is not None and id(p) in eng.by_param and not eng.owns_whole(p):
+                        continue
+                    dev = self._device_of(p)
+                    self.state[p] = {
+                        "momentum_buffer": st_saved["momentum_buffer"].to(dev, torch.float32).clone(),
+                        "second_momentum_buffer": st_saved["second_momentum_buffer"].to(dev, torch.float32).clone(),
+                    }
+
+
+__all__ = ["POLAR_EXPRESS_COEFFS", "AdamConfig", "DistMuonAdamW", "DistMuonAdamWConfig", "MuonConfig"]

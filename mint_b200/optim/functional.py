@@ -1,0 +1,116 @@
+"""Optimizer math shared by ``MuonAdamW`` and ``DistMuonAdamW``.
+
+AdamW (mint/optim/muon_adamw.py:69-92): decoupled weight decay, lerp moments, bias-corrected
+step. NorMuon (muon_adamw.py:187-252): Nesterov momentum, Frobenius normalization,
+Polar-Express orthogonalization (5 quintic iterations with the published coefficients of
+Amsel et al., "The Polar Express", 2025), NorMuon row/column second-moment rescaling back to the
+pre-normalization norm, cautious weight decay, LR x sqrt(max(1, rows/cols)).
+
+On CUDA: AdamW is one fused kernel per bucket shard; the Polar-Express chain runs on the
+tcgen05 GEMM with the ``b*A + c*A@A`` and ``a*X + B@X`` combinations folded into the GEMM
+epilogue (``alpha``/``beta`` with a ``D`` operand), bf16 operands and fp32 accumulation.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from mint_b200.ops import _ext
+from mint_b200.ops.gemm import matmul
+
+POLAR_EXPRESS_COEFFS = [
+    (8.156554524902461, -22.48329292557795, 15.878769915207462),
+    (4.042929935166739, -2.808917465908714, 0.5000178451051316),
+    (3.8916678022926607, -2.772484153217685, 0.5060648178503393),
+    (3.285753657755655, -2.3681294933425376, 0.46449024233003106),
+    (2.3465413258596377, -1.7097828382687081, 0.42323551169305323),
+]
+
+
+@torch.no_grad()
+def adamw_update(
+    p: torch.Tensor,
+    g: torch.Tensor,
+    exp_avg: torch.Tensor,
+    exp_avg_sq: torch.Tensor,
+    step: int,
+    lr: float,
+    beta1: float,
+    beta2: float,
+    eps: float,
+    wd: float,
+) -> None:
+    if p.is_cuda and _ext.kernels_enabled():
+        _ext.require().adamw_step(p, g, exp_avg, exp_avg_sq, float(lr), float(beta1), float(beta2),
+                                  float(eps), float(wd), int(step))
+        return
+    p.mul_(1 - lr * wd)
+    exp_avg.lerp_(g, 1 - beta1)
+    exp_avg_sq.lerp_(g.square(), 1 - beta2)
+    bias1 = 1 - beta1**step
+    bias2 = 1 - beta2**step
+    denom = (exp_avg_sq / bias2).sqrt() + eps
+    p.add_(exp_avg / denom, alpha=-(lr / bias1))
+
+
+@torch.no_grad()
+def polar_express(g: torch.Tensor, ns_steps: int) -> torch.Tensor:
+    """Orthogonalize a 2-D matrix: ``X <- X / (1.01 ||X||_F + 1e-6)`` then ``ns_steps`` quintic steps."""
+    tall = g.shape[0] > g.shape[1]
+    if g.is_cuda and _ext.kernels_enabled():
+        x = g.float()
+        x = (x / (x.norm() * 1.01 + 1e-6)).to(torch.bfloat16)
+        for a, b, c in POLAR_EXPRESS_COEFFS[:ns_steps]:
+            if tall:
+                A = matmul(x, x, trans_a=True)  # X^T X
+                B = matmul(A, A, alpha=c, beta=b, d=A)
+                x = matmul(x, B, alpha=1.0, beta=a, d=x)  # a X + X B
+            else:
+                A = matmul(x, x, trans_b=True)  # X X^T
+                B = matmul(A, A, alpha=c, beta=b, d=A)
+                x = matmul(B, x, alpha=1.0, beta=a, d=x)  # a X + B X
+        return x.float()
+    x = g.float()
+    x = x / (x.norm() * 1.01 + 1e-6)
+    for a, b, c in POLAR_EXPRESS_COEFFS[:ns_steps]:
+        if tall:
+            A = x.mT @ x
+            B = b * A + c * (A @ A)
+            x = a * x + x @ B
+        else:
+            A = x @ x.mT
+            B = b * A + c * (A @ A)
+            x = a * x + B @ x
+    return x
+
+
+@torch.no_grad()
+def normuon_update(
+    p: torch.Tensor,
+    grad: torch.Tensor,
+    momentum_buffer: torch.Tensor,
+    second_momentum_buffer: torch.Tensor,
+    *,
+    lr: float,
+    momentum: float,
+    beta2: float,
+    wd: float,
+    ns_steps: int,
+) -> None:
+    """One NorMuon step on a whole 2-D matrix ``p`` (views of ZeRO shards are fine)."""
+    rows, cols = p.shape
+    red_dim = -1 if rows >= cols else -2
+    lr = lr * max(1.0, rows / cols) ** 0.5
+    momentum_buffer.lerp_(grad, 1 - momentum)
+    g = grad.lerp(momentum_buffer, momentum)
+    g = polar_express(g, ns_steps)
+    v_mean = g.square().mean(dim=red_dim, keepdim=True)
+    red = g.size(red_dim)
+    v_norm = (v_mean.sum() * red).sqrt()
+    second_momentum_buffer.lerp_(v_mean, 1 - beta2)
+    step_scale = second_momentum_buffer.clamp_min(1e-10).rsqrt()
+    v_norm_new = ((v_mean * red) * step_scale.square()).sum().sqrt()
+    g = g * (step_scale * (v_norm / v_norm_new.clamp_min(1e-10)))
+    pf = p.float()
+    mask = (g * pf) >= 0
+    p.sub_((lr * g + lr * wd * pf * mask).to(p.dtype))

@@ -1,0 +1,522 @@
+"""Bucketed data-parallel gradient engine: DDP and ZeRO-1/2/3 (reference: mint/utils/parallel.py:92-522).
+
+The reference keeps one ``_ZeROParam`` per tensor and issues one synchronous NCCL call per
+parameter from its grad hook. Here parameters are packed into flat fp32 **buckets** (one per
+(module group, kind) — e.g. the matrices of block 7 — capped in size) so that:
+
+* every rank's gradient communication is a handful of large async collectives issued as soon as
+  a bucket's last gradient lands, overlapping the rest of backward;
+* grads are views into the bucket buffer (no per-step allocation; one fused optimizer launch
+  sweeps a whole shard);
+* ``ddp_level`` 0/1 all-reduce the bucket, 2/3 reduce-scatter it; 1/2 all-gather updated
+  parameter shards after the step; 3 keeps only the shard resident and all-gathers each block's
+  buckets right before the block runs (forward and backward, with one-block-ahead prefetch).
+
+Bucket kinds: ``flat`` (element-granular shards, AdamW-style elementwise updates) and ``owner``
+(2-D block matrices assigned whole to one rank each, padded per rank) so NorMuon can
+orthogonalize complete matrices on their owner rank.
+"""
+
+from __future__ import annotations
+
+import math
+from collections import defaultdict
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from mint_b200.parallel.context import ParallelContext
+
+_ALIGN = 64  # elements: keeps every shard / param offset 256-byte aligned for fp32
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def param_kind(name: str, p: torch.Tensor) -> str:
+    """Optimizer grouping of the reference's configure_optimizer (mint/models/gemma.py:195-206)."""
+    if "tok_embeddings" in name:
+        return "embedding"
+    if "output" in name:
+        return "lm_head"
+    if p.ndim == 2:
+        return "matrix"
+    return "scalar"
+
+
+def _module_group(name: str) -> str:
+    parts = name.split(".")
+    if len(parts) >= 2 and parts[0] == "blocks" and parts[1].isdigit():
+        return f"blocks.{parts[1]}"
+    return "top"
+
+
+@dataclass
+class Slot:
+    param: nn.Parameter
+    name: str
+    start: int  # offset in the bucket's padded flat space
+    numel: int
+    shape: torch.Size
+    owner: int  # owning dp rank for owner buckets, -1 for flat buckets
+
+
+@dataclass
+class Bucket:
+    index: int
+    group: str
+    kind: str  # "flat" | "owner"
+    pkind: str  # optimizer param kind (matrix / scalar / embedding / lm_head)
+    dtype: torch.dtype
+    slots: list[Slot]
+    size: int
+    shard: int
+    data: torch.Tensor | None = None  # full params [size] (levels 0-2; transient at level 3)
+    shard_data: torch.Tensor | None = None  # this rank's param shard [shard]
+    grad: torch.Tensor | None = None  # full grads [size] (persistent 0-2, transient 3)
+    grad_shard: torch.Tensor | None = None  # reduced grad shard [shard] (levels 2/3)
+    ready: int = 0
+    handle: Any = None
+    gather_handle: Any = None
+    gathered: bool = True
+    pending_scale: bool = False
+    extra: dict = field(default_factory=dict)
+
+
+class _BackwardGather(torch.autograd.Function):
+    """Identity whose backward re-gathers a ZeRO-3 module group before that group's backward."""
+
+    @staticmethod
+    def forward(ctx, x, engine, group):  # noqa: ANN001, ANN205
+        ctx.engine, ctx.group = engine, group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        ctx.engine._pre_backward(ctx.group)
+        return g, None, None
+
+
+class GradEngine:
+    def __init__(self, model: nn.Module, parallel: ParallelContext, bucket_cap_mb: float = 256.0) -> None:
+        self.model = model
+        self.parallel = parallel
+        self.level = parallel.ddp_level
+        self.dp = parallel.dp_size
+        self.rank = parallel.dp_rank
+        self.group = parallel.dp_group
+        self.tp_group = parallel.tp_group
+        self.distributed = self.dp > 1 and dist.is_available() and dist.is_initialized()
+        self.sync_grads = True
+        self._in_backward: set[str] = set()
+        self.buckets: list[Bucket] = []
+        self.by_param: dict[int, tuple[Bucket, Slot]] = {}
+        self.groups: dict[str, list[Bucket]] = defaultdict(list)
+        self.group_order: list[str] = []
+        self._build(bucket_cap_mb)
+        self._install_hooks()
+
+    # ------------------------------------------------------------------ layout
+    def _build(self, cap_mb: float) -> None:
+        seen: set[int] = set()
+        entries: dict[tuple[str, str, str, torch.dtype], list[tuple[str, nn.Parameter]]] = defaultdict(list)
+        order: list[tuple[str, str, str, torch.dtype]] = []
+        for name, p in self.model.named_parameters():
+            if id(p) in seen or not p.requires_grad:
+                continue
+            seen.add(id(p))
+            pk = param_kind(name, p)
+            kind = "owner" if (pk == "matrix" and self.dp > 1) else "flat"
+            key = (_module_group(name), kind, pk, p.dtype)
+            if key not in entries:
+                order.append(key)
+            entries[key].append((name, p))
+        cap = max(1, int(cap_mb * 1024 * 1024 / 4))
+        for key in order:
+            grp, kind, pk, dtype = key
+            chunk: list[tuple[str, nn.Parameter]] = []
+            acc = 0
+            for name, p in entries[key]:
+                if chunk and acc + p.numel() > cap:
+                    self._add_bucket(grp, kind, pk, dtype, chunk)
+                    chunk, acc = [], 0
+                chunk.append((name, p))
+                acc += p.numel()
+            if chunk:
+                self._add_bucket(grp, kind, pk, dtype, chunk)
+        for b in self.buckets:
+            if b.group not in self.groups:
+                self.group_order.append(b.group)
+            self.groups[b.group].append(b)
+
+    def _add_bucket(self, grp: str, kind: str, pk: str, dtype: torch.dtype, items: list[tuple[str, nn.Parameter]]) -> None:
+        dp = self.dp
+        slots: list[Slot] = []
+        if kind == "owner":
+            # greedy largest-first assignment of whole matrices to ranks
+            loads = [0] * dp
+            assign: list[list[tuple[str, nn.Parameter]]] = [[] for _ in range(dp)]
+            for name, p in sorted(items, key=lambda it: -it[1].numel()):
+                r = min(range(dp), key=lambda i: loads[i])
+                assign[r].append((name, p))
+                loads[r] += _round_up(p.numel(), _ALIGN)
+            shard = _round_up(max(max(loads), 1), _ALIGN)
+            for r in range(dp):
+                off = r * shard
+                for name, p in assign[r]:
+                    slots.append(Slot(p, name, off, p.numel(), p.shape, r))
+                    off += _round_up(p.numel(), _ALIGN)
+            size = shard * dp
+        else:
+            off = 0
+            for name, p in items:
+                slots.append(Slot(p, name, off, p.numel(), p.shape, -1))
+                off += _round_up(p.numel(), _ALIGN)
+            size = _round_up(max(off, 1), _ALIGN * dp)
+            shard = size // dp
+        b = Bucket(len(self.buckets), grp, kind, pk, dtype, slots, size, shard)
+        dev = items[0][1].device
+        data = torch.zeros(size, dtype=dtype, device=dev)
+        for s in slots:
+            data[s.start : s.start + s.numel].copy_(s.param.detach().reshape(-1))
+            self.by_param[id(s.param)] = (b, s)
+        lo = self.rank * shard
+        if self.level == 3 and self.dp > 1:
+            b.shard_data = data[lo : lo + shard].clone()
+            b.data = None
+            b.gathered = False
+            for s in slots:
+                s.param.data = torch.empty(0, dtype=dtype, device=dev)
+        else:
+            b.data = data
+            b.shard_data = data[lo : lo + shard]
+            for s in slots:
+                s.param.data = data[s.start : s.start + s.numel].view(s.shape)
+            b.grad = torch.zeros(size, dtype=dtype, device=dev)
+        if self.level >= 2 and self.dp > 1:
+            b.grad_shard = torch.zeros(shard, dtype=dtype, device=dev)
+        self.buckets.append(b)
+        for s in slots:
+            s.param._grad_engine = self  # lets the optimizer find the engine
+
+    # ------------------------------------------------------------------ grads
+    def _install_grad_views(self, b: Bucket) -> None:
+        if b.grad is None:
+            return
+        for s in b.slots:
+            s.param.grad = b.grad[s.start : s.start + s.numel].view(s.shape)
+
+    def zero_grad(self) -> None:
+        for b in self.buckets:
+            if b.grad is not None:
+                b.grad.zero_()
+                self._install_grad_views(b)
+            if b.grad_shard is not None:
+                b.grad_shard.zero_()
+            b.ready = 0
+            b.handle = None
+            b.pending_scale = False
+
+    def _install_hooks(self) -> None:
+        for b in self.buckets:
+            for s in b.slots:
+                s.param.register_post_accumulate_grad_hook(self._make_hook(b))
+        self.zero_grad()
+        if self.level == 3 and self.dp > 1:
+            self._install_zero3_hooks()
+
+    def _make_hook(self, b: Bucket):  # noqa: ANN202
+        def hook(_p: torch.Tensor) -> None:
+            b.ready += 1
+            if b.ready == len(b.slots):
+                self._launch(b)
+        return hook
+
+    def _launch(self, b: Bucket) -> None:
+        b.ready = 0
+        if b.grad is None:
+            return
+        if not self.distributed:
+            if self.level == 3 and self.dp > 1:
+                pass
+            return
+        if self.level in (0, 1):
+            if not self.sync_grads:
+                return
+            b.handle = dist.all_reduce(b.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        else:
+            if not self.sync_grads and self.level == 2:
+                return
+            out = torch.empty_like(b.grad_shard)
+            h = dist.reduce_scatter_tensor(out, b.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+            b.handle = (h, out)
+        b.pending_scale = True
+        if self.level == 3:
+            self._finish_bucket(b)  # level 3 must release the full grad buffer promptly
+
+    def _finish_bucket(self, b: Bucket) -> None:
+        if b.handle is None:
+            return
+        if isinstance(b.handle, tuple):
+            h, out = b.handle
+            h.wait()
+            b.grad_shard.add_(out)
+        else:
+            b.handle.wait()
+        b.handle = None
+        if self.level == 3:
+            self._release_grads(b)
+
+    def finish_grad_sync(self) -> None:
+        """Wait for all bucket collectives (launching any bucket a hook never completed) and scale by 1/dp."""
+        if not self.distributed:
+            return
+        for b in self.buckets:
+            if b.handle is None and b.grad is not None and (self.sync_grads or self.level == 3):
+                if b.ready or self.level != 3:
+                    self._launch(b)
+            self._finish_bucket(b)
+        inv = 1.0 / self.dp
+        for b in self.buckets:
+            if self.level in (0, 1):
+                if b.grad is not None:
+                    b.grad.mul_(inv)
+            elif b.grad_shard is not None:
+                b.grad_shard.mul_(inv)
+            b.pending_scale = False
+
+    def sync_tp_partial_grads(self) -> None:
+        """Sum grads of TP-replicated params whose contributions are partial (QK-norm, SP norms)."""
+        tp_group = self.tp_group
+        if tp_group is None or dist.get_world_size(tp_group) == 1:
+            return
+        grads = [p.grad for p in self.model.parameters() if getattr(p, "_tp_partial_grad", False) and p.grad is not None]
+        if not grads:
+            return
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=tp_group)
+        off = 0
+        for g in grads:
+            g.copy_(flat[off : off + g.numel()].view_as(g))
+            off += g.numel()
+
+    # ------------------------------------------------------------------ optimizer views
+    def segments(self, p: torch.Tensor) -> list[tuple[torch.Tensor, torch.Tensor, int, int]]:
+        """This rank's ``(param_view, grad_view, elem_offset_in_param, numel)`` pieces of ``p``."""
+        b, s = self.by_param[id(p)]
+        if self.level == 0 or self.dp == 1:
+            return [(b.data[s.start : s.start + s.numel], b.grad[s.start : s.start + s.numel], 0, s.numel)]
+        lo, hi = self.rank * b.shard, (self.rank + 1) * b.shard
+        a, e = max(lo, s.start), min(hi, s.start + s.numel)
+        if a >= e:
+            return []
+        pv = b.shard_data[a - lo : e - lo]
+        if self.level == 1:
+            gv = b.grad[a:e]
+        else:
+            gv = b.grad_shard[a - lo : e - lo]
+        return [(pv, gv, a - s.start, e - a)]
+
+    def owns_whole(self, p: torch.Tensor) -> bool:
+        b, s = self.by_param[id(p)]
+        if self.level == 0 or self.dp == 1:
+            return True
+        return s.owner == self.rank
+
+    def slot(self, p: torch.Tensor) -> tuple[Bucket, Slot]:
+        return self.by_param[id(p)]
+
+    def after_step(self) -> None:
+        """Propagate updated shards: all-gather params (levels 1/2); level 3 drops stale full copies."""
+        if not self.distributed or self.level == 0:
+            return
+        if self.level == 3:
+            for grp in self.group_order:
+                self.free_group(grp)
+            self._in_backward.clear()
+            return
+        handles = []
+        for b in self.buckets:
+            src = b.shard_data.clone()
+            handles.append(dist.all_gather_into_tensor(b.data, src, group=self.group, async_op=True))
+        for h in handles:
+            h.wait()
+
+    # ------------------------------------------------------------------ grad norm
+    def grad_norm_sq(self) -> torch.Tensor:
+        """Squared global grad norm over dp x tp, each element counted once."""
+        dev = self.buckets[0].grad.device if self.buckets and self.buckets[0].grad is not None else (
+            self.buckets[0].shard_data.device if self.buckets else torch.device("cpu"))
+        total = torch.zeros((), dtype=torch.float32, device=dev)
+        tp = self.parallel.tp_size
+        for b in self.buckets:
+            for s in b.slots:
+                replicated_over_tp = tp > 1 and not getattr(s.param, "_tp_sharded", False)
+                if replicated_over_tp and self.parallel.tp_rank != 0:
+                    continue
+                for _pv, gv, _o, _n in self.segments(s.param):
+                    total += gv.float().pow(2).sum()
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            dist.all_reduce(total, op=dist.ReduceOp.SUM)
+        return total
+
+    def clip_grad_norm(self, max_norm: float) -> torch.Tensor:
+        norm = self.grad_norm_sq().sqrt()
+        coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
+        for b in self.buckets:
+            if self.level >= 2 and self.distributed:
+                b.grad_shard.mul_(coef)
+            elif b.grad is not None:
+                b.grad.mul_(coef)
+        return norm
+
+    # ------------------------------------------------------------------ ZeRO-3 gather / free
+    def _gather_bucket(self, b: Bucket, async_op: bool = False) -> None:
+        if b.gathered or b.gather_handle is not None:
+            return
+        full = torch.empty(b.size, dtype=b.dtype, device=b.shard_data.device)
+        h = dist.all_gather_into_tensor(full, b.shard_data, group=self.group, async_op=async_op)
+        b.extra["full"] = full
+        if async_op:
+            b.gather_handle = h
+        else:
+            self._bind_full(b)
+
+    def _bind_full(self, b: Bucket) -> None:
+        if b.gather_handle is not None:
+            b.gather_handle.wait()
+            b.gather_handle = None
+        full = b.extra.pop("full", None)
+        if full is None:
+            return
+        b.data = full
+        for s in b.slots:
+            s.param.data = full[s.start : s.start + s.numel].view(s.shape)
+        b.gathered = True
+
+    def _free_bucket(self, b: Bucket) -> None:
+        if not b.gathered:
+            return
+        for s in b.slots:
+            s.param.data = torch.empty(0, dtype=b.dtype, device=b.shard_data.device)
+        b.data = None
+        b.gathered = False
+
+    def gather_group(self, grp: str, async_op: bool = False) -> None:
+        for b in self.groups.get(grp, []):
+            self._gather_bucket(b, async_op=async_op)
+
+    def wait_group(self, grp: str) -> None:
+        for b in self.groups.get(grp, []):
+            if not b.gathered:
+                if b.gather_handle is None and "full" not in b.extra:
+                    self._gather_bucket(b)
+                self._bind_full(b)
+
+    def free_group(self, grp: str) -> None:
+        for b in self.groups.get(grp, []):
+            self._free_bucket(b)
+
+    def _alloc_grads(self, grp: str) -> None:
+        for b in self.groups.get(grp, []):
+            if b.grad is None:
+                b.grad = torch.zeros(b.size, dtype=b.dtype, device=b.shard_data.device)
+                self._install_grad_views(b)
+
+    def _release_grads(self, b: Bucket) -> None:
+        for s in b.slots:
+            s.param.grad = None
+        b.grad = None
+        if b.group != "top" and all(x.grad is None for x in self.groups[b.group]):
+            self._in_backward.discard(b.group)
+            for x in self.groups[b.group]:
+                self._free_bucket(x)
+
+    def _pre_backward(self, grp: str) -> None:
+        self._in_backward.add(grp)
+        self.wait_group(grp)
+        self._alloc_grads(grp)
+        i = self.group_order.index(grp)
+        if i - 1 >= 0 and self.group_order[i - 1] != "top":
+            self.gather_group(self.group_order[i - 1], async_op=True)
+
+    def _install_zero3_hooks(self) -> None:
+        model = self.model
+        blocks = getattr(model, "blocks", None)
+        order = [g for g in self.group_order if g != "top"]
+
+        def model_pre(_m, _args):  # noqa: ANN001, ANN202
+            self.wait_group("top")
+            if torch.is_grad_enabled():
+                self._alloc_grads("top")
+            if order:
+                self.gather_group(order[0], async_op=True)
+
+        model.register_forward_pre_hook(model_pre)
+        if blocks is None:
+            return
+        for i, blk in enumerate(blocks):
+            grp = f"blocks.{i}"
+            if grp not in self.groups:
+                continue
+            nxt = f"blocks.{i + 1}" if f"blocks.{i + 1}" in self.groups else None
+
+            def pre(_m, _args, grp=grp, nxt=nxt):  # noqa: ANN001, ANN202
+                self.wait_group(grp)
+                if nxt is not None:
+                    self.gather_group(nxt, async_op=True)
+
+            def post(_m, _args, out, grp=grp):  # noqa: ANN001, ANN202
+                if grp not in self._in_backward:  # a recompute inside backward keeps the params
+                    self.free_group(grp)
+                if torch.is_grad_enabled() and isinstance(out, torch.Tensor) and out.requires_grad:
+                    return _BackwardGather.apply(out, self, grp)
+                return out
+
+            blk.register_forward_pre_hook(pre)
+            blk.register_forward_hook(post)
+
+    # ------------------------------------------------------------------ state
+    def full_param(self, p: torch.Tensor) -> torch.Tensor:
+        """The full (dp-consolidated) value of ``p`` (collective at ZeRO-3)."""
+        b, s = self.by_param[id(p)]
+        if b.gathered and b.data is not None:
+            return b.data[s.start : s.start + s.numel].view(s.shape)
+        full = torch.empty(b.size, dtype=b.dtype, device=b.shard_data.device)
+        dist.all_gather_into_tensor(full, b.shard_data, group=self.group)
+        return full[s.start : s.start + s.numel].view(s.shape)
+
+    def load_full_param(self, p: torch.Tensor, value: torch.Tensor) -> None:
+        b, s = self.by_param[id(p)]
+        flat = value.reshape(-1).to(b.dtype)
+        lo = self.rank * b.shard
+        a, e = max(lo, s.start), min(lo + b.shard, s.start + s.numel)
+        if a < e:
+            b.shard_data[a - lo : e - lo].copy_(flat[a - s.start : e - s.start])
+        if b.data is not None:
+            b.data[s.start : s.start + s.numel].copy_(flat)
+
+
+def get_engine(model: nn.Module) -> GradEngine | None:
+    return getattr(model, "_grad_engine", None)
+
+
+def apply_ddp(model: nn.Module, parallel: ParallelContext, bucket_cap_mb: float = 256.0) -> nn.Module:
+    engine = GradEngine(model, parallel, bucket_cap_mb=bucket_cap_mb)
+    model._grad_engine = engine
+    return model
+
+
+def bucket_summary(engine: GradEngine) -> str:
+    lines = []
+    for b in engine.buckets:
+        lines.append(f"bucket {b.index}: {b.group}/{b.kind}/{b.pkind} params={len(b.slots)} size={b.size} "
+                     f"shard={b.shard} ({b.size * 4 / 2**20:.1f} MiB)")
+    return "\n".join(lines)
+
+
+__all__ = ["GradEngine", "apply_ddp", "bucket_summary", "get_engine", "param_kind", "math"]

@@ -1,0 +1,80 @@
+"""tcgen05 GEMM vs a PyTorch fp32 reference: every operand major-ness, bf16 / fp32 output, alpha/beta."""
+
+import pytest
+import torch
+
+from mint_b200.ops.gemm import matmul
+
+pytestmark = pytest.mark.gpu
+
+
+def ref(a, b, ta, tb, alpha=1.0, beta=0.0, d=None):
+    a_ = a.float().t() if ta else a.float()
+    b_ = b.float().t() if tb else b.float()
+    c = alpha * (a_ @ b_)
+    if d is not None:
+        c = c + beta * d.float()
+    return c
+
+
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+@pytest.mark.parametrize("shape", [(256, 512, 256), (384, 640, 192), (1000, 776, 328), (128, 128, 64), (300, 2304, 768)])
+def test_gemm_layouts(ta, tb, shape):
+    torch.manual_seed(0)
+    M, N, K = shape
+    a = torch.randn((K, M) if ta else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((N, K) if tb else (K, N), device="cuda", dtype=torch.bfloat16)
+    out = matmul(a, b, trans_a=ta, trans_b=tb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    exp = ref(a, b, ta, tb)
+    err = (out - exp).abs().max().item()
+    assert err < 1e-2 * max(1.0, exp.abs().max().item() / 50), f"max err {err}"
+
+
+@pytest.mark.parametrize("ta,tb", [(False, True), (False, False), (True, False)])
+def test_gemm_bf16_out_alpha_beta(ta, tb):
+    torch.manual_seed(1)
+    M, N, K = 512, 768, 1024
+    a = torch.randn((K, M) if ta else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((N, K) if tb else (K, N), device="cuda", dtype=torch.bfloat16)
+    d = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    out = matmul(a, b, trans_a=ta, trans_b=tb, alpha=0.5, beta=-1.5, d=d, out_dtype=torch.bfloat16)
+    exp = ref(a, b, ta, tb, 0.5, -1.5, d)
+    rel = ((out.float() - exp).norm() / exp.norm()).item()
+    assert rel < 1e-2, rel
+
+
+def test_gemm_fp32_accumulate_inplace():
+    torch.manual_seed(2)
+    M, N, K = 768, 512, 4096
+    a = torch.randn(K, M, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)
+    c = torch.randn(M, N, device="cuda", dtype=torch.float32)
+    c0 = c.clone()
+    matmul(a, b, trans_a=True, beta=1.0, d=c, out=c)
+    exp = a.float().t() @ b.float() + c0
+    rel = ((c - exp).norm() / exp.norm()).item()
+    assert rel < 2e-3, rel
+
+
+def test_gemm_large_lm_head_shape():
+    torch.manual_seed(3)
+    M, N, K = 4096, 65536, 768
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16) * 0.5
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.5
+    out = matmul(a, b, trans_b=True, out_dtype=torch.bfloat16)
+    exp = a.float() @ b.float().t()
+    rel = ((out.float() - exp).norm() / exp.norm()).item()
+    assert rel < 1e-2, rel
+    from mint_b200.ops import _ext
+    assert _ext.require().read_status(False) == 0
+
+
+def test_gemm_repeatable():
+    torch.manual_seed(4)
+    a = torch.randn(640, 512, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(384, 512, device="cuda", dtype=torch.bfloat16)
+    x = matmul(a, b, trans_b=True, out_dtype=torch.float32)
+    y = matmul(a, b, trans_b=True, out_dtype=torch.float32)
+    assert torch.equal(x, y)
