@@ -99,6 +99,8 @@ class Gemma(nn.Module):
         # set by mint_b200.parallel.apply_tp: vocab-parallel embedding / LM head
         self.tp: tpc.TPInfo | None = None
         self.vocab_start = 0
+        # set by the ZeRO-3 engine: materializes sharded top-level parameters before a pass
+        self._before_forward = None
         self.reset_parameters()
 
     def reset_parameters(self) -> None:
@@ -130,6 +132,8 @@ class Gemma(nn.Module):
         doc_ids: torch.Tensor | None,
         attn_mask: torch.Tensor | None,
     ) -> torch.Tensor:
+        if self._before_forward is not None:
+            self._before_forward()
         h = self._embed(input_ids)
         for i, block in enumerate(self.blocks):
             kv_cache = kv_caches[i] if kv_caches is not None else None
@@ -278,7 +282,7 @@ def configure_optimizer(
             groups["embedding"].append(param)
         elif "output" in name:
             groups["lm_head"].append(param)
-        elif param.ndim == 2:
+        elif len(getattr(param, "_orig_shape", param.shape)) == 2:
             groups["matrix"].append(param)
         else:
             groups["scalar"].append(param)

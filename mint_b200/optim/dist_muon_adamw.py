@@ -93,7 +93,7 @@ class DistMuonAdamW(Optimizer):
     def _step_muon(self, group: dict) -> None:
         eng = self._engine
         for p in group["params"]:
-            if p.ndim != 2:
+            if len(getattr(p, "_orig_shape", p.shape)) != 2:
                 raise ValueError("NorMuon groups must hold 2-D matrices")
             if eng is not None and id(p) in eng.by_param:
                 if not eng.owns_whole(p):
@@ -107,8 +107,9 @@ class DistMuonAdamW(Optimizer):
                     continue
                 pm, gm = p.data, p.grad
             st = self.state[p]
+            tp_group, tp_dim = self._tp_of(p)
             if "momentum_buffer" not in st:
-                rows, cols = pm.shape
+                rows, cols = self._full_shape(p, pm.shape)
                 st["momentum_buffer"] = torch.zeros(pm.shape, dtype=torch.float32, device=pm.device)
                 st["second_momentum_buffer"] = torch.zeros(
                     (rows, 1) if rows >= cols else (1, cols), dtype=torch.float32, device=pm.device)
@@ -116,8 +117,32 @@ class DistMuonAdamW(Optimizer):
                 pm, gm.float(), st["momentum_buffer"], st["second_momentum_buffer"],
                 lr=group["lr"], momentum=group["momentum"],
                 beta2=group["beta2"] if group.get("beta2") is not None else 0.0,
-                wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5),
+                wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5), tp_group=tp_group, tp_dim=tp_dim,
             )
+
+    def _tp_of(self, p: torch.Tensor):  # noqa: ANN202
+        """(TP group, split dim) for a tensor-parallel sharded parameter, else (None, 0)."""
+        eng = self._engine
+        if eng is None or not getattr(p, "_tp_sharded", False) or eng.parallel.tp_size <= 1:
+            return None, 0
+        return eng.tp_group, getattr(p, "_tp_dim", 0)
+
+    def _full_shape(self, p: torch.Tensor, local: torch.Size) -> tuple[int, int]:
+        group, dim = self._tp_of(p)
+        if group is None:
+            return tuple(local)
+        size = self._engine.parallel.tp_size
+        return (local[0] * size, local[1]) if dim == 0 else (local[0], local[1] * size)
+
+    def _tp_consolidate(self, p: torch.Tensor, t: torch.Tensor, name: str) -> torch.Tensor:
+        """Full-matrix view of a per-parameter state tensor under TP (collective over the TP group)."""
+        group, dim = self._tp_of(p)
+        if group is None or name == "second_momentum_buffer":
+            return t
+        size = self._engine.parallel.tp_size
+        parts = [torch.empty_like(t) for _ in range(size)]
+        dist.all_gather(parts, t.contiguous(), group=group)
+        return torch.cat(parts, dim=dim)
 
     @torch.no_grad()
     def step(self, closure: Callable[[], float] | None = None) -> float | None:  # type: ignore[override]
@@ -187,14 +212,15 @@ class DistMuonAdamW(Optimizer):
                         step = int(t.item())
                     if step > 0:
                         full["step"] = step
-                        full["exp_avg"] = self._full_state_tensor(p, st, "exp_avg").detach().cpu().clone()
-                        full["exp_avg_sq"] = self._full_state_tensor(p, st, "exp_avg_sq").detach().cpu().clone()
+                        for nm in ("exp_avg", "exp_avg_sq"):
+                            t = self._full_state_tensor(p, st, nm)
+                            full[nm] = self._tp_consolidate(p, t, nm).detach().cpu().clone()
                 else:
                     have = "momentum_buffer" in st
                     shape = p.shape if eng is None or id(p) not in eng.by_param else eng.slot(p)[1].shape
                     mb = st["momentum_buffer"] if have else torch.zeros(shape, dtype=torch.float32,
                                                                           device=self._device_of(p))
-                    rows, cols = shape
+                    rows, cols = self._full_shape(p, shape)
                     sshape = (rows, 1) if rows >= cols else (1, cols)
                     smb = st["second_momentum_buffer"] if have else torch.zeros(sshape, dtype=torch.float32,
                                                                                  device=mb.device)
@@ -209,7 +235,7 @@ class DistMuonAdamW(Optimizer):
                         dist.all_reduce(flag, group=eng.group)
                         have = flag.item() > 0
                     if have:
-                        full["momentum_buffer"] = mb.detach().cpu().clone()
+                        full["momentum_buffer"] = self._tp_consolidate(p, mb, "momentum_buffer").detach().cpu().clone()
                         full["second_momentum_buffer"] = smb.detach().cpu().clone()
                 if full:
                     state[idx] = full
@@ -219,6 +245,17 @@ class DistMuonAdamW(Optimizer):
             gcopy["params"] = ids
             groups.append(gcopy)
         return {"state": state, "param_groups": groups}
+
+    def _tp_local(self, p: torch.Tensor, st: dict) -> dict:
+        group, dim = self._tp_of(p)
+        if group is None:
+            return st
+        size, rank = self._engine.parallel.tp_size, self._engine.parallel.tp_rank
+        out = dict(st)
+        for nm in ("exp_avg", "exp_avg_sq", "momentum_buffer"):
+            if nm in st:
+                out[nm] = st[nm].chunk(size, dim=dim)[rank]
+        return out
 
     def _device_of(self, p: torch.Tensor) -> torch.device:
         eng = self._engine
@@ -240,6 +277,7 @@ class DistMuonAdamW(Optimizer):
                 st_saved = state_dict["state"].get(pid, state_dict["state"].get(str(pid)))
                 if not st_saved:
                     continue
+                st_saved = self._tp_local(p, st_saved)
                 if g.get("kind", "adamw") == "adamw":
                     if eng is None or id(p) not in eng.by_param:
                         dev = p.device

@@ -84,6 +84,15 @@ def polar_express(g: torch.Tensor, ns_steps: int) -> torch.Tensor:
     return x
 
 
+def _tp_gather(t: torch.Tensor, dim: int, group) -> torch.Tensor:  # noqa: ANN001
+    import torch.distributed as dist  # noqa: PLC0415
+
+    size = dist.get_world_size(group)
+    parts = [torch.empty_like(t) for _ in range(size)]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    return torch.cat(parts, dim=dim)
+
+
 @torch.no_grad()
 def normuon_update(
     p: torch.Tensor,
@@ -96,13 +105,24 @@ def normuon_update(
     beta2: float,
     wd: float,
     ns_steps: int,
+    tp_group=None,  # noqa: ANN001
+    tp_dim: int = 0,
 ) -> None:
-    """One NorMuon step on a whole 2-D matrix ``p`` (views of ZeRO shards are fine)."""
-    rows, cols = p.shape
-    red_dim = -1 if rows >= cols else -2
-    lr = lr * max(1.0, rows / cols) ** 0.5
+    """One NorMuon step on a 2-D matrix ``p`` (views of ZeRO shards are fine).
+
+    With ``tp_group``, ``p``/``grad``/``momentum_buffer`` are this rank's tensor-parallel shard of a
+    matrix split along ``tp_dim``: the Nesterov gradient is all-gathered so orthogonalization and the
+    NorMuon statistics see the whole matrix (``second_momentum_buffer`` has the full matrix's shape
+    and is replicated), and each rank applies its slice of the update.
+    """
     momentum_buffer.lerp_(grad, 1 - momentum)
     g = grad.lerp(momentum_buffer, momentum)
+    shard_rows, shard_cols = p.shape
+    if tp_group is not None:
+        g = _tp_gather(g, tp_dim, tp_group)
+    rows, cols = g.shape
+    red_dim = -1 if rows >= cols else -2
+    lr = lr * max(1.0, rows / cols) ** 0.5
     g = polar_express(g, ns_steps)
     v_mean = g.square().mean(dim=red_dim, keepdim=True)
     red = g.size(red_dim)
@@ -111,6 +131,11 @@ def normuon_update(
     step_scale = second_momentum_buffer.clamp_min(1e-10).rsqrt()
     v_norm_new = ((v_mean * red) * step_scale.square()).sum().sqrt()
     g = g * (step_scale * (v_norm / v_norm_new.clamp_min(1e-10)))
+    if tp_group is not None:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        r = dist.get_rank(tp_group)
+        g = g.narrow(tp_dim, r * (shard_rows if tp_dim == 0 else shard_cols), shard_rows if tp_dim == 0 else shard_cols)
     pf = p.float()
     mask = (g * pf) >= 0
     p.sub_((lr * g + lr * wd * pf * mask).to(p.dtype))

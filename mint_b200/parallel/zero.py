@@ -184,6 +184,7 @@ class GradEngine:
         for s in slots:
             data[s.start : s.start + s.numel].copy_(s.param.detach().reshape(-1))
             self.by_param[id(s.param)] = (b, s)
+            s.param._orig_shape = s.shape  # logical shape while ZeRO-3 keeps only a shard
         lo = self.rank * shard
         if self.level == 3 and self.dp > 1:
             b.shard_data = data[lo : lo + shard].clone()
@@ -290,17 +291,26 @@ class GradEngine:
             b.pending_scale = False
 
     def sync_tp_partial_grads(self) -> None:
-        """Sum grads of TP-replicated params whose contributions are partial (QK-norm, SP norms)."""
+        """Sum grads of TP-replicated params whose contributions are partial (QK-norm, SP norms).
+
+        Runs after the dp collectives on this rank's *reduced* gradient pieces (full grads at
+        ddp_level 0/1, reduce-scattered shards at 2/3); every rank of a TP group has the same bucket
+        layout for replicated parameters, so the pieces line up across the group.
+        """
         tp_group = self.tp_group
         if tp_group is None or dist.get_world_size(tp_group) == 1:
             return
-        grads = [p.grad for p in self.model.parameters() if getattr(p, "_tp_partial_grad", False) and p.grad is not None]
-        if not grads:
+        pieces = []
+        for b in self.buckets:
+            for s in b.slots:
+                if getattr(s.param, "_tp_partial_grad", False):
+                    pieces.extend(gv for _pv, gv, _o, _n in self.segments(s.param))
+        if not pieces:
             return
-        flat = torch.cat([g.reshape(-1) for g in grads])
+        flat = torch.cat([g.reshape(-1) for g in pieces])
         dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=tp_group)
         off = 0
-        for g in grads:
+        for g in pieces:
             g.copy_(flat[off : off + g.numel()].view_as(g))
             off += g.numel()
 
@@ -361,7 +371,12 @@ class GradEngine:
                 for _pv, gv, _o, _n in self.segments(s.param):
                     total += gv.float().pow(2).sum()
         if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
-            dist.all_reduce(total, op=dist.ReduceOp.SUM)
+            if self.level == 0 or self.dp == 1:
+                # dp replicas hold identical full gradients: reduce over the TP group only
+                if tp > 1:
+                    dist.all_reduce(total, op=dist.ReduceOp.SUM, group=self.tp_group)
+            else:
+                dist.all_reduce(total, op=dist.ReduceOp.SUM)
         return total
 
     def clip_grad_norm(self, max_norm: float) -> torch.Tensor:
@@ -456,7 +471,11 @@ class GradEngine:
             if order:
                 self.gather_group(order[0], async_op=True)
 
-        model.register_forward_pre_hook(model_pre)
+        if hasattr(model, "_before_forward"):
+            # models with entry points other than forward() (Gemma.loss) call this themselves
+            model._before_forward = lambda: model_pre(model, ())
+        else:
+            model.register_forward_pre_hook(model_pre)
         if blocks is None:
             return
         for i, blk in enumerate(blocks):
