@@ -1,0 +1,431 @@
+// FlashAttention backward for sm_100a on tcgen05 tensor cores (head_dim 128, bf16, GQA).
+//
+// One CTA per (128-key tile, KV head, batch) loops over every query head that shares the KV
+// head and over the query tiles inside the causal / sliding-window band, so dK and dV accumulate
+// in tensor memory without atomics. Per query tile (all operands from shared memory, fp32 TMEM
+// accumulators, 256 threads: warp 0 TMA, warp 1 MMA issue, warps 4..7 math):
+//   S^T  = K Q^T            -> TMEM [0,128)     (rows = keys)
+//   dP^T = V dO^T           -> TMEM [128,256)
+//   P^T  = exp(S^T*scale - lse),  dS^T = P^T * (dP^T - D)      (math warps, one key row each)
+//   dV  += P^T dO           -> TMEM [256,384)   (P^T K-major, dO read MN-major)
+//   dK  += dS^T Q           -> TMEM [384,512)   (Q read MN-major)
+//   dQ_i = dS K             -> TMEM [0,128)     (dS^T read MN-major as the A operand; K MN-major)
+// The same shared-memory bytes serve as K-major and MN-major operands: a TMA box of 64 head dims
+// x 128 rows with 128B swizzle is the canonical layout for both. dQ is accumulated across key tiles
+// with 16-byte fp32 vector reductions into an fp32 buffer; a final pass converts it to bf16.
+// D_i = rowsum(dO_i * O_i) is computed by a preprocessing kernel. All waits are bounded.
+#include "common.cuh"
+#include "host_common.h"
+
+namespace mint {
+namespace fab {
+
+constexpr int kB = 128;  // rows per tile (keys or queries)
+constexpr int kD = 128;
+constexpr int kThreads = 256;
+constexpr int kTileBytes = kB * kD * 2;
+constexpr int kAtomBytes = kTileBytes / 2;
+
+struct BwdParams {
+  float* dq_acc;          // [B, T, Hq, D] fp32 (zero-initialized)
+  __nv_bfloat16* dk;      // [B, T, Hkv, D]
+  __nv_bfloat16* dv;      // [B, T, Hkv, D]
+  const float* lse;       // [B, Hq, T] natural log
+  const float* delta;     // [B, Hq, T]
+  const int* doc;         // [B, T] or null
+  int B, T, Hq, Hkv;
+  int causal, window;
+  float scale, scale_log2;
+  uint32_t* status;
+};
+
+struct Smem {
+  uint8_t k[kTileBytes];
+  uint8_t v[kTileBytes];
+  uint8_t q[kTileBytes];
+  uint8_t dout[kTileBytes];
+  uint8_t p[kTileBytes];
+  uint8_t ds[kTileBytes];
+  uint64_t kv_full, q_full, q_empty, do_full, do_empty;
+  uint64_t s_full, dp_full, p_ready, ds_ready, dq_full, dq_free, mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// K-major operand (row-contiguous 128 x 128 tile, 2 atoms along K): descriptor of K-step k
+__device__ __forceinline__ uint64_t kmaj(uint32_t base, int k) {
+  return umma_desc_sw128(base + (k >> 2) * kAtomBytes + (k & 3) * 32, 16, 1024);
+}
+// the same tile read MN-major (its rows are the contraction dim): K-step k = 16 rows
+__device__ __forceinline__ uint64_t mnmaj(uint32_t base, int k) {
+  return umma_desc_sw128(base + k * 2048, kAtomBytes, 1024);
+}
+
+__device__ __forceinline__ void mma_kk(uint32_t d, uint32_t a, uint32_t b, bool acc) {
+  constexpr uint32_t idesc = umma_idesc_bf16(kB, kB, false, false);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) umma_bf16(d, kmaj(a, k), kmaj(b, k), idesc, (acc || k > 0) ? 1u : 0u);
+}
+__device__ __forceinline__ void mma_kmn(uint32_t d, uint32_t a, uint32_t b, bool acc) {
+  constexpr uint32_t idesc = umma_idesc_bf16(kB, kD, false, true);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) umma_bf16(d, kmaj(a, k), mnmaj(b, k), idesc, (acc || k > 0) ? 1u : 0u);
+}
+__device__ __forceinline__ void mma_mnmn(uint32_t d, uint32_t a, uint32_t b, bool acc) {
+  constexpr uint32_t idesc = umma_idesc_bf16(kB, kD, true, true);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) umma_bf16(d, mnmaj(a, k), mnmaj(b, k), idesc, (acc || k > 0) ? 1u : 0u);
+}
+
+// row r of a K-major 128B-swizzled bf16 tile from 128 fp32 values
+__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int r, const float (&x)[128]) {
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int e = a * 64 + c * 8;
+      uint4 v4 = make_uint4(pack_bf16x2(x[e], x[e + 1]), pack_bf16x2(x[e + 2], x[e + 3]),
+                            pack_bf16x2(x[e + 4], x[e + 5]), pack_bf16x2(x[e + 6], x[e + 7]));
+      *reinterpret_cast<uint4*>(tile + a * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
+    }
+  }
+}
+
+__device__ __forceinline__ void load_row128(uint32_t taddr, float (&x)[128]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t u[32];
+    tmem_ld_32x32b_x32(taddr + c * 32, u);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo, BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int G = p.Hq / p.Hkv;
+  const int k0 = kt * kB;
+  const int ntq = (p.T + kB - 1) / kB;
+  const int i0 = p.causal ? k0 / kB : 0;
+  int i1 = ntq;
+  if (p.window >= 0) i1 = min(ntq, (k0 + kB - 1 + p.window) / kB + 1);
+  const int nq = max(0, i1 - i0);
+  const int n = G * nq;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.kv_full, 1);
+    mbar_init(&s.q_full, 1);
+    mbar_init(&s.q_empty, 1);
+    mbar_init(&s.do_full, 1);
+    mbar_init(&s.do_empty, 1);
+    mbar_init(&s.s_full, 1);
+    mbar_init(&s.dp_full, 1);
+    mbar_init(&s.p_ready, 4);
+    mbar_init(&s.ds_ready, 4);
+    mbar_init(&s.dq_full, 1);
+    mbar_init(&s.dq_free, 4);
+    mbar_init(&s.mma_done, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&s.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      tma_prefetch_desc(&tdo);
+      const int krow = b * p.T + k0;
+      mbar_arrive_expect_tx(&s.kv_full, 2 * kTileBytes);
+      tma_load_3d(s.k, &tk, &s.kv_full, 0, hk, krow);
+      tma_load_3d(s.k + kAtomBytes, &tk, &s.kv_full, 64, hk, krow);
+      tma_load_3d(s.v, &tv, &s.kv_full, 0, hk, krow);
+      tma_load_3d(s.v + kAtomBytes, &tv, &s.kv_full, 64, hk, krow);
+      for (int it = 0; it < n; ++it) {
+        const int h = hk * G + it / nq;
+        const int qrow = b * p.T + (i0 + it % nq) * kB;
+        const uint32_t ph = it & 1;
+        if (!mbar_wait(&s.q_empty, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.q_full, kTileBytes);
+        tma_load_3d(s.q, &tq, &s.q_full, 0, h, qrow);
+        tma_load_3d(s.q + kAtomBytes, &tq, &s.q_full, 64, h, qrow);
+        if (!mbar_wait(&s.do_empty, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.do_full, kTileBytes);
+        tma_load_3d(s.dout, &tdo, &s.do_full, 0, h, qrow);
+        tma_load_3d(s.dout + kAtomBytes, &tdo, &s.do_full, 64, h, qrow);
+      }
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      const uint32_t a_k = smem_u32(s.k), a_v = smem_u32(s.v), a_q = smem_u32(s.q), a_do = smem_u32(s.dout);
+      const uint32_t a_p = smem_u32(s.p), a_ds = smem_u32(s.ds);
+      bool ok = mbar_wait(&s.kv_full, 0, p.status, kStatusTimeoutAttention, abort_flag);
+      for (int it = 0; it < n && ok; ++it) {
+        const uint32_t ph = it & 1;
+        if (!(ok = mbar_wait(&s.q_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+        if (!(ok = mbar_wait(&s.do_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+        if (it > 0 && !(ok = mbar_wait(&s.dq_free, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag))) break;
+        tc_fence_after();
+        mma_kk(t_s, a_k, a_q, false);    // S^T = K Q^T
+        umma_commit(&s.s_full);
+        mma_kk(t_dp, a_v, a_do, false);  // dP^T = V dO^T
+        umma_commit(&s.dp_full);
+        if (!(ok = mbar_wait(&s.p_ready, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+        tc_fence_after();
+        mma_kmn(t_dv, a_p, a_do, it > 0);  // dV += P^T dO
+        if (!(ok = mbar_wait(&s.ds_ready, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+        tc_fence_after();
+        mma_kmn(t_dk, a_ds, a_q, it > 0);  // dK += dS^T Q
+        mma_mnmn(t_s, a_ds, a_k, false);   // dQ_i = dS K
+        umma_commit(&s.dq_full);
+        umma_commit(&s.q_empty);
+        umma_commit(&s.do_empty);
+      }
+      umma_commit(&s.mma_done);
+      mbar_wait(&s.mma_done, 0, p.status, kStatusTimeoutAttention, nullptr);
+    }
+  } else if (warp >= 4) {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int kj = k0 + r;
+    const int doc_k = (p.doc != nullptr && kj < p.T) ? p.doc[static_cast<long long>(b) * p.T + kj] : 0;
+    bool ok = n > 0;
+    for (int it = 0; it < n && ok; ++it) {
+      const uint32_t ph = it & 1;
+      const int h = hk * G + it / nq;
+      const int q0 = (i0 + it % nq) * kB;
+      const float* lse_row = p.lse + (static_cast<long long>(b) * p.Hq + h) * p.T;
+      const float* dl_row = p.delta + (static_cast<long long>(b) * p.Hq + h) * p.T;
+      if (!(ok = mbar_wait_warp(&s.s_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      tc_fence_after();
+      float x[128];
+      load_row128(t_s + lane_off, x);
+      const bool need_mask = (p.causal && k0 + kB - 1 > q0) || (p.window >= 0 && q0 + kB - 1 - k0 > p.window) ||
+                             q0 + kB > p.T || k0 + kB > p.T || p.doc != nullptr;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const int qi = q0 + c;
+        bool keep = true;
+        if (need_mask) {
+          keep = qi < p.T && kj < p.T;
+          if (p.causal) keep = keep && kj <= qi;
+          if (p.window >= 0) keep = keep && qi - kj <= p.window;
+          if (p.doc != nullptr && keep) keep = p.doc[static_cast<long long>(b) * p.T + qi] == doc_k;
+        }
+        const float l2 = keep ? lse_row[qi] * 1.4426950408889634f : 0.f;
+        x[c] = keep ? exp2f(x[c] * p.scale_log2 - l2) : 0.f;
+      }
+      store_row_sw128(s.p, r, x);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.p_ready);
+      if (!(ok = mbar_wait_warp(&s.dp_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(t_dp + lane_off + c4 * 32, u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int c = c4 * 32 + e;
+          const int qi = q0 + c;
+          const float dl = qi < p.T ? dl_row[qi] : 0.f;
+          x[c] = x[c] * (__uint_as_float(u[e]) - dl);
+        }
+      }
+      store_row_sw128(s.ds, r, x);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.ds_ready);
+      if (!(ok = mbar_wait_warp(&s.dq_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      tc_fence_after();
+      // dQ rows: TMEM lane = query index within the tile
+      const int qi = q0 + r;
+      float* dst = p.dq_acc + ((static_cast<long long>(b) * p.T + qi) * p.Hq + h) * kD;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(t_s + lane_off + c4 * 32, u);
+        tmem_ld_wait();
+        if (qi < p.T) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            red_add_v4(dst + c4 * 32 + e, __uint_as_float(u[e]) * p.scale, __uint_as_float(u[e + 1]) * p.scale,
+                       __uint_as_float(u[e + 2]) * p.scale, __uint_as_float(u[e + 3]) * p.scale);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.dq_free);
+    }
+    // dK / dV rows: TMEM lane = key index (tcgen05.ld is warp-collective: every lane loads)
+    ok = __all_sync(0xffffffffu, ok);
+    const bool key_ok = kj < p.T;
+    __nv_bfloat16* dkr = p.dk + ((static_cast<long long>(b) * p.T + (key_ok ? kj : 0)) * p.Hkv + hk) * kD;
+    __nv_bfloat16* dvr = p.dv + ((static_cast<long long>(b) * p.T + (key_ok ? kj : 0)) * p.Hkv + hk) * kD;
+    if (ok && n > 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t uk[32], uv[32];
+        tmem_ld_32x32b_x32(t_dk + lane_off + c4 * 32, uk);
+        tmem_ld_32x32b_x32(t_dv + lane_off + c4 * 32, uv);
+        tmem_ld_wait();
+        if (!key_ok) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 a, v;
+          a.x = pack_bf16x2(__uint_as_float(uk[e]) * p.scale, __uint_as_float(uk[e + 1]) * p.scale);
+          a.y = pack_bf16x2(__uint_as_float(uk[e + 2]) * p.scale, __uint_as_float(uk[e + 3]) * p.scale);
+          a.z = pack_bf16x2(__uint_as_float(uk[e + 4]) * p.scale, __uint_as_float(uk[e + 5]) * p.scale);
+          a.w = pack_bf16x2(__uint_as_float(uk[e + 6]) * p.scale, __uint_as_float(uk[e + 7]) * p.scale);
+          v.x = pack_bf16x2(__uint_as_float(uv[e]), __uint_as_float(uv[e + 1]));
+          v.y = pack_bf16x2(__uint_as_float(uv[e + 2]), __uint_as_float(uv[e + 3]));
+          v.z = pack_bf16x2(__uint_as_float(uv[e + 4]), __uint_as_float(uv[e + 5]));
+          v.w = pack_bf16x2(__uint_as_float(uv[e + 6]), __uint_as_float(uv[e + 7]));
+          *reinterpret_cast<uint4*>(dkr + c4 * 32 + e) = a;
+          *reinterpret_cast<uint4*>(dvr + c4 * 32 + e) = v;
+        }
+      }
+    } else if (n == 0 && key_ok) {
+      for (int c = 0; c < kD; ++c) {
+        dkr[c] = __float2bfloat16_rn(0.f);
+        dvr[c] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[b, h, i] = sum_d dO[b, i, h, d] * O[b, i, h, d]   (one warp per row)
+__global__ void __launch_bounds__(256) fa_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout,
+                                                           const __nv_bfloat16* __restrict__ o,
+                                                           float* __restrict__ delta, int B, int T, int Hq) {
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= static_cast<long long>(B) * T * Hq) return;
+  const __nv_bfloat16* a = dout + row * kD + lane * 4;
+  const __nv_bfloat16* c = o + row * kD + lane * 4;
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) acc += __bfloat162float(a[e]) * __bfloat162float(c[e]);
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const int h = static_cast<int>(row % Hq);
+    const long long bt = row / Hq;
+    const int t = static_cast<int>(bt % T);
+    const int bb = static_cast<int>(bt / T);
+    delta[(static_cast<long long>(bb) * Hq + h) * T + t] = acc;
+  }
+}
+
+__global__ void fa_cast_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long long n4) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    uint2 u;
+    u.x = pack_bf16x2(v.x, v.y);
+    u.y = pack_bf16x2(v.z, v.w);
+    reinterpret_cast<uint2*>(dst)[i] = u;
+  }
+}
+
+}  // namespace fab
+
+std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                       const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                                       const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
+                                       double scale) {
+  const at::Tensor* inputs[5] = {&dout, &q, &k, &v, &o};
+  for (const at::Tensor* t : inputs) {
+    check_contig(*t, "flash_attn_bwd input");
+    MINT_CHECK(t->scalar_type() == at::kBFloat16, "flash_attn_bwd expects bf16");
+  }
+  const int B = static_cast<int>(q.size(0)), T = static_cast<int>(q.size(1));
+  const int Hq = static_cast<int>(q.size(2)), Hkv = static_cast<int>(k.size(2));
+  MINT_CHECK(q.size(3) == fab::kD && Hq % Hkv == 0 && dout.sizes() == q.sizes() && o.sizes() == q.sizes(),
+             "flash_attn_bwd shape mismatch");
+  auto dq_acc = at::zeros(q.sizes(), q.options().dtype(at::kFloat));
+  auto dq = at::empty_like(q);
+  auto dk = at::empty_like(k);
+  auto dv = at::empty_like(v);
+  auto delta = at::empty({B, Hq, T}, q.options().dtype(at::kFloat));
+  if (B == 0 || T == 0) return {dq.zero_(), dk.zero_(), dv.zero_()};
+  c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const long long rows = static_cast<long long>(B) * T * Hq;
+  fab::fa_bwd_delta_kernel<<<static_cast<int>((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()),
+      delta.data_ptr<float>(), B, T, Hq);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+
+  fab::BwdParams p{};
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  if (doc.has_value() && doc->defined()) p.doc = doc->data_ptr<int>();
+  p.B = B;
+  p.T = T;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.causal = causal ? 1 : 0;
+  p.window = static_cast<int>(window);
+  p.scale = static_cast<float>(scale);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.status = status_ptr(q.get_device());
+  auto map = [&](const at::Tensor& t, int H) {
+    return make_tmap_3d_bf16(t.data_ptr(), fab::kD, H, static_cast<uint64_t>(B) * T, fab::kD,
+                             static_cast<uint64_t>(H) * fab::kD, 64, 1, 128, true);
+  };
+  const CUtensorMap tq = map(q, Hq), tk = map(k, Hkv), tv = map(v, Hkv), tdo = map(dout, Hq);
+  const int smem = static_cast<int>(sizeof(fab::Smem)) + 1024;
+  static bool configured = false;
+  if (!configured) {
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(fab::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  dim3 grid((T + fab::kB - 1) / fab::kB, Hkv, B);
+  fab::fa_bwd_kernel<<<grid, fab::kThreads, smem, stream>>>(tq, tk, tv, tdo, p);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  const long long n4 = q.numel() / 4;
+  fab::fa_cast_kernel<<<static_cast<int>(std::min<long long>((n4 + 255) / 256, 148LL * 16)), 256, 0, stream>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n4);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {dq, dk, dv};
+}
+
+}  // namespace mint

@@ -1,0 +1,387 @@
+// FlashAttention forward for sm_100a on tcgen05 tensor cores (head_dim 128, bf16, GQA).
+//
+// One CTA per (128-query tile, query head, batch); 256 threads:
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles into 2-stage rings (128B swizzle)
+//   warp 1      TMEM owner + single-thread MMA issue:
+//                 S_j = Q K_j^T   (M=128 queries, N=128 keys, K=128)  -> TMEM S buffer j%2
+//                 O  += P_j V_j   (M=128, N=128 head dims, K=128 keys, P from shared memory)
+//               S_{j+1} is issued before PV_j so the softmax of tile j+1 overlaps PV_j.
+//   warps 4..7  softmax: each thread owns one query row (TMEM lane), loads its 128 scores with
+//               tcgen05.ld, applies causal / sliding-window / document / sequence-end masks,
+//               exp2 with a lazily updated running max (O is rescaled in TMEM only when the max
+//               grows by more than 2^8), writes P (bf16) in the 128B-swizzled K-major layout the
+//               PV MMA reads, and finally normalizes O and stores O and the log-sum-exp.
+// Tiles outside the causal / window band are never visited. All waits are bounded.
+#include "common.cuh"
+#include "host_common.h"
+
+namespace mint {
+namespace fa {
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kD = 128;
+constexpr int kThreads = 256;
+constexpr int kTileBytes = kBM * kD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-wide swizzle atoms)
+constexpr int kAtomBytes = kTileBytes / 2;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FwdParams {
+  __nv_bfloat16* o;       // [B, T, Hq, D]
+  float* lse;             // [B, Hq, T]
+  const int* doc;         // [B, T] or null
+  int B, T, Hq, Hkv;
+  int causal, window;     // window < 0: none
+  float scale_log2;       // softmax scale * log2(e)
+  uint32_t* status;
+};
+
+struct Smem {
+  uint8_t q[kTileBytes];
+  uint8_t k[2][kTileBytes];
+  uint8_t v[2][kTileBytes];
+  uint8_t p[kTileBytes];
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t pv_done;
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ void kv_range(int q0, int T, int causal, int window, int& j0, int& j1) {
+  const int q_last = min(T, q0 + kBM) - 1;
+  const int hi = causal ? q_last + 1 : T;
+  const int lo = window >= 0 ? max(0, q0 - window) : 0;
+  j0 = lo / kBN;
+  j1 = (hi + kBN - 1) / kBN;
+}
+
+// S = Q K^T: both operands K-major (head dim contiguous), 2 swizzle atoms along K.
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
+  constexpr uint32_t idesc = umma_idesc_bf16(kBM, kBN, false, false);
+#pragma unroll
+  for (int k = 0; k < kD / 16; ++k) {
+    const uint32_t off = (k >> 2) * kAtomBytes + (k & 3) * 32;
+    umma_bf16(d_tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024), idesc,
+              k > 0 ? 1u : 0u);
+  }
+}
+
+// O += P V: P K-major (keys contiguous, 2 atoms along K); V MN-major (head dim contiguous):
+// atoms of 64 head dims x 128 key rows (16 KB apart), 16 keys = 2048 bytes per K step.
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_addr, uint32_t v_addr, bool accumulate) {
+  constexpr uint32_t idesc = umma_idesc_bf16(kBM, kD, false, true);
+#pragma unroll
+  for (int k = 0; k < kBN / 16; ++k) {
+    const uint32_t poff = (k >> 2) * kAtomBytes + (k & 3) * 32;
+    umma_bf16(d_tmem, umma_desc_sw128(p_addr + poff, 16, 1024), umma_desc_sw128(v_addr + k * 2048, kAtomBytes, 1024),
+              idesc, (accumulate || k > 0) ? 1u : 0u);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                  const __grid_constant__ CUtensorMap tv, FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int q0 = qt * kBM;
+  int j0, j1;
+  kv_range(q0, p.T, p.causal, p.window, j0, j1);
+  const int n = j1 - j0;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.k_empty[i], 1);
+      mbar_init(&s.v_full[i], 1);
+      mbar_init(&s.v_empty[i], 1);
+      mbar_init(&s.s_full[i], 1);
+    }
+    mbar_init(&s.p_full, 4);
+    mbar_init(&s.pv_done, 1);
+    mbar_init(&s.mma_done, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&s.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t tmem_o = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      const int qrow = b * p.T + q0;
+      mbar_arrive_expect_tx(&s.q_full, kTileBytes);
+      tma_load_3d(s.q, &tq, &s.q_full, 0, h, qrow);
+      tma_load_3d(s.q + kAtomBytes, &tq, &s.q_full, 64, h, qrow);
+      for (int t = 0; t < n; ++t) {
+        const int st = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
+        const int krow = b * p.T + (j0 + t) * kBN;
+        if (!mbar_wait(&s.k_empty[st], ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
+        tma_load_3d(s.k[st], &tk, &s.k_full[st], 0, hk, krow);
+        tma_load_3d(s.k[st] + kAtomBytes, &tk, &s.k_full[st], 64, hk, krow);
+        if (!mbar_wait(&s.v_empty[st], ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
+        tma_load_3d(s.v[st], &tv, &s.v_full[st], 0, hk, krow);
+        tma_load_3d(s.v[st] + kAtomBytes, &tv, &s.v_full[st], 64, hk, krow);
+      }
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      const uint32_t q_addr = smem_u32(s.q);
+      const uint32_t p_addr = smem_u32(s.p);
+      bool ok = mbar_wait(&s.q_full, 0, p.status, kStatusTimeoutAttention, abort_flag);
+      if (ok && (ok = mbar_wait(&s.k_full[0], 0, p.status, kStatusTimeoutAttention, abort_flag))) {
+        tc_fence_after();
+        issue_qk(tmem, q_addr, smem_u32(s.k[0]));
+        umma_commit(&s.s_full[0]);
+        umma_commit(&s.k_empty[0]);
+      }
+      for (int t = 0; t < n && ok; ++t) {
+        if (t + 1 < n) {
+          const int st = (t + 1) & 1;
+          if (!mbar_wait(&s.k_full[st], ((t + 1) >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
+          tc_fence_after();
+          issue_qk(tmem + st * 128, q_addr, smem_u32(s.k[st]));
+          umma_commit(&s.s_full[st]);
+          umma_commit(&s.k_empty[st]);
+        }
+        if (!mbar_wait(&s.p_full, t & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        if (!mbar_wait(&s.v_full[t & 1], (t >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        tc_fence_after();
+        issue_pv(tmem_o, p_addr, smem_u32(s.v[t & 1]), t > 0);
+        umma_commit(&s.pv_done);
+        umma_commit(&s.v_empty[t & 1]);
+      }
+      umma_commit(&s.mma_done);
+      mbar_wait(&s.mma_done, 0, p.status, kStatusTimeoutAttention, nullptr);
+    }
+  } else if (warp >= 4) {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int doc_q = (p.doc != nullptr && qi < p.T) ? p.doc[static_cast<long long>(b) * p.T + qi] : 0;
+    float m = -INFINITY, l = 0.f;
+    bool ok = n > 0;
+    int pv_waited = -1;  // index of the last PV whose completion this thread observed
+    for (int t = 0; t < n && ok; ++t) {
+      const int kb = (j0 + t) * kBN;
+      if (!mbar_wait_warp(&s.s_full[t & 1], (t >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + c * 32, u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
+      }
+      const bool need_mask = (p.causal && kb + kBN - 1 > q0) || (p.window >= 0 && q0 + kBM - 1 - kb > p.window) ||
+                             kb + kBN > p.T || p.doc != nullptr;
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const int kj = kb + c;
+          bool keep = kj < p.T;
+          if (p.causal) keep = keep && kj <= qi;
+          if (p.window >= 0) keep = keep && qi - kj <= p.window;
+          if (p.doc != nullptr && keep) keep = p.doc[static_cast<long long>(b) * p.T + kj] == doc_q;
+          if (!keep) x[c] = -INFINITY;
+        }
+      }
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mt = fmaxf(mt, x[c]);
+      const float m_new = fmaxf(m, mt);
+      // tcgen05.ld/st are warp-collective: the rescale decision must be uniform across the warp
+      const bool grow = m != -INFINITY && m_new > m + kRescaleThreshold;
+      if (t > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds PV_0..PV_{t-1}: wait for PV_{t-1}, then rescale the rows in tensor memory
+        if (pv_waited < t - 1) {
+          if (!mbar_wait_warp(&s.pv_done, (t - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
+            ok = false;
+            break;
+          }
+          pv_waited = t - 1;
+          tc_fence_after();
+        }
+        const float alpha = (m == -INFINITY || m_new == -INFINITY) ? 0.f : exp2f(m - m_new);
+        l *= alpha;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t u[16];
+          tmem_ld_32x32b_x16(tmem_o + lane_off + c * 16, u);
+          tmem_ld_wait();
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+          tmem_st_32x32b_x16(tmem_o + lane_off + c * 16, w);
+        }
+        tmem_st_wait();
+        m = m_new;
+      } else if (m == -INFINITY) {
+        m = m_new;  // nothing accumulated in this row yet
+      }
+      // P = exp2(x - m) in bf16, row sum in fp32
+      uint32_t pk[64];
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float a = (m == -INFINITY) ? 0.f : exp2f(x[2 * c] - m);
+        const float bb = (m == -INFINITY) ? 0.f : exp2f(x[2 * c + 1] - m);
+        rs += a + bb;
+        pk[c] = pack_bf16x2(a, bb);
+      }
+      l += rs;
+      // the single P buffer is free once PV_{t-1} completed
+      if (t > 0 && pv_waited < t - 1) {
+        if (!mbar_wait_warp(&s.pv_done, (t - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
+          ok = false;
+          break;
+        }
+        pv_waited = t - 1;
+      }
+      // 128B-swizzled K-major store of this row: atom a (64 keys), 16B chunk c at c ^ (row % 8)
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 v4 = make_uint4(pk[a * 32 + c * 4], pk[a * 32 + c * 4 + 1], pk[a * 32 + c * 4 + 2], pk[a * 32 + c * 4 + 3]);
+          *reinterpret_cast<uint4*>(s.p + a * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.p_full);
+    }
+    if (ok && n > 0 && pv_waited < n - 1) {
+      ok = mbar_wait_warp(&s.pv_done, (n - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool row_ok = qi < p.T;
+      __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + (row_ok ? qi : 0)) * p.Hq + h) * kD;
+      {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t u[32];
+          tmem_ld_32x32b_x32(tmem_o + lane_off + c * 32, u);  // warp-collective: every lane loads
+          tmem_ld_wait();
+          if (!row_ok) continue;
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 v4;
+            v4.x = pack_bf16x2(__uint_as_float(u[e]) * inv, __uint_as_float(u[e + 1]) * inv);
+            v4.y = pack_bf16x2(__uint_as_float(u[e + 2]) * inv, __uint_as_float(u[e + 3]) * inv);
+            v4.z = pack_bf16x2(__uint_as_float(u[e + 4]) * inv, __uint_as_float(u[e + 5]) * inv);
+            v4.w = pack_bf16x2(__uint_as_float(u[e + 6]) * inv, __uint_as_float(u[e + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v4;
+          }
+        }
+        // natural-log LSE of the scaled scores: (m + log2 l) * ln 2
+        if (row_ok) {
+          p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] =
+              l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+        }
+      }
+    } else if (n == 0 && qi < p.T) {
+      __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + qi) * p.Hq + h) * kD;
+      for (int c = 0; c < kD; ++c) orow[c] = __float2bfloat16_rn(0.f);
+      p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] = -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fa
+
+std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                       const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
+                                       double scale) {
+  check_contig(q, "q");
+  check_contig(k, "k");
+  check_contig(v, "v");
+  MINT_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
+             "flash_attn expects bf16");
+  MINT_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "flash_attn expects [B, T, H, D]");
+  const int B = static_cast<int>(q.size(0)), T = static_cast<int>(q.size(1));
+  const int Hq = static_cast<int>(q.size(2)), Hkv = static_cast<int>(k.size(2));
+  MINT_CHECK(q.size(3) == fa::kD && k.size(3) == fa::kD && v.size(3) == fa::kD, "head_dim must be 128");
+  MINT_CHECK(k.size(1) == T && v.size(1) == T && k.size(0) == B && v.sizes() == k.sizes(), "k/v shape mismatch");
+  MINT_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
+  auto o = at::empty_like(q);
+  auto lse = at::empty({B, Hq, T}, q.options().dtype(at::kFloat));
+  if (B == 0 || T == 0) return {o, lse};
+  c10::cuda::CUDAGuard guard(q.device());
+  fa::FwdParams p{};
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.lse = lse.data_ptr<float>();
+  if (doc.has_value() && doc->defined()) {
+    check_contig(*doc, "doc_ids");
+    MINT_CHECK(doc->scalar_type() == at::kInt && doc->numel() == static_cast<int64_t>(B) * T, "doc_ids must be int32 [B, T]");
+    p.doc = doc->data_ptr<int>();
+  }
+  p.B = B;
+  p.T = T;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.causal = causal ? 1 : 0;
+  p.window = static_cast<int>(window);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.status = status_ptr(q.get_device());
+  const CUtensorMap tq = make_tmap_3d_bf16(q.data_ptr(), fa::kD, Hq, static_cast<uint64_t>(B) * T, fa::kD,
+                                           static_cast<uint64_t>(Hq) * fa::kD, 64, 1, 128, true);
+  const CUtensorMap tk = make_tmap_3d_bf16(k.data_ptr(), fa::kD, Hkv, static_cast<uint64_t>(B) * T, fa::kD,
+                                           static_cast<uint64_t>(Hkv) * fa::kD, 64, 1, 128, true);
+  const CUtensorMap tv = make_tmap_3d_bf16(v.data_ptr(), fa::kD, Hkv, static_cast<uint64_t>(B) * T, fa::kD,
+                                           static_cast<uint64_t>(Hkv) * fa::kD, 64, 1, 128, true);
+  const int smem = static_cast<int>(sizeof(fa::Smem)) + 1024;
+  static bool configured = false;
+  if (!configured) {
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  dim3 grid((T + fa::kBM - 1) / fa::kBM, Hq, B);
+  fa::fa_fwd_kernel<<<grid, fa::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return {o, lse};
+}
+
+}  // namespace mint

@@ -5,7 +5,8 @@
 
 namespace mint {
 void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& D,
-               bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t);
+               bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t,
+               bool accumulate);
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& scale, double eps, int64_t out_code);
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd,
                                     const at::Tensor& scale, int64_t dx_code);
@@ -35,6 +36,13 @@ void ce_grad_inplace(at::Tensor& logits, const at::Tensor& targets, const at::Te
                      const at::Tensor& denom, int64_t valid, int64_t vstart);
 void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1, double b2,
                 double eps, double wd, int64_t step);
+std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                       const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
+                                       double scale);
+std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                       const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                                       const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
+                                       double scale);
 }  // namespace mint
 
 static int64_t read_status(bool reset) {
@@ -49,7 +57,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("reset") = false);
   m.def("gemm", &mint::gemm_bf16, "C = alpha * op(A) @ op(B) + beta * D (tcgen05)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("D"), py::arg("a_kmajor"), py::arg("b_kmajor"), py::arg("alpha") = 1.0,
-        py::arg("beta") = 0.0, py::arg("alpha_t") = py::none());
+        py::arg("beta") = 0.0, py::arg("alpha_t") = py::none(), py::arg("accumulate") = false);
   m.def("launch_count", &mint::launch_count, "kernels launched by this extension so far");
   m.def("rmsnorm_fwd", &mint::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &mint::rmsnorm_bwd);
@@ -65,4 +73,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_row_stats", &mint::ce_row_stats);
   m.def("ce_grad_inplace", &mint::ce_grad_inplace);
   m.def("adamw_step", &mint::adamw_step);
+  m.def("flash_attn_fwd", &mint::flash_attn_fwd, "tcgen05 FlashAttention forward -> (o, lse)");
+  m.def("flash_attn_bwd", &mint::flash_attn_bwd, "tcgen05 FlashAttention backward -> (dq, dk, dv)");
 }

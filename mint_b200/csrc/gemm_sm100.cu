@@ -42,6 +42,9 @@ struct Params {
   const float* alpha_ptr;
   int c_fp32, d_fp32;
   int tiles_m, tiles_n;
+  int splits;      // split-K factor: work item = (tile, split)
+  int kbps;        // k-blocks per split
+  int atomic_out;  // C (fp32) += alpha * acc with 16-byte vector reductions
   uint32_t* status;
 };
 
@@ -54,6 +57,16 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   const int r = tile % per_group;
   tm = first_m + r % gsize;
   tn = r / gsize;
+}
+
+// work item -> (tile m, tile n, first k-block, k-block count)
+__device__ __forceinline__ void work_item(const Params& p, int w, int kblocks, int& tm, int& tn, int& kb0, int& nkb) {
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int tile = w % tiles;
+  const int split = w / tiles;
+  tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+  kb0 = split * p.kbps;
+  nkb = min(kblocks, kb0 + p.kbps) - kb0;
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -94,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int num_tiles = p.tiles_m * p.tiles_n * p.splits;
   const int kblocks = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
@@ -105,10 +118,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int tm, tn;
-        tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+        int tm, tn, kb0, nkb;
+        work_item(p, tile, kblocks, tm, tn, kb0, nkb);
         const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb0 + nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer, abort_flag)) {
             ok = false;
             break;
@@ -155,7 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, kStatusTimeoutMma, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        int tm_, tn_, kb0, nkb;
+        work_item(p, tile, kblocks, tm_, tn_, kb0, nkb);
+        for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma, abort_flag)) {
             ok = false;
             break;
@@ -195,10 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
-      int tm, tn;
-      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      int tm, tn, kb0_, nkb_;
+      work_item(p, tile, kblocks, tm, tn, kb0_, nkb_);
       const int row = tm * BM + row_in_tile;
       const bool row_ok = row < p.M;
 #pragma unroll 1
@@ -247,7 +262,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (p.c_fp32) {
+        if (p.atomic_out) {
+          float* cp = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col0;
+          if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) red_add_v4(cp + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < p.N; ++j) atomicAdd(cp + j, v[j]);
+          }
+        } else if (p.c_fp32) {
           float* cp = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col0;
           if (full_chunk) {
 #pragma unroll
@@ -295,7 +318,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int s
     MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes));
     configured = true;
   }
-  const int tiles = p.tiles_m * p.tiles_n;
+  const int tiles = p.tiles_m * p.tiles_n * p.splits;
   const int grid = tiles < sms ? tiles : sms;
   kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, p);
   MINT_CUDA_CHECK(cudaGetLastError());
@@ -305,8 +328,11 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int s
 }  // namespace gemm
 
 // C = alpha * op(A) @ op(B) + beta * D.  a_kmajor: A stored [M,K]; else [K,M].  b_kmajor: B stored [N,K]; else [K,N].
+// accumulate = true: C (fp32) += alpha * op(A) @ op(B) through vector reductions; the contraction is
+// split across CTAs (split-K) when the output alone has too few tiles to fill the GPU.
 void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& D,
-               bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t) {
+               bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t,
+               bool accumulate) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   check_cuda(C, "C");
@@ -366,6 +392,22 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c1
   const int BN = use256 ? 256 : 128;
   p.tiles_m = static_cast<int>((M + 127) / 128);
   p.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  const int kblocks = static_cast<int>((K + gemm::BK - 1) / gemm::BK);
+  p.splits = 1;
+  p.kbps = kblocks;
+  if (accumulate) {
+    MINT_CHECK(p.c_fp32, "accumulating GEMM needs an fp32 C");
+    MINT_CHECK(p.D == nullptr, "accumulating GEMM adds into C; D is not used");
+    p.atomic_out = 1;
+    const int tiles = p.tiles_m * p.tiles_n;
+    if (tiles < sms && kblocks >= 8) {
+      // enough (tile, split) work items for ~2 waves, each split with >= 4 k-blocks
+      int splits = std::min((2 * sms + tiles - 1) / tiles, kblocks / 4);
+      splits = std::max(splits, 1);
+      p.kbps = (kblocks + splits - 1) / splits;
+      p.splits = (kblocks + p.kbps - 1) / p.kbps;
+    }
+  }
   const int64_t lda = A.stride(0), ldb = B.stride(0);
   const CUtensorMap ta = a_kmajor ? make_tmap_2d_bf16(A.data_ptr(), M, K, lda, 128, 64, true)
                                   : make_tmap_2d_bf16(A.data_ptr(), K, M, lda, 64, 64, true);

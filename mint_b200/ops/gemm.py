@@ -46,9 +46,16 @@ def matmul(
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype | None = None,
     alpha_tensor: torch.Tensor | None = None,
+    accumulate: bool = False,
 ) -> torch.Tensor:
     """2-D GEMM. ``d`` may alias ``out`` (in-place accumulate). ``alpha_tensor`` (1-element fp32 on
-    the device) multiplies ``alpha`` without a host synchronization."""
+    the device) multiplies ``alpha`` without a host synchronization. ``accumulate=True`` adds the
+    product into the fp32 ``out`` (split-K with vector reductions on CUDA)."""
+    if accumulate:
+        if out is None or out.dtype != torch.float32:
+            raise ValueError("accumulate=True needs an fp32 out tensor")
+        if d is not None:
+            raise ValueError("accumulate=True adds into out; pass no d")
     assert a.dim() == 2 and b.dim() == 2
     m = a.shape[1] if trans_a else a.shape[0]
     k = a.shape[0] if trans_a else a.shape[1]
@@ -68,15 +75,23 @@ def matmul(
         out_ok = out.stride(1) == 1 and (out.stride(0) * out.element_size()) % 16 == 0
         d_ok = d is None or (d.stride(1) == 1 and (d.stride(0) * d.element_size()) % 16 == 0)
         if _tma_ok(a) and _tma_ok(b) and out_ok and d_ok:
-            C.gemm(a, b, out, d, not trans_a, trans_b, float(alpha), float(beta), alpha_tensor)
+            C.gemm(a, b, out, d, not trans_a, trans_b, float(alpha), float(beta), alpha_tensor, accumulate)
             return out
         # operands whose rows are not 16-byte multiples cannot be described to TMA
-        out.copy_(_ref(a, b, trans_a, trans_b, alpha, beta, d, out_dtype)
-                  * (1.0 if alpha_tensor is None else alpha_tensor.float()))
+        res = _ref(a, b, trans_a, trans_b, alpha, beta, d, torch.float32)
+        if alpha_tensor is not None:
+            res = res * alpha_tensor.float()
+        if accumulate:
+            out.add_(res)
+        else:
+            out.copy_(res)
         return out
     res = _ref(a, b, trans_a, trans_b, alpha, beta, d, out_dtype)
     if alpha_tensor is not None:
         res = (res.float() * alpha_tensor.float()).to(out_dtype)
+    if accumulate:
+        out.add_(res.float())
+        return out
     if out is not None:
         out.copy_(res)
         return out

@@ -16,11 +16,45 @@ from mint_b200.ops import _ext
 from mint_b200.ops.gemm import matmul
 
 
+def _main_grad(w: torch.Tensor) -> torch.Tensor | None:
+    """The fp32 gradient-bucket view of an engine-managed weight (CUDA), else None."""
+    if not hasattr(w, "_mint_grad_ready"):
+        return None
+    g = w.grad
+    if g is None or g.dtype != torch.float32 or not g.is_cuda or g.shape != getattr(w, "_orig_shape", w.shape):
+        return None
+    return g
+
+
+_CAST_CACHE: dict[tuple, tuple[tuple, torch.Tensor]] = {}
+
+
+def _stamp(weights: tuple[torch.Tensor, ...]) -> tuple | None:
+    """Identity of the weights' current values; None disables caching (ZeRO-3 re-gathers)."""
+    eng = getattr(weights[0], "_grad_engine", None)
+    if eng is not None and eng.level == 3 and eng.dp > 1:
+        return None
+    epoch = eng.epoch if eng is not None else 0
+    return (epoch, tuple(w.data_ptr() for w in weights), tuple(w._version for w in weights))
+
+
 def _cast_weight(weights: tuple[torch.Tensor, ...], dtype: torch.dtype) -> torch.Tensor:
+    """bf16 (compute dtype) copy of the concatenated weights, cached until the weights change."""
+    if len(weights) == 1 and weights[0].dtype == dtype and weights[0].is_contiguous():
+        return weights[0]
+    key = (tuple(id(w) for w in weights), dtype)
+    stamp = _stamp(weights)
+    if stamp is not None:
+        hit = _CAST_CACHE.get(key)
+        if hit is not None and hit[0] == stamp:
+            return hit[1]
     if len(weights) == 1:
-        w = weights[0]
-        return w if w.dtype == dtype and w.is_contiguous() else w.to(dtype).contiguous()
-    return torch.cat([w.to(dtype) for w in weights], dim=0)
+        out = weights[0].detach().to(dtype).contiguous()
+    else:
+        out = torch.cat([w.detach().to(dtype) for w in weights], dim=0)
+    if stamp is not None:
+        _CAST_CACHE[key] = (stamp, out)
+    return out
 
 
 class _LinearFn(torch.autograd.Function):
@@ -56,13 +90,24 @@ class _LinearFn(torch.autograd.Function):
                 dx = dx.to(ctx.x_dtype)
         grads: list[torch.Tensor | None] = [None] * len(weights)
         want = [ctx.needs_input_grad[2 + i] for i in range(len(weights))]
-        if any(want):
+        fused = [want[i] and _main_grad(w) is not None for i, w in enumerate(weights)]
+        if any(fused):
+            # weight-gradient GEMMs accumulate straight into the gradient engine's fp32 buckets
+            off = 0
+            for i, w in enumerate(weights):
+                rows = w.shape[0]
+                if fused[i]:
+                    mg = _main_grad(w)
+                    matmul(dy2[:, off : off + rows], x2, trans_a=True, out=mg.view(rows, -1), accumulate=True)
+                    w._mint_grad_ready()
+                off += rows
+        if any(want[i] and not fused[i] for i in range(len(weights))):
             gdtype = weights[0].dtype if weights[0].dtype in (torch.float32, torch.bfloat16) else torch.float32
             dw = matmul(dy2, x2, trans_a=True, out_dtype=gdtype)
             off = 0
             for i, w in enumerate(weights):
                 rows = w.shape[0]
-                if want[i]:
+                if want[i] and not fused[i]:
                     grads[i] = dw[off : off + rows]
                 off += rows
         return (dx, None, *grads)

@@ -61,34 +61,78 @@ class DistMuonAdamW(Optimizer):
         super().zero_grad(set_to_none=True)
 
     # ------------------------------------------------------------------ units
-    def _adamw_units(self, group: dict) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor, dict]]:
+    def _bucket_shard(self, b) -> tuple[torch.Tensor, torch.Tensor, int]:  # noqa: ANN001
+        """(param shard, grad shard, shard offset in bucket coordinates) of bucket ``b`` on this rank."""
         eng = self._engine
-        units = []
-        for p in group["params"]:
-            if eng is None or id(p) not in eng.by_param:
-                if p.grad is None:
-                    continue
-                units.append((p, p.data, p.grad, self.state[p]))
+        if eng.level == 0 or eng.dp == 1:
+            return b.data, b.grad, 0
+        lo = eng.rank * b.shard
+        gv = b.grad[lo : lo + b.shard] if eng.level == 1 else b.grad_shard
+        return b.shard_data, gv, lo
+
+    def _ensure_bucket_state(self, b) -> dict:  # noqa: ANN001
+        """Bucket-level AdamW moments; every parameter's state holds views into them."""
+        st = self._shard_state.get(b.index)
+        if st is not None:
+            return st
+        pv, _gv, lo = self._bucket_shard(b)
+        st = {"step": 0, "exp_avg": torch.zeros_like(pv), "exp_avg_sq": torch.zeros_like(pv), "views": []}
+        n = pv.numel()
+        for sl in b.slots:
+            a, e = max(lo, sl.start), min(lo + n, sl.start + sl.numel)
+            if a >= e:
                 continue
-            for pv, gv, off, n in eng.segments(p):
-                st = self.state[p]
-                key = f"shard@{off}"
-                if key not in st:
-                    st[key] = {"step": 0, "exp_avg": torch.zeros_like(pv), "exp_avg_sq": torch.zeros_like(pv),
-                               "offset": off, "numel": n}
-                units.append((p, pv, gv, st[key]))
-        return units
+            sub = {"step": 0, "exp_avg": st["exp_avg"][a - lo : e - lo], "exp_avg_sq": st["exp_avg_sq"][a - lo : e - lo],
+                   "offset": a - sl.start, "numel": e - a}
+            self.state[sl.param][f"shard@{a - sl.start}"] = sub
+            st["views"].append(sub)
+        self._shard_state[b.index] = st
+        return st
 
     def _step_adamw(self, group: dict) -> None:
         beta1, beta2 = group["betas"]
-        for _p, pv, gv, st in self._adamw_units(group):
-            if "step" not in st:
-                st["step"] = 0
-                st["exp_avg"] = torch.zeros_like(pv)
-                st["exp_avg_sq"] = torch.zeros_like(pv)
-            st["step"] += 1
-            adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
-                         group["eps"], group["weight_decay"])
+        eng = self._engine
+        ids = {id(p) for p in group["params"]}
+        covered: set[int] = set()
+        if eng is not None:
+            # one fused update per bucket shard whose parameters all belong to this group
+            for b in eng.buckets:
+                if not all(id(sl.param) in ids for sl in b.slots):
+                    continue
+                covered.update(id(sl.param) for sl in b.slots)
+                pv, gv, _lo = self._bucket_shard(b)
+                if gv is None or pv.numel() == 0:
+                    continue
+                st = self._ensure_bucket_state(b)
+                st["step"] += 1
+                adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
+                             group["eps"], group["weight_decay"])
+                for sub in st["views"]:
+                    sub["step"] = st["step"]
+        for p in group["params"]:
+            if id(p) in covered:
+                continue
+            if eng is None or id(p) not in eng.by_param:
+                if p.grad is None:
+                    continue
+                units = [(p.data, p.grad, self.state[p])]
+            else:
+                units = []
+                for pv, gv, off, n in eng.segments(p):
+                    key = f"shard@{off}"
+                    st = self.state[p]
+                    if key not in st:
+                        st[key] = {"step": 0, "exp_avg": torch.zeros_like(pv), "exp_avg_sq": torch.zeros_like(pv),
+                                   "offset": off, "numel": n}
+                    units.append((pv, gv, st[key]))
+            for pv, gv, st in units:
+                if "step" not in st:
+                    st["step"] = 0
+                    st["exp_avg"] = torch.zeros_like(pv)
+                    st["exp_avg_sq"] = torch.zeros_like(pv)
+                st["step"] += 1
+                adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
+                             group["eps"], group["weight_decay"])
 
     def _step_muon(self, group: dict) -> None:
         eng = self._engine
@@ -269,6 +313,7 @@ class DistMuonAdamW(Optimizer):
             raise ValueError("optimizer state has a different number of param groups")
         eng = self._engine
         self.state.clear()
+        self._shard_state.clear()
         for g, sg in zip(self.param_groups, saved_groups, strict=True):
             for k, v in sg.items():
                 if k != "params":
@@ -285,13 +330,16 @@ class DistMuonAdamW(Optimizer):
                                          "exp_avg": st_saved["exp_avg"].to(dev, torch.float32).view_as(p).clone(),
                                          "exp_avg_sq": st_saved["exp_avg_sq"].to(dev, torch.float32).view_as(p).clone()}
                         continue
-                    st = {}
-                    for pv, _gv, off, n in eng.segments(p):
-                        ea = st_saved["exp_avg"].reshape(-1)[off : off + n].to(pv.device, pv.dtype).clone()
-                        es = st_saved["exp_avg_sq"].reshape(-1)[off : off + n].to(pv.device, pv.dtype).clone()
-                        st[f"shard@{off}"] = {"step": int(st_saved["step"]), "exp_avg": ea, "exp_avg_sq": es,
-                                              "offset": off, "numel": n}
-                    self.state[p] = st
+                    bkt, _slot = eng.slot(p)
+                    bst = self._ensure_bucket_state(bkt)
+                    bst["step"] = int(st_saved["step"])
+                    for key, sub in self.state[p].items():
+                        if not key.startswith("shard@"):
+                            continue
+                        off, n = sub["offset"], sub["numel"]
+                        sub["exp_avg"].copy_(st_saved["exp_avg"].reshape(-1)[off : off + n])
+                        sub["exp_avg_sq"].copy_(st_saved["exp_avg_sq"].reshape(-1)[off : off + n])
+                        sub["step"] = int(st_saved["step"])
                 else:
                     if eng is not None and id(p) in eng.by_param and not eng.owns_whole(p):
                         continue

@@ -112,6 +112,7 @@ class GradEngine:
         self.tp_group = parallel.tp_group
         self.distributed = self.dp > 1 and dist.is_available() and dist.is_initialized()
         self.sync_grads = True
+        self.epoch = 0  # bumped whenever parameter values change (optimizer step, load)
         self._in_backward: set[str] = set()
         self.buckets: list[Bucket] = []
         self.by_param: dict[int, tuple[Bucket, Slot]] = {}
@@ -224,8 +225,11 @@ class GradEngine:
 
     def _install_hooks(self) -> None:
         for b in self.buckets:
+            hook = self._make_hook(b)
             for s in b.slots:
-                s.param.register_post_accumulate_grad_hook(self._make_hook(b))
+                s.param.register_post_accumulate_grad_hook(hook)
+                # kernels that accumulate a weight gradient directly into the bucket call this
+                s.param._mint_grad_ready = (lambda h=hook, prm=s.param: h(prm))
         self.zero_grad()
         if self.level == 3 and self.dp > 1:
             self._install_zero3_hooks()
@@ -342,6 +346,7 @@ class GradEngine:
 
     def after_step(self) -> None:
         """Propagate updated shards: all-gather params (levels 1/2); level 3 drops stale full copies."""
+        self.epoch += 1
         if not self.distributed or self.level == 0:
             return
         if self.level == 3:
@@ -357,19 +362,39 @@ class GradEngine:
             h.wait()
 
     # ------------------------------------------------------------------ grad norm
+    def _reduced_grad(self, b: Bucket) -> torch.Tensor | None:
+        """This rank's reduced gradient piece of bucket ``b`` (full, slice or reduce-scattered shard)."""
+        if self.level == 0 or self.dp == 1 or not self.distributed:
+            return b.grad
+        if self.level == 1:
+            lo = self.rank * b.shard
+            return b.grad[lo : lo + b.shard]
+        return b.grad_shard
+
     def grad_norm_sq(self) -> torch.Tensor:
-        """Squared global grad norm over dp x tp, each element counted once."""
-        dev = self.buckets[0].grad.device if self.buckets and self.buckets[0].grad is not None else (
-            self.buckets[0].shard_data.device if self.buckets else torch.device("cpu"))
-        total = torch.zeros((), dtype=torch.float32, device=dev)
+        """Squared global grad norm over dp x tp, each element counted once (fused per-bucket norms)."""
         tp = self.parallel.tp_size
+        pieces = []
         for b in self.buckets:
-            for s in b.slots:
-                replicated_over_tp = tp > 1 and not getattr(s.param, "_tp_sharded", False)
-                if replicated_over_tp and self.parallel.tp_rank != 0:
+            g = self._reduced_grad(b)
+            if g is None:
+                continue
+            sharded = [getattr(sl.param, "_tp_sharded", False) for sl in b.slots]
+            if tp > 1 and not all(sharded):
+                if any(sharded):  # mixed bucket: fall back to per-parameter pieces
+                    for sl in b.slots:
+                        if getattr(sl.param, "_tp_sharded", False) or self.parallel.tp_rank == 0:
+                            pieces.extend(gv for _pv, gv, _o, _n in self.segments(sl.param))
                     continue
-                for _pv, gv, _o, _n in self.segments(s.param):
-                    total += gv.float().pow(2).sum()
+                if self.parallel.tp_rank != 0:
+                    continue
+            pieces.append(g)
+        dev = self.buckets[0].shard_data.device if self.buckets else torch.device("cpu")
+        if pieces:
+            norms = torch._foreach_norm([t.float() if t.dtype != torch.float32 else t for t in pieces])
+            total = torch.stack(norms).square().sum()
+        else:
+            total = torch.zeros((), dtype=torch.float32, device=dev)
         if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
             if self.level == 0 or self.dp == 1:
                 # dp replicas hold identical full gradients: reduce over the TP group only
@@ -382,11 +407,9 @@ class GradEngine:
     def clip_grad_norm(self, max_norm: float) -> torch.Tensor:
         norm = self.grad_norm_sq().sqrt()
         coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
-        for b in self.buckets:
-            if self.level >= 2 and self.distributed:
-                b.grad_shard.mul_(coef)
-            elif b.grad is not None:
-                b.grad.mul_(coef)
+        grads = [g for g in (self._reduced_grad(b) for b in self.buckets) if g is not None]
+        if grads:
+            torch._foreach_mul_(grads, coef)
         return norm
 
     # ------------------------------------------------------------------ ZeRO-3 gather / free
@@ -510,6 +533,7 @@ class GradEngine:
         return full[s.start : s.start + s.numel].view(s.shape)
 
     def load_full_param(self, p: torch.Tensor, value: torch.Tensor) -> None:
+        self.epoch += 1
         b, s = self.by_param[id(p)]
         flat = value.reshape(-1).to(b.dtype)
         lo = self.rank * b.shard

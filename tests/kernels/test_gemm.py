@@ -78,3 +78,30 @@ def test_gemm_repeatable():
     x = matmul(a, b, trans_b=True, out_dtype=torch.float32)
     y = matmul(a, b, trans_b=True, out_dtype=torch.float32)
     assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("shape", [(768, 768, 65536), (2304, 768, 16384), (300, 200, 1000), (128, 256, 64)])
+def test_gemm_split_k_accumulate(shape):
+    """Weight-gradient shape: tiny output, huge contraction -> split-K with fp32 vector reductions."""
+    torch.manual_seed(5)
+    M, N, K = shape
+    a = torch.randn(K, M, device="cuda", dtype=torch.bfloat16)  # dy [tokens, out]
+    b = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)  # x  [tokens, in]
+    c = torch.randn(M, N, device="cuda", dtype=torch.float32)
+    c0 = c.clone()
+    matmul(a, b, trans_a=True, out=c, accumulate=True)
+    matmul(a, b, trans_a=True, out=c, accumulate=True)
+    exp = c0 + 2 * (a.float().t() @ b.float())
+    rel = ((c - exp).norm() / exp.norm()).item()
+    assert rel < 2e-3, rel
+
+
+def test_gemm_column_slice_operand():
+    """A strided column slice (fused-QKV weight-gradient rows) is a valid TMA operand."""
+    torch.manual_seed(6)
+    dy = torch.randn(4096, 2304, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(4096, 768, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(768, 768, device="cuda")
+    matmul(dy[:, 768:1536], x, trans_a=True, out=out, accumulate=True)
+    exp = dy[:, 768:1536].float().t() @ x.float()
+    assert ((out - exp).norm() / exp.norm()).item() < 2e-3
