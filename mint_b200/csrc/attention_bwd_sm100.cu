@@ -14,6 +14,11 @@
 // x 128 rows with 128B swizzle is the canonical layout for both. dQ is accumulated across key tiles
 // with 16-byte fp32 vector reductions into an fp32 buffer; a final pass converts it to bf16.
 // D_i = rowsum(dO_i * O_i) is computed by a preprocessing kernel. All waits are bounded.
+//
+// Pipelining: Q / dO stream through a 2-stage ring; P and dS share one shared-memory tile (dS is
+// written once dV has consumed P); dQ_i lands in the dP^T columns once dS is computed, so the MMA
+// issue order dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1} keeps the tensor pipe busy while the math warps
+// produce dS_i and drain dQ_i.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -42,12 +47,11 @@ struct BwdParams {
 struct Smem {
   uint8_t k[kTileBytes];
   uint8_t v[kTileBytes];
-  uint8_t q[kTileBytes];
-  uint8_t dout[kTileBytes];
-  uint8_t p[kTileBytes];
-  uint8_t ds[kTileBytes];
-  uint64_t kv_full, q_full, q_empty, do_full, do_empty;
-  uint64_t s_full, dp_full, p_ready, ds_ready, dq_full, dq_free, mma_done;
+  uint8_t q[2][kTileBytes];
+  uint8_t dout[2][kTileBytes];
+  uint8_t pds[kTileBytes];  // P^T, then dS^T of the same query tile
+  uint64_t kv_full, q_full[2], q_empty[2], do_full[2], do_empty[2];
+  uint64_t s_full, dp_full, p_ready, dv_done, ds_ready, dq_full, dq_free, mma_done;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -121,13 +125,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&s.kv_full, 1);
-    mbar_init(&s.q_full, 1);
-    mbar_init(&s.q_empty, 1);
-    mbar_init(&s.do_full, 1);
-    mbar_init(&s.do_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      mbar_init(&s.q_empty[i], 1);
+      mbar_init(&s.do_full[i], 1);
+      mbar_init(&s.do_empty[i], 1);
+    }
     mbar_init(&s.s_full, 1);
     mbar_init(&s.dp_full, 1);
     mbar_init(&s.p_ready, 4);
+    mbar_init(&s.dv_done, 1);
     mbar_init(&s.ds_ready, 4);
     mbar_init(&s.dq_full, 1);
     mbar_init(&s.dq_free, 4);
@@ -140,7 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
-  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
+  // dQ_i reuses the dP^T columns once dS_i has been computed from them
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
 
   if (warp == 0) {
     if (lane == 0 && n > 0) {
@@ -157,15 +165,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int it = 0; it < n; ++it) {
         const int h = hk * G + it / nq;
         const int qrow = b * p.T + (i0 + it % nq) * kB;
-        const uint32_t ph = it & 1;
-        if (!mbar_wait(&s.q_empty, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
-        mbar_arrive_expect_tx(&s.q_full, kTileBytes);
-        tma_load_3d(s.q, &tq, &s.q_full, 0, h, qrow);
-        tma_load_3d(s.q + kAtomBytes, &tq, &s.q_full, 64, h, qrow);
-        if (!mbar_wait(&s.do_empty, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
-        mbar_arrive_expect_tx(&s.do_full, kTileBytes);
-        tma_load_3d(s.dout, &tdo, &s.do_full, 0, h, qrow);
-        tma_load_3d(s.dout + kAtomBytes, &tdo, &s.do_full, 64, h, qrow);
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        if (!mbar_wait(&s.q_empty[st], ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.q_full[st], kTileBytes);
+        tma_load_3d(s.q[st], &tq, &s.q_full[st], 0, h, qrow);
+        tma_load_3d(s.q[st] + kAtomBytes, &tq, &s.q_full[st], 64, h, qrow);
+        if (!mbar_wait(&s.do_empty[st], ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.do_full[st], kTileBytes);
+        tma_load_3d(s.dout[st], &tdo, &s.do_full[st], 0, h, qrow);
+        tma_load_3d(s.dout[st] + kAtomBytes, &tdo, &s.do_full[st], 64, h, qrow);
       }
       if (*abort_flag) {
         const uint64_t t0 = globaltimer();
@@ -175,29 +184,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {
-      const uint32_t a_k = smem_u32(s.k), a_v = smem_u32(s.v), a_q = smem_u32(s.q), a_do = smem_u32(s.dout);
-      const uint32_t a_p = smem_u32(s.p), a_ds = smem_u32(s.ds);
-      bool ok = mbar_wait(&s.kv_full, 0, p.status, kStatusTimeoutAttention, abort_flag);
-      for (int it = 0; it < n && ok; ++it) {
-        const uint32_t ph = it & 1;
-        if (!(ok = mbar_wait(&s.q_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
-        if (!(ok = mbar_wait(&s.do_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
-        if (it > 0 && !(ok = mbar_wait(&s.dq_free, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      const uint32_t a_k = smem_u32(s.k), a_v = smem_u32(s.v), a_pds = smem_u32(s.pds);
+      bool ok = mbar_wait(&s.kv_full, 0, p.status, kStatusTimeoutAttention, abort_flag) &&
+                mbar_wait(&s.q_full[0], 0, p.status, kStatusTimeoutAttention, abort_flag) &&
+                mbar_wait(&s.do_full[0], 0, p.status, kStatusTimeoutAttention, abort_flag);
+      if (ok) {
         tc_fence_after();
-        mma_kk(t_s, a_k, a_q, false);    // S^T = K Q^T
+        mma_kk(t_s, a_k, smem_u32(s.q[0]), false);      // S^T_0 = K Q_0^T
         umma_commit(&s.s_full);
-        mma_kk(t_dp, a_v, a_do, false);  // dP^T = V dO^T
+        mma_kk(t_dp, a_v, smem_u32(s.dout[0]), false);  // dP^T_0 = V dO_0^T
         umma_commit(&s.dp_full);
+      }
+      for (int it = 0; it < n && ok; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = it & 1;
+        const uint32_t a_q = smem_u32(s.q[st]), a_do = smem_u32(s.dout[st]);
         if (!(ok = mbar_wait(&s.p_ready, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
         tc_fence_after();
-        mma_kmn(t_dv, a_p, a_do, it > 0);  // dV += P^T dO
+        mma_kmn(t_dv, a_pds, a_do, it > 0);  // dV += P^T dO
+        umma_commit(&s.dv_done);
+        const bool more = it + 1 < n;
+        if (more) {
+          const int sn = (it + 1) & 1;
+          const uint32_t pn = ((it + 1) >> 1) & 1;
+          if (!(ok = mbar_wait(&s.q_full[sn], pn, p.status, kStatusTimeoutAttention, abort_flag))) break;
+          tc_fence_after();
+          mma_kk(t_s, a_k, smem_u32(s.q[sn]), false);  // S^T_{i+1}: S_i was consumed before p_ready_i
+          umma_commit(&s.s_full);
+        }
         if (!(ok = mbar_wait(&s.ds_ready, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
         tc_fence_after();
-        mma_kmn(t_dk, a_ds, a_q, it > 0);  // dK += dS^T Q
-        mma_mnmn(t_s, a_ds, a_k, false);   // dQ_i = dS K
+        mma_kmn(t_dk, a_pds, a_q, it > 0);  // dK += dS^T Q
+        mma_mnmn(t_dq, a_pds, a_k, false);  // dQ_i = dS K (dP^T_i was consumed before ds_ready_i)
         umma_commit(&s.dq_full);
-        umma_commit(&s.q_empty);
-        umma_commit(&s.do_empty);
+        umma_commit(&s.q_empty[st]);
+        umma_commit(&s.do_empty[st]);
+        if (more) {
+          const int sn = (it + 1) & 1;
+          const uint32_t pn = ((it + 1) >> 1) & 1;
+          if (!(ok = mbar_wait(&s.do_full[sn], pn, p.status, kStatusTimeoutAttention, abort_flag))) break;
+          if (!(ok = mbar_wait(&s.dq_free, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+          tc_fence_after();
+          mma_kk(t_dp, a_v, smem_u32(s.dout[sn]), false);  // dP^T_{i+1}
+          umma_commit(&s.dp_full);
+        }
       }
       umma_commit(&s.mma_done);
       mbar_wait(&s.mma_done, 0, p.status, kStatusTimeoutAttention, nullptr);
@@ -234,7 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float l2 = keep ? lse_row[qi] * 1.4426950408889634f : 0.f;
         x[c] = keep ? exp2f(x[c] * p.scale_log2 - l2) : 0.f;
       }
-      store_row_sw128(s.p, r, x);
+      // the shared P/dS tile is free: dK_{i-1} / dQ_{i-1} (dq_full_{i-1}) finished reading dS_{i-1}
+      store_row_sw128(s.pds, r, x);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -254,7 +285,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           x[c] = x[c] * (__uint_as_float(u[e]) - dl);
         }
       }
-      store_row_sw128(s.ds, r, x);
+      // dS overwrites P only after dV has consumed it
+      if (!(ok = mbar_wait_warp(&s.dv_done, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      store_row_sw128(s.pds, r, x);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -263,11 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       // dQ rows: TMEM lane = query index within the tile
       const int qi = q0 + r;
-      float* dst = p.dq_acc + ((static_cast<long long>(b) * p.T + qi) * p.Hq + h) * kD;
+      float* dst = p.dq_acc + ((static_cast<long long>(b) * p.T + (qi < p.T ? qi : 0)) * p.Hq + h) * kD;
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t u[32];
-        tmem_ld_32x32b_x32(t_s + lane_off + c4 * 32, u);
+        tmem_ld_32x32b_x32(t_dq + lane_off + c4 * 32, u);
         tmem_ld_wait();
         if (qi < p.T) {
 #pragma unroll

@@ -29,8 +29,9 @@ struct Cfg {
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+  static constexpr int kBarrierBytes = 1024;
+  static constexpr int kStagingBytes = 4 * 2 * 4096;  // 4 epilogue warps x 2 buffers x (32 x 32 fp32)
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
 };
 
 struct Params {
@@ -71,7 +72,8 @@ __device__ __forceinline__ void work_item(const Params& p, int w, int kblocks, i
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                const __grid_constant__ CUtensorMap tmc, Params p) {
   using C_ = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* staging = smem + C_::kStages * C_::kStageBytes + C_::kBarrierBytes;  // 1024-aligned
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -201,12 +204,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(mma_done, 0, p.status, kStatusTimeoutMma, nullptr);
     }
   } else {
-    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4). Each 32x32 accumulator chunk is converted
+    // in registers, written to a swizzled shared-memory staging buffer (double-buffered per warp)
+    // and written out by one TMA store (or TMA reduce-add for accumulating GEMMs); TMA clips rows
+    // and columns outside C.
     const int q = warp & 3;
-    const int row_in_tile = q * 32 + lane;
+    uint8_t* bufs = staging + (warp - 2) * 2 * 4096;
     float alpha = p.alpha;
     if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
+    const bool f32_out = p.c_fp32 || p.atomic_out;
     int t = 0;
+    int seq = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
@@ -214,20 +222,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int tm, tn, kb0_, nkb_;
       work_item(p, tile, kblocks, tm, tn, kb0_, nkb_);
-      const int row = tm * BM + row_in_tile;
-      const bool row_ok = row < p.M;
+      const int row0 = tm * BM + q * 32;
+      const int row = row0 + lane;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
         tmem_ld_wait();
         const int col0 = tn * BN + c * 32;
-        if (!row_ok || col0 >= p.N) continue;
+        if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
-        const bool full_chunk = col0 + 32 <= p.N;
-        if (p.D != nullptr && p.beta != 0.0f) {
+        if (p.D != nullptr && p.beta != 0.0f && row < p.M) {
+          const bool full_chunk = col0 + 32 <= p.N;
           if (p.d_fp32) {
             const float* dp = static_cast<const float*>(p.D) + static_cast<long long>(row) * p.ldd + col0;
             if (full_chunk) {
@@ -262,43 +270,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (p.atomic_out) {
-          float* cp = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col0;
-          if (full_chunk) {
+        uint8_t* buf = bufs + (seq & 1) * 4096;
+        // the TMA store issued two chunks ago read this buffer: wait for it (keep one in flight)
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        if (f32_out) {
+          // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row `lane` at j ^ (lane % 8)
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) red_add_v4(cp + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; ++j) atomicAdd(cp + j, v[j]);
-          }
-        } else if (p.c_fp32) {
-          float* cp = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col0;
-          if (full_chunk) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(cp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; ++j) cp[j] = v[j];
+          for (int j = 0; j < 8; ++j) {
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           }
         } else {
-          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col0;
-          if (full_chunk) {
+          // 32 rows x 64 B, 64B swizzle: 16-byte chunk j of row `lane` at j ^ ((lane / 2) % 4)
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 u;
-              u.x = pack_bf16x2(v[j], v[j + 1]);
-              u.y = pack_bf16x2(v[j + 2], v[j + 3]);
-              u.z = pack_bf16x2(v[j + 4], v[j + 5]);
-              u.w = pack_bf16x2(v[j + 6], v[j + 7]);
-              *reinterpret_cast<uint4*>(cp + j) = u;
-            }
-          } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; ++j) cp[j] = __float2bfloat16_rn(v[j]);
+          for (int j = 0; j < 4; ++j) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
           }
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (p.atomic_out) {
+            tma_reduce_add_2d(&tmc, buf, col0, row0);
+          } else {
+            tma_store_2d(&tmc, buf, col0, row0);
+          }
+          bulk_commit();
+        }
+        ++seq;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -310,7 +322,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, bool A_MN, bool B_MN>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int sms, cudaStream_t stream) {
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, int sms,
+            cudaStream_t stream) {
   using C_ = Cfg<BN>;
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
   static bool configured = false;
@@ -320,7 +333,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int s
   }
   const int tiles = p.tiles_m * p.tiles_n * p.splits;
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, tc, p);
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
@@ -413,12 +426,16 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c1
                                   : make_tmap_2d_bf16(A.data_ptr(), K, M, lda, 64, 64, true);
   const CUtensorMap tb = b_kmajor ? make_tmap_2d_bf16(B.data_ptr(), N, K, ldb, BN, 64, true)
                                   : make_tmap_2d_bf16(B.data_ptr(), K, N, ldb, 64, 64, true);
+  const bool f32c = p.c_fp32 != 0;
+  const CUtensorMap tcm = make_tmap_2d(C.data_ptr(), f32c ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                       f32c ? 4 : 2, M, N, C.stride(0), 32, 32,
+                                       f32c ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   const bool a_mn = !a_kmajor, b_mn = !b_kmajor;
-#define MINT_GEMM_DISPATCH(BNV)                                                  \
-  if (!a_mn && !b_mn) gemm::launch<BNV, false, false>(ta, tb, p, sms, stream);   \
-  else if (!a_mn && b_mn) gemm::launch<BNV, false, true>(ta, tb, p, sms, stream); \
-  else if (a_mn && !b_mn) gemm::launch<BNV, true, false>(ta, tb, p, sms, stream); \
-  else gemm::launch<BNV, true, true>(ta, tb, p, sms, stream);
+#define MINT_GEMM_DISPATCH(BNV)                                                       \
+  if (!a_mn && !b_mn) gemm::launch<BNV, false, false>(ta, tb, tcm, p, sms, stream);   \
+  else if (!a_mn && b_mn) gemm::launch<BNV, false, true>(ta, tb, tcm, p, sms, stream); \
+  else if (a_mn && !b_mn) gemm::launch<BNV, true, false>(ta, tb, tcm, p, sms, stream); \
+  else gemm::launch<BNV, true, true>(ta, tb, tcm, p, sms, stream);
   if (BN == 256) {
     MINT_GEMM_DISPATCH(256)
   } else {

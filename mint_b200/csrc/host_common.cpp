@@ -82,6 +82,22 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t cols, ui
   return map;
 }
 
+CUtensorMap make_tmap_2d(const void* base, int dtype, int esize, uint64_t rows, uint64_t cols, uint64_t ld,
+                         uint32_t box_rows, uint32_t box_cols, int swizzle) {
+  MINT_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  MINT_CHECK((ld * esize) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * esize};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, static_cast<CUtensorMapDataType>(dtype), 2, const_cast<void*>(base), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, static_cast<CUtensorMapSwizzle>(swizzle),
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MINT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store map) failed (", static_cast<int>(r), ")");
+  return map;
+}
+
 CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                               uint64_t stride2, uint32_t box0, uint32_t box1, uint32_t box2, bool swizzle128) {
   MINT_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
