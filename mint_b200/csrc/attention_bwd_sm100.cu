@@ -21,6 +21,7 @@
 // produce dS_i and drain dQ_i.
 #include "common.cuh"
 #include "host_common.h"
+#include "attention_bwd_raw.h"
 
 namespace mint {
 namespace fab {
@@ -459,6 +460,54 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
   return {dq, dk, dv};
+}
+
+// Raw-pointer launch of the same three backward kernels (delta, main, dQ cast) for callers that
+// own every buffer themselves; used by the allocation-free entry point in
+// flash_attn_bwd_noalloc.cu. `dq_acc` must hold zeros when the first kernel runs.
+void flash_attn_bwd_launch_raw(const FlashBwdRaw& a, cudaStream_t stream) {
+  const long long rows = static_cast<long long>(a.B) * a.T * a.Hq;
+  fab::fa_bwd_delta_kernel<<<static_cast<int>((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(a.dout), static_cast<const __nv_bfloat16*>(a.o), a.delta, a.B, a.T, a.Hq);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  fab::BwdParams p{};
+  p.dq_acc = a.dq_acc;
+  p.dk = static_cast<__nv_bfloat16*>(a.dk);
+  p.dv = static_cast<__nv_bfloat16*>(a.dv);
+  p.lse = a.lse;
+  p.delta = a.delta;
+  p.doc = a.doc;
+  p.B = a.B;
+  p.T = a.T;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.causal = a.causal ? 1 : 0;
+  p.window = a.window;
+  p.scale = a.scale;
+  p.scale_log2 = static_cast<float>(static_cast<double>(a.scale) * 1.4426950408889634);
+  p.status = a.status;
+  const uint64_t bt = static_cast<uint64_t>(a.B) * a.T;
+  auto map = [&](const void* base, int H) {
+    return make_tmap_3d_bf16(base, fab::kD, H, bt, fab::kD, static_cast<uint64_t>(H) * fab::kD, 64, 1, 128, true);
+  };
+  const CUtensorMap tq = map(a.q, a.Hq), tk = map(a.k, a.Hkv), tv = map(a.v, a.Hkv), tdo = map(a.dout, a.Hq);
+  dim3 grid((a.T + fab::kB - 1) / fab::kB, a.Hkv, a.B);
+  fab::fa_bwd_kernel<<<grid, fab::kThreads, flash_attn_bwd_smem_bytes(), stream>>>(tq, tk, tv, tdo, p);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  const long long n4 = rows * fab::kD / 4;
+  fab::fa_cast_kernel<<<static_cast<int>(std::min<long long>((n4 + 255) / 256, 148LL * 16)), 256, 0, stream>>>(
+      a.dq_acc, static_cast<__nv_bfloat16*>(a.dq), n4);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+int flash_attn_bwd_smem_bytes() { return static_cast<int>(sizeof(fab::Smem)) + 1024; }
+
+void flash_attn_bwd_configure_current_device() {
+  MINT_CUDA_CHECK(cudaFuncSetAttribute(fab::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       flash_attn_bwd_smem_bytes()));
 }
 
 }  // namespace mint
