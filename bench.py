@@ -5,6 +5,9 @@ Config (config 2): Gemma-style d12 decoder -- 12 layers, d_model 
 (MHA), GeGLU ffn 3072, RoPE theta 10000, tied embeddings, vocab 65,536 -- seq 2048, micro-batch 32
 per dp rank, next-token CE on uniform-random token ids (random-init weights), NorMuon (Polar
 Express, 5 iterations) on block matrices and AdamW elsewhere, bf16 autocast, grad clip 1.0.
+Every row holds two documents of seq/2 tokens (doc ids 0 and 1), the input the reference's own
+benchmark worker gives its model (scripts/benchmark.py:258-263), so attention is causal within each
+document on both arms.
 Layouts: 1 GPU single; 2 GPUs tp=2 sp; 4 GPUs tp=2 sp ZeRO-2 dp=2; 8 GPUs tp=2 sp ZeRO-2 dp=4.
 
     python bench.py [--gpus 1] [--steps K] [--warmup W]
@@ -37,6 +40,7 @@ sys.path.insert(0, str(ROOT))
 
 BASELINE_TOKS = None  # BASELINE.md publishes no number for this config
 METRIC = "pretrain tokens/sec (device-timed, max over ranks)"
+DOCS_PER_ROW = 2
 
 MODELS = {
     "d12": dict(embed_dim=768, hidden_dim=3072, seq_length=2048, vocab_size=65536, n_layers=12, n_heads=6,
@@ -185,9 +189,9 @@ def build_ours(args, cfg: dict, lay: dict):  # noqa: ANN001, ANN201
     opt = configure_optimizer(model, mcfg, SchedulerConfig(), MuonAdamWConfig(matrix_optimizer=args.matrix_optimizer),
                               dp_group=device.parallel.dp_group)
 
-    def step(x, y, m):  # noqa: ANN001, ANN202
+    def step(x, y, m, doc):  # noqa: ANN001, ANN202
         with device.autocast():
-            loss = model.loss(x, y, m)
+            loss = model.loss(x, y, m, doc_ids=doc)
         device.backward(loss)
         device.optimizer_step(opt, grad_clip=1.0, params=None)
         opt.zero_grad()
@@ -220,9 +224,9 @@ def build_reference(args, cfg: dict, lay: dict):  # noqa: ANN001, ANN201
     opt = configure_optimizer(model, mcfg, SchedulerConfig(), MuonAdamWConfig(), dp_group=device.parallel.dp_group)
     loss_fn = torch.compile(_masked_cross_entropy)
 
-    def step(x, y, m):  # noqa: ANN001, ANN202
+    def step(x, y, m, doc):  # noqa: ANN001, ANN202
         with device.autocast():
-            logits = model(x)
+            logits = model(x, doc_ids=doc)
             loss = loss_fn(logits, y, m, None)
         device.backward(loss)
         device.optimizer_step(opt, grad_clip=1.0, params=model.parameters())
@@ -266,6 +270,10 @@ def main() -> None:
                             "micro_batch_per_dp_rank": mb,
                             "optimizer": ("NorMuon(matrices)+AdamW" if args.impl == "ours" and args.matrix_optimizer == "muon"
                                           else "AdamW (all groups; reference configure_optimizer)"),
+                            "docs_per_row": DOCS_PER_ROW,
+                            "tokens_per_gpu_per_step": mb * T * dp // args.gpus,
+                            "attention_mask": "causal + same-document (2 docs per row, as the reference benchmark worker); "
+                                              "even layers also a seq/4 sliding window",
                             "l2": "per-step working set >> 126 MB L2 (logits alone 8.6 GB); no flush needed"}}
     if args.impl == "reference":
         base_line["impl"] = "reference"
@@ -284,10 +292,12 @@ def main() -> None:
         pinned.append((row[:, :-1].contiguous().pin_memory(), row[:, 1:].contiguous().pin_memory()))
     dev_batches = [(x.cuda(), y.cuda()) for x, y in pinned]
     mask = torch.ones(mb, T, device="cuda", dtype=torch.float32)
+    # two documents per row, as the reference's benchmark worker feeds its model (scripts/benchmark.py:258-263)
+    doc = (torch.arange(T, device="cuda") // (T // DOCS_PER_ROW)).to(torch.int32).expand(mb, -1).contiguous()
 
     for i in range(args.warmup):
         x, y = dev_batches[i % 2]
-        loss = step(x, y, mask)
+        loss = step(x, y, mask, doc)
     torch.cuda.synchronize()
     barrier()
 
@@ -308,14 +318,14 @@ def main() -> None:
     start.record()
     for i in range(args.steps):
         x, y = dev_batches[i % 2]
-        loss = step(x, y, mask)
+        loss = step(x, y, mask, doc)
     end.record()
     torch.cuda.synchronize()
     clocks = sampler.stop()
     launches = (ext.launch_count() - launches0) if ext is not None else 0
     ms = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms)
-    last_loss = float(loss)
+    last_loss = float(loss.detach())
 
     e2e = None
     if not args.no_e2e:
@@ -329,7 +339,7 @@ def main() -> None:
             hx, hy = pinned[i % 2]
             xin.copy_(hx, non_blocking=True)
             yin.copy_(hy, non_blocking=True)
-            loss = step(xin, yin, mask)
+            loss = step(xin, yin, mask, doc)
             _ = loss.item()
         e2_.record()
         torch.cuda.synchronize()

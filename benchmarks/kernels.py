@@ -1,0 +1,191 @@
+#!/usr/bin/env python
+"""Kernel microbenchmarks: the framework's sm_100a kernels against the PyTorch library path
+(cuBLAS for GEMMs, torch SDPA -- flash / cuDNN backends -- for attention) on one GPU.
+
+    python benchmarks/kernels.py attn --B 8 --T 4096 --hq 16 --hkv 4          # GQA fwd + bwd
+    python benchmarks/kernels.py attn --B 4 --T 2048 --hq 6 --hkv 6 --docs 2  # packed documents
+    python benchmarks/kernels.py gemm --M 65536 --N 2304 --K 768              # y = x W^T
+    python benchmarks/kernels.py gemm --M 768 --N 2304 --K 65536 --layout wgrad
+    python benchmarks/kernels.py gemm --M 768 --N 3072 --K 768 --batch 24     # batched (Polar Express)
+    python benchmarks/kernels.py attn ... --once   # one untimed call per kernel (for ncu captures)
+
+Timing: CUDA events on the launching stream, after warm-up, a synchronize on both sides, median
+of ``--iters`` runs; before each run a 256 MB buffer is rewritten so no run starts with the
+previous run's operands in L2. Attention FLOPs count only the unmasked work
+(``4 * B * Hq * D * kept_pairs`` forward, 2.5x that backward), so causal / window / document
+masks do not inflate the rate.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import statistics
+import sys
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F  # noqa: N812
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+from mint_b200.ops import _ext  # noqa: E402
+from mint_b200.ops.gemm import matmul  # noqa: E402
+
+_FLUSH: torch.Tensor | None = None
+
+
+def flush_l2() -> None:
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    _FLUSH.fill_(1.0)
+
+
+def time_fn(fn, iters: int, warmup: int = 3) -> float:  # noqa: ANN001
+    """Median milliseconds of ``fn()`` over ``iters`` runs, L2 flushed before each."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush_l2()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+def kept_pairs(T: int, causal: bool, window: int, docs: int) -> int:
+    """Number of (query, key) pairs the mask keeps, per batch row and head."""
+    seg = T // docs
+    total = 0
+    for d in range(docs):
+        n = seg if d < docs - 1 else T - seg * (docs - 1)
+        for i in range(n):
+            lo = max(0, i - window) if window >= 0 else 0
+            hi = i if causal else n - 1
+            total += hi - lo + 1
+    return total
+
+
+def run_attn(a: argparse.Namespace) -> dict:
+    C = _ext.require()
+    torch.manual_seed(0)
+    B, T, Hq, Hkv, D = a.B, a.T, a.hq, a.hkv, 128
+    q = torch.randn(B, T, Hq, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, T, Hkv, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, T, Hkv, D, device="cuda", dtype=torch.bfloat16)
+    do = torch.randn_like(q)
+    doc = bounds = None
+    if a.docs > 1:
+        doc = (torch.arange(T, device="cuda") // (T // a.docs)).clamp_max(a.docs - 1).int().expand(B, -1).contiguous()
+        bounds = C.doc_bounds(doc) if hasattr(C, "doc_bounds") else None
+    scale = 1.0 / math.sqrt(D)
+    causal = not a.no_causal
+    extra = (bounds,) if bounds is not None else ()
+    o, lse = C.flash_attn_fwd(q, k, v, doc, causal, a.window, scale, *extra)
+    if a.once:
+        C.flash_attn_bwd(do, q, k, v, o, lse, doc, causal, a.window, scale, *extra)
+        torch.cuda.synchronize()
+        return {"once": True}
+    pairs = kept_pairs(T, causal, a.window, a.docs)
+    fwd_flop = 4.0 * B * Hq * D * pairs
+    res = {"B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "causal": causal, "window": a.window, "docs": a.docs}
+    t_fwd = time_fn(lambda: C.flash_attn_fwd(q, k, v, doc, causal, a.window, scale, *extra), a.iters)
+    t_bwd = time_fn(lambda: C.flash_attn_bwd(do, q, k, v, o, lse, doc, causal, a.window, scale, *extra), a.iters)
+    res.update(ours_fwd_ms=t_fwd, ours_bwd_ms=t_bwd, ours_fwd_tflops=fwd_flop / t_fwd / 1e9,
+               ours_bwd_tflops=2.5 * fwd_flop / t_bwd / 1e9)
+    if a.window < 0 and a.docs == 1:
+        # library reference: torch SDPA (flash / cuDNN backends pick themselves), GQA native
+        qt, kt, vt = (t.transpose(1, 2).detach().requires_grad_() for t in (q, k, v))
+        gqa = Hq != Hkv
+
+        def sdpa_fwd():  # noqa: ANN202
+            return F.scaled_dot_product_attention(qt, kt, vt, is_causal=causal, enable_gqa=gqa)
+
+        ot = sdpa_fwd()
+        dot = do.transpose(1, 2)
+        t_sf = time_fn(sdpa_fwd, a.iters)
+        t_sb = time_fn(lambda: torch.autograd.grad(ot, (qt, kt, vt), dot, retain_graph=True), a.iters)
+        res.update(sdpa_fwd_ms=t_sf, sdpa_bwd_ms=t_sb, sdpa_fwd_tflops=fwd_flop / t_sf / 1e9,
+                   sdpa_bwd_tflops=2.5 * fwd_flop / t_sb / 1e9)
+    return res
+
+
+def run_gemm(a: argparse.Namespace) -> dict:
+    _ext.require()
+    torch.manual_seed(0)
+    M, N, K, nb = a.M, a.N, a.K, a.batch
+    lead = (nb,) if nb > 1 else ()
+    if a.layout == "fwd":  # y[M,N] = x[M,K] @ W[N,K]^T
+        x = torch.randn(*lead, M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(*lead, N, K, device="cuda", dtype=torch.bfloat16)
+
+        def ours():  # noqa: ANN202
+            return matmul(x, w, trans_b=True, out_dtype=torch.bfloat16)
+
+        def lib():  # noqa: ANN202
+            return x @ w.mT
+    elif a.layout == "dgrad":  # dx[M,N] = dy[M,K] @ W[K,N]
+        x = torch.randn(*lead, M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(*lead, K, N, device="cuda", dtype=torch.bfloat16)
+
+        def ours():  # noqa: ANN202
+            return matmul(x, w, out_dtype=torch.bfloat16)
+
+        def lib():  # noqa: ANN202
+            return x @ w
+    else:  # wgrad: dW[M,N] (fp32, accumulated) += dy[K,M]^T @ x[K,N]
+        dy = torch.randn(*lead, K, M, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(*lead, K, N, device="cuda", dtype=torch.bfloat16)
+        out = torch.zeros(*lead, M, N, device="cuda", dtype=torch.float32)
+
+        def ours():  # noqa: ANN202
+            return matmul(dy, x, trans_a=True, out=out, accumulate=True)
+
+        def lib():  # noqa: ANN202  (cuBLAS bf16 GEMM of the same shape, fp32 accumulation inside)
+            return dy.mT @ x
+    if a.once:
+        ours()
+        torch.cuda.synchronize()
+        return {"once": True}
+    flop = 2.0 * M * N * K * nb
+    t_o = time_fn(ours, a.iters)
+    t_l = time_fn(lib, a.iters)
+    return {"M": M, "N": N, "K": K, "batch": nb, "layout": a.layout, "ours_ms": t_o, "cublas_ms": t_l,
+            "ours_tflops": flop / t_o / 1e9, "cublas_tflops": flop / t_l / 1e9}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    at = sub.add_parser("attn")
+    at.add_argument("--B", type=int, default=4)
+    at.add_argument("--T", type=int, default=2048)
+    at.add_argument("--hq", type=int, default=6)
+    at.add_argument("--hkv", type=int, default=6)
+    at.add_argument("--window", type=int, default=-1)
+    at.add_argument("--docs", type=int, default=1)
+    at.add_argument("--no-causal", action="store_true")
+    gm = sub.add_parser("gemm")
+    gm.add_argument("--M", type=int, default=65536)
+    gm.add_argument("--N", type=int, default=2304)
+    gm.add_argument("--K", type=int, default=768)
+    gm.add_argument("--batch", type=int, default=1)
+    gm.add_argument("--layout", choices=["fwd", "dgrad", "wgrad"], default="fwd")
+    for p in (at, gm):
+        p.add_argument("--iters", type=int, default=10)
+        p.add_argument("--once", action="store_true")
+    a = ap.parse_args()
+    res = run_attn(a) if a.cmd == "attn" else run_gemm(a)
+    _ext.check_device_status()
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -24,11 +24,15 @@
 #include "attention_bwd_raw.h"
 
 namespace mint {
+
+const int2* doc_bounds_ptr(const c10::optional<at::Tensor>& doc, const c10::optional<at::Tensor>& dbounds,
+                           int64_t B, int64_t T, at::Tensor& holder);
+
 namespace fab {
 
 constexpr int kB = 128;  // rows per tile (keys or queries)
 constexpr int kD = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warps 4..11 math (2 per TMEM lane quadrant)
 constexpr int kTileBytes = kB * kD * 2;
 constexpr int kAtomBytes = kTileBytes / 2;
 
@@ -39,6 +43,7 @@ struct BwdParams {
   const float* lse;       // [B, Hq, T] natural log
   const float* delta;     // [B, Hq, T]
   const int* doc;         // [B, T] or null
+  const int2* dbounds;    // [B, T] document run [start, end) per token; start < 0: row not sorted
   int B, T, Hq, Hkv;
   int causal, window;
   float scale, scale_log2;
@@ -51,8 +56,11 @@ struct Smem {
   uint8_t q[2][kTileBytes];
   uint8_t dout[2][kTileBytes];
   uint8_t pds[kTileBytes];  // P^T, then dS^T of the same query tile
+  float lse2[2][kB];        // log2-scaled LSE of the current query tile (double-buffered)
+  float dlt[2][kB];         // delta of the current query tile
   uint64_t kv_full, q_full[2], q_empty[2], do_full[2], do_empty[2];
   uint64_t s_full, dp_full, p_ready, dv_done, ds_ready, dq_full, dq_free, mma_done;
+  uint64_t stg_full;  // the 8 math warps staged this tile's LSE / delta
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -82,23 +90,20 @@ __device__ __forceinline__ void mma_mnmn(uint32_t d, uint32_t a, uint32_t b, boo
   for (int k = 0; k < 8; ++k) umma_bf16(d, mnmaj(a, k), mnmaj(b, k), idesc, (acc || k > 0) ? 1u : 0u);
 }
 
-// row r of a K-major 128B-swizzled bf16 tile from 128 fp32 values
-__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int r, const float (&x)[128]) {
+// 64 columns (one swizzle atom `a`) of row r of a K-major 128B-swizzled bf16 tile from fp32 values
+__device__ __forceinline__ void store_half_row_sw128(uint8_t* tile, int a, int r, const float (&x)[64]) {
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int e = a * 64 + c * 8;
-      uint4 v4 = make_uint4(pack_bf16x2(x[e], x[e + 1]), pack_bf16x2(x[e + 2], x[e + 3]),
-                            pack_bf16x2(x[e + 4], x[e + 5]), pack_bf16x2(x[e + 6], x[e + 7]));
-      *reinterpret_cast<uint4*>(tile + a * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
-    }
+  for (int c = 0; c < 8; ++c) {
+    const int e = c * 8;
+    uint4 v4 = make_uint4(pack_bf16x2(x[e], x[e + 1]), pack_bf16x2(x[e + 2], x[e + 3]),
+                          pack_bf16x2(x[e + 4], x[e + 5]), pack_bf16x2(x[e + 6], x[e + 7]));
+    *reinterpret_cast<uint4*>(tile + a * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
   }
 }
 
-__device__ __forceinline__ void load_row128(uint32_t taddr, float (&x)[128]) {
+__device__ __forceinline__ void load_row64(uint32_t taddr, float (&x)[64]) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t u[32];
     tmem_ld_32x32b_x32(taddr + c * 32, u);
     tmem_ld_wait();
@@ -117,9 +122,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int G = p.Hq / p.Hkv;
   const int k0 = kt * kB;
   const int ntq = (p.T + kB - 1) / kB;
-  const int i0 = p.causal ? k0 / kB : 0;
+  const int2* db = p.dbounds != nullptr ? p.dbounds + static_cast<long long>(b) * p.T : nullptr;
+  const int k_last = min(p.T, k0 + kB) - 1;
+  int i0 = p.causal ? k0 / kB : 0;
   int i1 = ntq;
   if (p.window >= 0) i1 = min(ntq, (k0 + kB - 1 + p.window) / kB + 1);
+  // doc_sorted: document masks come from the [start, end) bounds; else (ids given without bounds,
+  // or an unsorted row) ids are compared per element and no tile is skipped for documents
+  const bool doc_sorted = db != nullptr && db[k0].x >= 0;
+  if (doc_sorted) {
+    // queries outside the documents of this key tile never attend to it
+    i0 = max(i0, db[k0].x / kB);
+    i1 = min(i1, (db[k_last].y + kB - 1) / kB);
+  }
   const int nq = max(0, i1 - i0);
   const int n = G * nq;
   volatile int* abort_flag = &s.abort_flag;
@@ -134,11 +149,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&s.s_full, 1);
     mbar_init(&s.dp_full, 1);
-    mbar_init(&s.p_ready, 4);
+    mbar_init(&s.p_ready, 8);
     mbar_init(&s.dv_done, 1);
-    mbar_init(&s.ds_ready, 4);
+    mbar_init(&s.ds_ready, 8);
     mbar_init(&s.dq_full, 1);
-    mbar_init(&s.dq_free, 4);
+    mbar_init(&s.dq_free, 8);
+    mbar_init(&s.stg_full, 8);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -234,39 +250,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&s.mma_done, 0, p.status, kStatusTimeoutAttention, nullptr);
     }
   } else if (warp >= 4) {
+    // warp 4 + 4h + q: TMEM lane quadrant q (rows q*32 .. q*32+31), columns [64h, 64h + 64)
     const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int cb = half * 64;
     const int r = q * 32 + lane;
+    const int mt = (warp - 4) * 32 + lane;  // 0..255 over the math warps
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int kj = k0 + r;
     const int doc_k = (p.doc != nullptr && kj < p.T) ? p.doc[static_cast<long long>(b) * p.T + kj] : 0;
+    const int2 dk = (doc_sorted && kj < p.T) ? db[kj] : make_int2(0, p.T);
     bool ok = n > 0;
     for (int it = 0; it < n && ok; ++it) {
       const uint32_t ph = it & 1;
       const int h = hk * G + it / nq;
       const int q0 = (i0 + it % nq) * kB;
-      const float* lse_row = p.lse + (static_cast<long long>(b) * p.Hq + h) * p.T;
-      const float* dl_row = p.delta + (static_cast<long long>(b) * p.Hq + h) * p.T;
+      const int q_last = min(p.T, q0 + kB) - 1;
+      // stage this query tile's LSE (log2 units) and delta; the buffer was last read two tiles ago,
+      // before every math warp arrived on the previous tile's staging barrier
+      {
+        const int c = mt & (kB - 1);
+        const int qi = q0 + c;
+        const long long rowbase = (static_cast<long long>(b) * p.Hq + h) * p.T;
+        if (mt < kB) {
+          s.lse2[it & 1][c] = qi < p.T ? p.lse[rowbase + qi] * 1.4426950408889634f : INFINITY;
+        } else {
+          s.dlt[it & 1][c] = qi < p.T ? p.delta[rowbase + qi] : 0.f;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.stg_full);
+      if (!(ok = mbar_wait_warp(&s.stg_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      const float* lse2 = s.lse2[it & 1] + cb;
+      const float* dlt = s.dlt[it & 1] + cb;
       if (!(ok = mbar_wait_warp(&s.s_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       tc_fence_after();
-      float x[128];
-      load_row128(t_s + lane_off, x);
+      float x[64];
+      load_row64(t_s + lane_off + cb, x);
+      const int lo_i = min(k0, q0), hi_i = max(k_last, q_last);
+      const bool doc_mask = p.doc != nullptr && !(doc_sorted && db[lo_i].y > hi_i);
       const bool need_mask = (p.causal && k0 + kB - 1 > q0) || (p.window >= 0 && q0 + kB - 1 - k0 > p.window) ||
-                             q0 + kB > p.T || k0 + kB > p.T || p.doc != nullptr;
+                             q0 + kB > p.T || k0 + kB > p.T || doc_mask;
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const int qi = q0 + c;
-        bool keep = true;
-        if (need_mask) {
-          keep = qi < p.T && kj < p.T;
+        for (int c = 0; c < 64; ++c) {
+          const int qi = q0 + cb + c;
+          bool keep = qi < p.T && kj < p.T && qi >= dk.x && qi < dk.y;
           if (p.causal) keep = keep && kj <= qi;
           if (p.window >= 0) keep = keep && qi - kj <= p.window;
-          if (p.doc != nullptr && keep) keep = p.doc[static_cast<long long>(b) * p.T + qi] == doc_k;
+          if (p.doc != nullptr && !doc_sorted && keep) keep = p.doc[static_cast<long long>(b) * p.T + qi] == doc_k;
+          x[c] = keep ? exp2f(x[c] * p.scale_log2 - lse2[c]) : 0.f;
         }
-        const float l2 = keep ? lse_row[qi] * 1.4426950408889634f : 0.f;
-        x[c] = keep ? exp2f(x[c] * p.scale_log2 - l2) : 0.f;
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) x[c] = exp2f(x[c] * p.scale_log2 - lse2[c]);
       }
       // the shared P/dS tile is free: dK_{i-1} / dQ_{i-1} (dq_full_{i-1}) finished reading dS_{i-1}
-      store_row_sw128(s.pds, r, x);
+      store_half_row_sw128(s.pds, half, r, x);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -274,39 +314,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait_warp(&s.dp_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       tc_fence_after();
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t u[32];
-        tmem_ld_32x32b_x32(t_dp + lane_off + c4 * 32, u);
+        tmem_ld_32x32b_x32(t_dp + lane_off + cb + c2 * 32, u);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const int c = c4 * 32 + e;
-          const int qi = q0 + c;
-          const float dl = qi < p.T ? dl_row[qi] : 0.f;
-          x[c] = x[c] * (__uint_as_float(u[e]) - dl);
+          const int c = c2 * 32 + e;
+          x[c] = x[c] * (__uint_as_float(u[e]) - dlt[c]);
         }
       }
       // dS overwrites P only after dV has consumed it
       if (!(ok = mbar_wait_warp(&s.dv_done, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
-      store_row_sw128(s.pds, r, x);
+      store_half_row_sw128(s.pds, half, r, x);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.ds_ready);
       if (!(ok = mbar_wait_warp(&s.dq_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       tc_fence_after();
-      // dQ rows: TMEM lane = query index within the tile
+      // dQ rows: TMEM lane = query index within the tile; this warp drains 64 of the 128 head dims
       const int qi = q0 + r;
-      float* dst = p.dq_acc + ((static_cast<long long>(b) * p.T + (qi < p.T ? qi : 0)) * p.Hq + h) * kD;
+      float* dst = p.dq_acc + ((static_cast<long long>(b) * p.T + (qi < p.T ? qi : 0)) * p.Hq + h) * kD + cb;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t u[32];
-        tmem_ld_32x32b_x32(t_dq + lane_off + c4 * 32, u);
+        tmem_ld_32x32b_x32(t_dq + lane_off + cb + c2 * 32, u);
         tmem_ld_wait();
         if (qi < p.T) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
-            red_add_v4(dst + c4 * 32 + e, __uint_as_float(u[e]) * p.scale, __uint_as_float(u[e + 1]) * p.scale,
+            red_add_v4(dst + c2 * 32 + e, __uint_as_float(u[e]) * p.scale, __uint_as_float(u[e + 1]) * p.scale,
                        __uint_as_float(u[e + 2]) * p.scale, __uint_as_float(u[e + 3]) * p.scale);
           }
         }
@@ -318,15 +356,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // dK / dV rows: TMEM lane = key index (tcgen05.ld is warp-collective: every lane loads)
     ok = __all_sync(0xffffffffu, ok);
     const bool key_ok = kj < p.T;
-    __nv_bfloat16* dkr = p.dk + ((static_cast<long long>(b) * p.T + (key_ok ? kj : 0)) * p.Hkv + hk) * kD;
-    __nv_bfloat16* dvr = p.dv + ((static_cast<long long>(b) * p.T + (key_ok ? kj : 0)) * p.Hkv + hk) * kD;
+    __nv_bfloat16* dkr = p.dk + ((static_cast<long long>(b) * p.T + (key_ok ? kj : 0)) * p.Hkv + hk) * kD + cb;
+    __nv_bfloat16* dvr = p.dv + ((static_cast<long long>(b) * p.T + (key_ok ? kj : 0)) * p.Hkv + hk) * kD + cb;
     if (ok && n > 0) {
       tc_fence_after();
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t uk[32], uv[32];
-        tmem_ld_32x32b_x32(t_dk + lane_off + c4 * 32, uk);
-        tmem_ld_32x32b_x32(t_dv + lane_off + c4 * 32, uv);
+        tmem_ld_32x32b_x32(t_dk + lane_off + cb + c2 * 32, uk);
+        tmem_ld_32x32b_x32(t_dv + lane_off + cb + c2 * 32, uv);
         tmem_ld_wait();
         if (!key_ok) continue;
 #pragma unroll
@@ -340,12 +378,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           v.y = pack_bf16x2(__uint_as_float(uv[e + 2]), __uint_as_float(uv[e + 3]));
           v.z = pack_bf16x2(__uint_as_float(uv[e + 4]), __uint_as_float(uv[e + 5]));
           v.w = pack_bf16x2(__uint_as_float(uv[e + 6]), __uint_as_float(uv[e + 7]));
-          *reinterpret_cast<uint4*>(dkr + c4 * 32 + e) = a;
-          *reinterpret_cast<uint4*>(dvr + c4 * 32 + e) = v;
+          *reinterpret_cast<uint4*>(dkr + c2 * 32 + e) = a;
+          *reinterpret_cast<uint4*>(dvr + c2 * 32 + e) = v;
         }
       }
     } else if (n == 0 && key_ok) {
-      for (int c = 0; c < kD; ++c) {
+      for (int c = 0; c < 64; ++c) {
         dkr[c] = __float2bfloat16_rn(0.f);
         dvr[c] = __float2bfloat16_rn(0.f);
       }
@@ -398,7 +436,7 @@ __global__ void fa_cast_kernel(const float* __restrict__ src, __nv_bfloat16* __r
 std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
-                                       double scale) {
+                                       double scale, const c10::optional<at::Tensor>& dbounds) {
   const at::Tensor* inputs[5] = {&dout, &q, &k, &v, &o};
   for (const at::Tensor* t : inputs) {
     check_contig(*t, "flash_attn_bwd input");
@@ -429,7 +467,13 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   p.lse = lse.data_ptr<float>();
   p.delta = delta.data_ptr<float>();
-  if (doc.has_value() && doc->defined()) p.doc = doc->data_ptr<int>();
+  at::Tensor bounds_holder;
+  if (doc.has_value() && doc->defined()) {
+    check_contig(*doc, "doc_ids");
+    MINT_CHECK(doc->scalar_type() == at::kInt && doc->numel() == static_cast<int64_t>(B) * T, "doc_ids must be int32 [B, T]");
+    p.doc = doc->data_ptr<int>();
+    p.dbounds = doc_bounds_ptr(doc, dbounds, B, T, bounds_holder);
+  }
   p.B = B;
   p.T = T;
   p.Hq = Hq;

@@ -30,6 +30,7 @@ struct FwdParams {
   __nv_bfloat16* o;       // [B, T, Hq, D]
   float* lse;             // [B, Hq, T]
   const int* doc;         // [B, T] or null
+  const int2* dbounds;    // [B, T] document run [start, end) of each token; start < 0: row not sorted
   int B, T, Hq, Hkv;
   int causal, window;     // window < 0: none
   float scale_log2;       // softmax scale * log2(e)
@@ -52,12 +53,21 @@ struct Smem {
   int abort_flag;
 };
 
-__device__ __forceinline__ void kv_range(int q0, int T, int causal, int window, int& j0, int& j1) {
+// Key tiles a query tile visits. With sorted document ids, keys before the document of the tile's
+// first query and (non-causal) after the document of its last query are skipped.
+__device__ __forceinline__ void kv_range(int q0, int T, int causal, int window, const int2* db, int& j0, int& j1) {
   const int q_last = min(T, q0 + kBM) - 1;
-  const int hi = causal ? q_last + 1 : T;
-  const int lo = window >= 0 ? max(0, q0 - window) : 0;
+  int hi = causal ? q_last + 1 : T;
+  int lo = window >= 0 ? max(0, q0 - window) : 0;
+  if (db != nullptr) {
+    const int2 f = db[q0], l = db[q_last];
+    if (f.x >= 0) {
+      lo = max(lo, f.x);
+      hi = min(hi, l.y);
+    }
+  }
   j0 = lo / kBN;
-  j1 = (hi + kBN - 1) / kBN;
+  j1 = max(j0, (hi + kBN - 1) / kBN);
 }
 
 // S = Q K^T: both operands K-major (head dim contiguous), 2 swizzle atoms along K.
@@ -93,8 +103,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hkv);
   const int q0 = qt * kBM;
+  const int2* db = p.dbounds != nullptr ? p.dbounds + static_cast<long long>(b) * p.T : nullptr;
   int j0, j1;
-  kv_range(q0, p.T, p.causal, p.window, j0, j1);
+  kv_range(q0, p.T, p.causal, p.window, db, j0, j1);
   const int n = j1 - j0;
   volatile int* abort_flag = &s.abort_flag;
 
@@ -184,6 +195,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qi = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int doc_q = (p.doc != nullptr && qi < p.T) ? p.doc[static_cast<long long>(b) * p.T + qi] : 0;
+    // doc_sorted: document masks come from the bounds; else ids (if given) are compared per element
+    const bool doc_sorted = db != nullptr && db[q0].x >= 0;
+    const int2 dq = (doc_sorted && qi < p.T) ? db[qi] : make_int2(0, p.T);
+    const int d_lo = dq.x, d_hi = dq.y;
+    // the tile's keys lie inside every row's document when the last row's document starts before
+    // the first key and the first row's document ends after the last key
+    const int2 dfirst = doc_sorted ? db[q0] : make_int2(0, p.T);
+    const int2 dlast = doc_sorted ? db[min(p.T, q0 + kBM) - 1] : make_int2(0, p.T);
     float m = -INFINITY, l = 0.f;
     bool ok = n > 0;
     int pv_waited = -1;  // index of the last PV whose completion this thread observed
@@ -203,17 +222,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
       }
+      const bool doc_mask = p.doc != nullptr && !(doc_sorted && dlast.x <= kb && dfirst.y >= kb + kBN);
       const bool need_mask = (p.causal && kb + kBN - 1 > q0) || (p.window >= 0 && q0 + kBM - 1 - kb > p.window) ||
-                             kb + kBN > p.T || p.doc != nullptr;
+                             kb + kBN > p.T || doc_mask;
       if (need_mask) {
+        if (doc_sorted || p.doc == nullptr) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const int kj = kb + c;
-          bool keep = kj < p.T;
-          if (p.causal) keep = keep && kj <= qi;
-          if (p.window >= 0) keep = keep && qi - kj <= p.window;
-          if (p.doc != nullptr && keep) keep = p.doc[static_cast<long long>(b) * p.T + kj] == doc_q;
-          if (!keep) x[c] = -INFINITY;
+          for (int c = 0; c < 128; ++c) {
+            const int kj = kb + c;
+            bool keep = kj < p.T && kj >= d_lo && kj < d_hi;
+            if (p.causal) keep = keep && kj <= qi;
+            if (p.window >= 0) keep = keep && qi - kj <= p.window;
+            if (!keep) x[c] = -INFINITY;
+          }
+        } else {
+          for (int c = 0; c < 128; ++c) {
+            const int kj = kb + c;
+            bool keep = kj < p.T;
+            if (p.causal) keep = keep && kj <= qi;
+            if (p.window >= 0) keep = keep && qi - kj <= p.window;
+            if (keep) keep = p.doc[static_cast<long long>(b) * p.T + kj] == doc_q;
+            if (!keep) x[c] = -INFINITY;
+          }
         }
       }
       float mt = -INFINITY;
@@ -329,11 +359,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Document run of every token for attention's tile skipping: with the row's ids non-decreasing,
+// token t's document is [lower_bound(doc[t]), upper_bound(doc[t])) of the row (binary searches).
+// Rows whose ids ever decrease get start = end = -1 (kernels then compare ids and skip nothing).
+__global__ void __launch_bounds__(256) doc_bounds_kernel(const int* __restrict__ doc, int2* __restrict__ out, int T) {
+  const int b = blockIdx.x;
+  const int* row = doc + static_cast<long long>(b) * T;
+  int unsorted = 0;
+  for (int t = threadIdx.x + 1; t < T; t += blockDim.x) unsorted |= row[t] < row[t - 1];
+  unsorted = __syncthreads_or(unsorted);
+  int2* o = out + static_cast<long long>(b) * T;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    if (unsorted) {
+      o[t] = make_int2(-1, -1);
+      continue;
+    }
+    const int v = row[t];
+    int lo = 0, hi = t;  // first index with row[i] >= v lies in [0, t]
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (row[mid] < v) lo = mid + 1; else hi = mid;
+    }
+    int lo2 = t + 1, hi2 = T;  // first index with row[i] > v lies in [t + 1, T]
+    while (lo2 < hi2) {
+      const int mid = (lo2 + hi2) >> 1;
+      if (row[mid] <= v) lo2 = mid + 1; else hi2 = mid;
+    }
+    o[t] = make_int2(lo, lo2);
+  }
+}
+
 }  // namespace fa
+
+at::Tensor doc_bounds(const at::Tensor& doc) {
+  check_contig(doc, "doc_ids");
+  MINT_CHECK(doc.scalar_type() == at::kInt && doc.dim() == 2, "doc_ids must be int32 [B, T]");
+  const int B = static_cast<int>(doc.size(0)), T = static_cast<int>(doc.size(1));
+  auto out = at::empty({B, T, 2}, doc.options());
+  if (B == 0 || T == 0) return out;
+  c10::cuda::CUDAGuard guard(doc.device());
+  fa::doc_bounds_kernel<<<B, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      doc.data_ptr<int>(), reinterpret_cast<int2*>(out.data_ptr<int>()), T);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return out;
+}
+
+const int2* doc_bounds_ptr(const c10::optional<at::Tensor>& doc, const c10::optional<at::Tensor>& dbounds,
+                           int64_t B, int64_t T, at::Tensor& holder) {
+  if (!doc.has_value() || !doc->defined()) return nullptr;
+  if (dbounds.has_value() && dbounds->defined()) {
+    check_contig(*dbounds, "doc bounds");
+    MINT_CHECK(dbounds->scalar_type() == at::kInt && dbounds->numel() == 2 * B * T, "doc bounds must be int32 [B, T, 2]");
+    holder = *dbounds;
+  } else {
+    holder = doc_bounds(doc->view({B, T}));
+  }
+  return reinterpret_cast<const int2*>(holder.data_ptr<int>());
+}
 
 std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
-                                       double scale) {
+                                       double scale, const c10::optional<at::Tensor>& dbounds) {
   check_contig(q, "q");
   check_contig(k, "k");
   check_contig(v, "v");
@@ -357,6 +444,8 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k,
     MINT_CHECK(doc->scalar_type() == at::kInt && doc->numel() == static_cast<int64_t>(B) * T, "doc_ids must be int32 [B, T]");
     p.doc = doc->data_ptr<int>();
   }
+  at::Tensor bounds_holder;
+  p.dbounds = doc_bounds_ptr(doc, dbounds, B, T, bounds_holder);
   p.B = B;
   p.T = T;
   p.Hq = Hq;

@@ -38,11 +38,12 @@ void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v
                 double eps, double wd, int64_t step);
 std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
-                                       double scale);
+                                       double scale, const c10::optional<at::Tensor>& dbounds);
 std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
-                                       double scale);
+                                       double scale, const c10::optional<at::Tensor>& dbounds);
+at::Tensor doc_bounds(const at::Tensor& doc);
 }  // namespace mint
 
 static int64_t read_status(bool reset) {
@@ -73,6 +74,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_row_stats", &mint::ce_row_stats);
   m.def("ce_grad_inplace", &mint::ce_grad_inplace);
   m.def("adamw_step", &mint::adamw_step);
-  m.def("flash_attn_fwd", &mint::flash_attn_fwd, "tcgen05 FlashAttention forward -> (o, lse)");
-  m.def("flash_attn_bwd", &mint::flash_attn_bwd, "tcgen05 FlashAttention backward -> (dq, dk, dv)");
+  m.def("flash_attn_fwd", &mint::flash_attn_fwd, "tcgen05 FlashAttention forward -> (o, lse)", py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("doc"), py::arg("causal"), py::arg("window"), py::arg("scale"),
+        py::arg("dbounds") = py::none());
+  m.def("flash_attn_bwd", &mint::flash_attn_bwd, "tcgen05 FlashAttention backward -> (dq, dk, dv)",
+        py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("doc"),
+        py::arg("causal"), py::arg("window"), py::arg("scale"), py::arg("dbounds") = py::none());
+  m.def("doc_bounds", &mint::doc_bounds, "[B, T, 2] int32 document run [start, end) of every token");
 }

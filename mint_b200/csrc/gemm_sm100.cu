@@ -46,6 +46,8 @@ struct Params {
   int splits;      // split-K factor: work item = (tile, split)
   int kbps;        // k-blocks per split
   int atomic_out;  // C (fp32) += alpha * acc with 16-byte vector reductions
+  int batch;       // independent GEMMs sharing shapes (operands / C addressed as 3-D TMA maps)
+  long long sd;    // batch stride of D in elements
   uint32_t* status;
 };
 
@@ -60,9 +62,13 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   tn = r / gsize;
 }
 
-// work item -> (tile m, tile n, first k-block, k-block count)
-__device__ __forceinline__ void work_item(const Params& p, int w, int kblocks, int& tm, int& tn, int& kb0, int& nkb) {
+// work item -> (batch, tile m, tile n, first k-block, k-block count)
+__device__ __forceinline__ void work_item(const Params& p, int w, int kblocks, int& bi, int& tm, int& tn, int& kb0,
+                                          int& nkb) {
   const int tiles = p.tiles_m * p.tiles_n;
+  const int per_batch = tiles * p.splits;
+  bi = w / per_batch;
+  w -= bi * per_batch;
   const int tile = w % tiles;
   const int split = w / tiles;
   tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
@@ -110,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_tiles = p.tiles_m * p.tiles_n * p.splits;
+  const int num_tiles = p.tiles_m * p.tiles_n * p.splits * p.batch;
   const int kblocks = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
@@ -121,8 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int tm, tn, kb0, nkb;
-        work_item(p, tile, kblocks, tm, tn, kb0, nkb);
+        int bi, tm, tn, kb0, nkb;
+        work_item(p, tile, kblocks, bi, tm, tn, kb0, nkb);
         const int m0 = tm * BM, n0 = tn * BN;
         for (int kb = kb0; kb < kb0 + nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer, abort_flag)) {
@@ -134,16 +140,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* b_dst = sB + stage * C_::kBBytes;
           const int k0 = kb * BK;
           if constexpr (!A_MN) {
-            tma_load_2d(a_dst, &tma, &full[stage], k0, m0);
+            tma_load_3d(a_dst, &tma, &full[stage], k0, m0, bi);
           } else {
 #pragma unroll
-            for (int i = 0; i < BM / 64; ++i) tma_load_2d(a_dst + i * 8192, &tma, &full[stage], m0 + i * 64, k0);
+            for (int i = 0; i < BM / 64; ++i) tma_load_3d(a_dst + i * 8192, &tma, &full[stage], m0 + i * 64, k0, bi);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(b_dst, &tmb, &full[stage], k0, n0);
+            tma_load_3d(b_dst, &tmb, &full[stage], k0, n0, bi);
           } else {
 #pragma unroll
-            for (int i = 0; i < BN / 64; ++i) tma_load_2d(b_dst + i * 8192, &tmb, &full[stage], n0 + i * 64, k0);
+            for (int i = 0; i < BN / 64; ++i) tma_load_3d(b_dst + i * 8192, &tmb, &full[stage], n0 + i * 64, k0, bi);
           }
           if (++stage == C_::kStages) {
             stage = 0;
@@ -171,8 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, kStatusTimeoutMma, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        int tm_, tn_, kb0, nkb;
-        work_item(p, tile, kblocks, tm_, tn_, kb0, nkb);
+        int bi_, tm_, tn_, kb0, nkb;
+        work_item(p, tile, kblocks, bi_, tm_, tn_, kb0, nkb);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma, abort_flag)) {
             ok = false;
@@ -220,8 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc_phase = (t >> 1) & 1;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
-      int tm, tn, kb0_, nkb_;
-      work_item(p, tile, kblocks, tm, tn, kb0_, nkb_);
+      int bi, tm, tn, kb0_, nkb_;
+      work_item(p, tile, kblocks, bi, tm, tn, kb0_, nkb_);
       const int row0 = tm * BM + q * 32;
       const int row = row0 + lane;
 #pragma unroll 1
@@ -237,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.D != nullptr && p.beta != 0.0f && row < p.M) {
           const bool full_chunk = col0 + 32 <= p.N;
           if (p.d_fp32) {
-            const float* dp = static_cast<const float*>(p.D) + static_cast<long long>(row) * p.ldd + col0;
+            const float* dp = static_cast<const float*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
             if (full_chunk) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
@@ -252,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             const __nv_bfloat16* dp =
-                static_cast<const __nv_bfloat16*>(p.D) + static_cast<long long>(row) * p.ldd + col0;
+                static_cast<const __nv_bfloat16*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
             if (full_chunk) {
 #pragma unroll
               for (int j = 0; j < 32; j += 8) {
@@ -297,9 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           if (p.atomic_out) {
-            tma_reduce_add_2d(&tmc, buf, col0, row0);
+            tma_reduce_add_3d(&tmc, buf, col0, row0, bi);
           } else {
-            tma_store_2d(&tmc, buf, col0, row0);
+            tma_store_3d(&tmc, buf, col0, row0, bi);
           }
           bulk_commit();
         }
@@ -331,8 +337,8 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
     MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes));
     configured = true;
   }
-  const int tiles = p.tiles_m * p.tiles_n * p.splits;
-  const int grid = tiles < sms ? tiles : sms;
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * p.splits * p.batch;
+  const int grid = tiles < sms ? static_cast<int>(tiles) : sms;
   kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, tc, p);
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
@@ -341,26 +347,36 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
 }  // namespace gemm
 
 // C = alpha * op(A) @ op(B) + beta * D.  a_kmajor: A stored [M,K]; else [K,M].  b_kmajor: B stored [N,K]; else [K,N].
-// accumulate = true: C (fp32) += alpha * op(A) @ op(B) through vector reductions; the contraction is
-// split across CTAs (split-K) when the output alone has too few tiles to fill the GPU.
-void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& D,
+// Operands are 2-D, or 3-D [batch, rows, cols] for `batch` independent GEMMs of one shape (every
+// 3-D operand needs unit inner stride; the batch stride is free). accumulate = true: C (fp32) +=
+// alpha * op(A) @ op(B) through TMA reduce-adds; the contraction is split across CTAs (split-K) when
+// the output alone has too few tiles to fill the GPU.
+void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const c10::optional<at::Tensor>& D_,
                bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t,
                bool accumulate) {
-  check_cuda(A, "A");
-  check_cuda(B, "B");
-  check_cuda(C, "C");
-  MINT_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm expects 2-D tensors");
+  check_cuda(A_, "A");
+  check_cuda(B_, "B");
+  check_cuda(C_, "C");
+  MINT_CHECK(A_.dim() == B_.dim() && A_.dim() == C_.dim() && (A_.dim() == 2 || A_.dim() == 3),
+             "gemm expects 2-D operands or 3-D batched operands");
+  const bool batched = A_.dim() == 3;
+  const at::Tensor A = batched ? A_ : A_.unsqueeze(0);
+  const at::Tensor B = batched ? B_ : B_.unsqueeze(0);
+  at::Tensor C = batched ? C_ : C_.unsqueeze(0);
+  const int64_t nb = A.size(0);
+  MINT_CHECK(B.size(0) == nb && C.size(0) == nb, "gemm batch sizes differ");
   MINT_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
-  MINT_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm operands need unit inner stride");
+  MINT_CHECK(A.stride(2) == 1 && B.stride(2) == 1 && C.stride(2) == 1, "gemm operands need unit inner stride");
   MINT_CHECK(C.scalar_type() == at::kBFloat16 || C.scalar_type() == at::kFloat, "C must be bf16 or fp32");
-  const int64_t M = a_kmajor ? A.size(0) : A.size(1);
-  const int64_t K = a_kmajor ? A.size(1) : A.size(0);
-  const int64_t N = b_kmajor ? B.size(0) : B.size(1);
-  const int64_t KB = b_kmajor ? B.size(1) : B.size(0);
+  const int64_t M = a_kmajor ? A.size(1) : A.size(2);
+  const int64_t K = a_kmajor ? A.size(2) : A.size(1);
+  const int64_t N = b_kmajor ? B.size(1) : B.size(2);
+  const int64_t KB = b_kmajor ? B.size(2) : B.size(1);
   MINT_CHECK(K == KB, "gemm K mismatch ", K, " vs ", KB);
-  MINT_CHECK(C.size(0) == M && C.size(1) == N, "C has shape ", C.sizes(), ", expected [", M, ", ", N, "]");
-  MINT_CHECK(C.stride(0) % (C.scalar_type() == at::kFloat ? 4 : 8) == 0, "C row stride must be 16-byte aligned");
-  MINT_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm dims too large");
+  MINT_CHECK(C.size(1) == M && C.size(2) == N, "C has shape ", C_.sizes(), ", expected [", M, ", ", N, "]");
+  const int cal = C.scalar_type() == at::kFloat ? 4 : 8;
+  MINT_CHECK(C.stride(1) % cal == 0 && (nb == 1 || C.stride(0) % cal == 0), "C strides must be 16-byte aligned");
+  MINT_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31) && nb < 65536, "gemm dims too large");
   c10::cuda::CUDAGuard guard(A.device());
   const int dev = A.get_device();
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -370,37 +386,41 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c1
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
-  p.ldc = C.stride(0);
+  p.ldc = C.stride(1);
   p.alpha = static_cast<float>(alpha);
   p.beta = static_cast<float>(beta);
   p.c_fp32 = C.scalar_type() == at::kFloat;
+  p.batch = static_cast<int>(nb);
   p.status = status_ptr(dev);
-  if (D.has_value() && D->defined() && beta != 0.0) {
-    check_cuda(*D, "D");
-    MINT_CHECK(D->dim() == 2 && D->size(0) == M && D->size(1) == N && D->stride(1) == 1, "D must match C");
-    MINT_CHECK(D->scalar_type() == at::kFloat || D->scalar_type() == at::kBFloat16, "D must be bf16 or fp32");
-    MINT_CHECK(D->stride(0) % (D->scalar_type() == at::kFloat ? 4 : 8) == 0, "D row stride must be 16-byte aligned");
-    p.D = D->data_ptr();
-    p.ldd = D->stride(0);
-    p.d_fp32 = D->scalar_type() == at::kFloat;
+  if (D_.has_value() && D_->defined() && beta != 0.0) {
+    const at::Tensor D = batched ? *D_ : D_->unsqueeze(0);
+    check_cuda(D, "D");
+    MINT_CHECK(D.dim() == 3 && D.size(0) == nb && D.size(1) == M && D.size(2) == N && D.stride(2) == 1,
+               "D must match C");
+    MINT_CHECK(D.scalar_type() == at::kFloat || D.scalar_type() == at::kBFloat16, "D must be bf16 or fp32");
+    MINT_CHECK(D.stride(1) % (D.scalar_type() == at::kFloat ? 4 : 8) == 0, "D row stride must be 16-byte aligned");
+    p.D = D.data_ptr();
+    p.ldd = D.stride(1);
+    p.sd = D.stride(0);
+    p.d_fp32 = D.scalar_type() == at::kFloat;
   }
   if (alpha_t.has_value() && alpha_t->defined()) {
     MINT_CHECK(alpha_t->scalar_type() == at::kFloat && alpha_t->numel() == 1 && alpha_t->is_cuda(),
                "alpha tensor must be a 1-element fp32 CUDA tensor");
     p.alpha_ptr = alpha_t->data_ptr<float>();
   }
-  if (M == 0 || N == 0) return;
+  if (M == 0 || N == 0 || nb == 0) return;
   if (K == 0) {
     // empty contraction: C = beta * D
     if (p.D != nullptr) {
-      C.copy_(D->to(C.scalar_type()).mul(beta));
-    } else {
-      C.zero_();
+      C_.copy_(D_->to(C_.scalar_type()).mul(beta));
+    } else if (!accumulate) {
+      C_.zero_();
     }
     return;
   }
   const int sms = num_sms(dev);
-  const int64_t tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
+  const int64_t tiles256 = nb * ((M + 127) / 128) * ((N + 255) / 256);
   const bool use256 = N > 128 && tiles256 >= sms;
   const int BN = use256 ? 256 : 128;
   p.tiles_m = static_cast<int>((M + 127) / 128);
@@ -412,24 +432,31 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c1
     MINT_CHECK(p.c_fp32, "accumulating GEMM needs an fp32 C");
     MINT_CHECK(p.D == nullptr, "accumulating GEMM adds into C; D is not used");
     p.atomic_out = 1;
-    const int tiles = p.tiles_m * p.tiles_n;
+    const int64_t tiles = nb * p.tiles_m * p.tiles_n;
     if (tiles < sms && kblocks >= 8) {
       // enough (tile, split) work items for ~2 waves, each split with >= 4 k-blocks
-      int splits = std::min((2 * sms + tiles - 1) / tiles, kblocks / 4);
+      int splits = static_cast<int>(std::min<int64_t>((2 * sms + tiles - 1) / tiles, kblocks / 4));
       splits = std::max(splits, 1);
       p.kbps = (kblocks + splits - 1) / splits;
       p.splits = (kblocks + p.kbps - 1) / p.kbps;
     }
   }
-  const int64_t lda = A.stride(0), ldb = B.stride(0);
-  const CUtensorMap ta = a_kmajor ? make_tmap_2d_bf16(A.data_ptr(), M, K, lda, 128, 64, true)
-                                  : make_tmap_2d_bf16(A.data_ptr(), K, M, lda, 64, 64, true);
-  const CUtensorMap tb = b_kmajor ? make_tmap_2d_bf16(B.data_ptr(), N, K, ldb, BN, 64, true)
-                                  : make_tmap_2d_bf16(B.data_ptr(), K, N, ldb, 64, 64, true);
+  MINT_CHECK(static_cast<int64_t>(p.tiles_m) * p.tiles_n * p.splits * nb < (1ll << 31), "too many GEMM tiles");
+  // 3-D maps {inner, outer, batch}; for a single GEMM the batch stride only has to be 16-byte aligned
+  auto bstride = [&](const at::Tensor& t) -> uint64_t {
+    return nb > 1 ? static_cast<uint64_t>(t.stride(0)) : static_cast<uint64_t>(t.size(1) * t.stride(1));
+  };
+  const uint64_t lda = A.stride(1), ldb = B.stride(1);
+  constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMap ta = a_kmajor ? make_tmap_3d(A.data_ptr(), BF, 2, K, M, nb, lda, bstride(A), 64, 128, 1, SW128)
+                                  : make_tmap_3d(A.data_ptr(), BF, 2, M, K, nb, lda, bstride(A), 64, 64, 1, SW128);
+  const CUtensorMap tb = b_kmajor ? make_tmap_3d(B.data_ptr(), BF, 2, K, N, nb, ldb, bstride(B), 64, BN, 1, SW128)
+                                  : make_tmap_3d(B.data_ptr(), BF, 2, N, K, nb, ldb, bstride(B), 64, 64, 1, SW128);
   const bool f32c = p.c_fp32 != 0;
-  const CUtensorMap tcm = make_tmap_2d(C.data_ptr(), f32c ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                                       f32c ? 4 : 2, M, N, C.stride(0), 32, 32,
-                                       f32c ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  const CUtensorMap tcm =
+      make_tmap_3d(C.data_ptr(), f32c ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : BF, f32c ? 4 : 2, N, M, nb, C.stride(1),
+                   bstride(C), 32, 32, 1, f32c ? SW128 : CU_TENSOR_MAP_SWIZZLE_64B);
   const bool a_mn = !a_kmajor, b_mn = !b_kmajor;
 #define MINT_GEMM_DISPATCH(BNV)                                                       \
   if (!a_mn && !b_mn) gemm::launch<BNV, false, false>(ta, tb, tcm, p, sms, stream);   \

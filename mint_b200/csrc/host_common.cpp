@@ -115,4 +115,21 @@ CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64
   return map;
 }
 
+CUtensorMap make_tmap_3d(const void* base, int dtype, int esize, uint64_t d0, uint64_t d1, uint64_t d2,
+                         uint64_t stride1, uint64_t stride2, uint32_t box0, uint32_t box1, uint32_t box2, int swizzle) {
+  MINT_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  MINT_CHECK((stride1 * esize) % 16 == 0 && (stride2 * esize) % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1 * esize, stride2 * esize};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&map, static_cast<CUtensorMapDataType>(dtype), 3, const_cast<void*>(base), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, static_cast<CUtensorMapSwizzle>(swizzle),
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MINT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3d) failed (", static_cast<int>(r), ") dims=", d0, "x", d1,
+             "x", d2);
+  return map;
+}
+
 }  // namespace mint

@@ -39,6 +39,10 @@ CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64
 CUtensorMap make_tmap_2d(const void* base, int dtype, int esize, uint64_t rows, uint64_t cols, uint64_t ld,
                          uint32_t box_rows, uint32_t box_cols, int swizzle);
 
+// 3-D tensor map of any dtype: dims (innermost first) {d0, d1, d2}, strides in elements for d1, d2.
+CUtensorMap make_tmap_3d(const void* base, int dtype, int esize, uint64_t d0, uint64_t d1, uint64_t d2,
+                         uint64_t stride1, uint64_t stride2, uint32_t box0, uint32_t box1, uint32_t box2, int swizzle);
+
 int num_sms(int device);
 
 // Number of kernels launched by this extension since process start (bench.py's gpu_launches).

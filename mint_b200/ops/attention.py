@@ -12,6 +12,7 @@ arbitrary boolean masks and ALiBi biases use the reference path.
 from __future__ import annotations
 
 import math
+import weakref
 
 import torch
 import torch.nn.functional as F  # noqa: N812
@@ -73,22 +74,42 @@ def attention_reference(
     return out.transpose(1, 2)
 
 
+_DOC_CACHE: dict = {}
+
+
+def _doc_inputs(doc_ids: torch.Tensor | None) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+    """int32 document ids and their per-token ``[start, end)`` runs, computed once per ids tensor
+    (every layer, forward and backward, shares them). The kernels skip key / query tiles outside
+    each tile's documents when a row's ids are sorted."""
+    if doc_ids is None:
+        return None, None
+    key = (id(doc_ids), doc_ids._version, doc_ids.data_ptr(), tuple(doc_ids.shape))
+    hit = _DOC_CACHE.get("entry")
+    if hit is not None and hit[0] == key and hit[1]() is doc_ids:
+        return hit[2], hit[3]
+    d = doc_ids.to(torch.int32).contiguous()
+    bounds = _ext.require().doc_bounds(d.view(d.shape[0], -1))
+    _DOC_CACHE["entry"] = (key, weakref.ref(doc_ids), d, bounds)
+    return d, bounds
+
+
 class _FlashAttnFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, causal, window_left, doc_ids, scale):  # noqa: ANN001, ANN205
+    def forward(ctx, q, k, v, causal, window_left, doc_ids, scale, bounds):  # noqa: ANN001, ANN205
         C = _ext.require()
-        o, lse = C.flash_attn_fwd(q, k, v, doc_ids, bool(causal), int(window_left), float(scale))
-        ctx.save_for_backward(q, k, v, o, lse, doc_ids)
+        o, lse = C.flash_attn_fwd(q, k, v, doc_ids, bool(causal), int(window_left), float(scale), bounds)
+        ctx.save_for_backward(q, k, v, o, lse, doc_ids, bounds)
         ctx.meta = (bool(causal), int(window_left), float(scale))
         return o
 
     @staticmethod
     def backward(ctx, do):  # noqa: ANN001, ANN205
         C = _ext.require()
-        q, k, v, o, lse, doc_ids = ctx.saved_tensors
+        q, k, v, o, lse, doc_ids, bounds = ctx.saved_tensors
         causal, window_left, scale = ctx.meta
-        dq, dk, dv = C.flash_attn_bwd(do.contiguous(), q, k, v, o, lse, doc_ids, causal, window_left, scale)
-        return dq, dk, dv, None, None, None, None
+        dq, dk, dv = C.flash_attn_bwd(do.contiguous(), q, k, v, o, lse, doc_ids, causal, window_left, scale,
+                                      bounds)
+        return dq, dk, dv, None, None, None, None, None
 
 
 def _kernel_supported(q: torch.Tensor, k: torch.Tensor) -> bool:
@@ -122,8 +143,9 @@ def attention(
         and bias is None
         and _kernel_supported(q, k)
     ):
-        d = None if doc_ids is None else doc_ids.to(torch.int32).contiguous()
-        return _FlashAttnFn.apply(q.contiguous(), k.contiguous(), v.contiguous(), causal, window_left, d, scale)
+        d, bounds = _doc_inputs(doc_ids)
+        return _FlashAttnFn.apply(q.contiguous(), k.contiguous(), v.contiguous(), causal, window_left, d, scale,
+                                  bounds)
     return attention_reference(
         q, k, v, causal=causal, window_left=window_left, doc_ids=doc_ids, attn_mask=attn_mask,
         bias=bias, scale=scale,

@@ -23,7 +23,7 @@ import torch
 import torch.distributed as dist
 from torch.optim import Optimizer
 
-from mint_b200.optim.functional import POLAR_EXPRESS_COEFFS, adamw_update, normuon_update
+from mint_b200.optim.functional import POLAR_EXPRESS_COEFFS, adamw_update, normuon_update_batched
 from mint_b200.optim.muon_adamw import AdamConfig, MuonAdamWConfig, MuonConfig
 
 
@@ -44,6 +44,8 @@ class DistMuonAdamW(Optimizer):
                     break
         # per-unit state, keyed by (param id, piece offset)
         self._shard_state: dict[int, dict[str, Any]] = {}
+        # stacked NorMuon state per (group, shape, dtype, tp split) of the matrices this rank updates
+        self._muon_stacks: dict[tuple, dict[str, Any]] = {}
 
     @property
     def engine(self):  # noqa: ANN201
@@ -134,8 +136,10 @@ class DistMuonAdamW(Optimizer):
                 adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
                              group["eps"], group["weight_decay"])
 
-    def _step_muon(self, group: dict) -> None:
+    def _muon_units(self, group: dict) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+        """(param, this rank's whole matrix view, its gradient view) for every matrix this rank updates."""
         eng = self._engine
+        units = []
         for p in group["params"]:
             if len(getattr(p, "_orig_shape", p.shape)) != 2:
                 raise ValueError("NorMuon groups must hold 2-D matrices")
@@ -145,20 +149,50 @@ class DistMuonAdamW(Optimizer):
                 (pv, gv, off, n), = eng.segments(p)
                 assert off == 0 and n == p.numel(), "owner buckets hold whole matrices"
                 _b, slot = eng.slot(p)
-                pm, gm = pv.view(slot.shape), gv.view(slot.shape)
+                units.append((p, pv.view(slot.shape), gv.view(slot.shape)))
             else:
                 if p.grad is None:
                     continue
-                pm, gm = p.data, p.grad
-            st = self.state[p]
+                units.append((p, p.data, p.grad))
+        return units
+
+    def _muon_stack_state(self, key: tuple, members: list[torch.Tensor], shape: torch.Size, device) -> dict:  # noqa: ANN001
+        """Stacked NorMuon state of one shape group; every parameter's state holds views into it."""
+        st = self._muon_stacks.get(key)
+        if st is not None and st["params"] == [id(p) for p in members]:
+            return st
+        rows, cols = self._full_shape(members[0], shape)
+        sshape = (rows, 1) if rows >= cols else (1, cols)
+        n = len(members)
+        mb = torch.zeros((n, *shape), dtype=torch.float32, device=device)
+        smb = torch.zeros((n, *sshape), dtype=torch.float32, device=device)
+        for i, p in enumerate(members):
+            old = self.state.get(p, {})
+            if "momentum_buffer" in old:  # e.g. loaded from a checkpoint: move into the stack
+                mb[i].copy_(old["momentum_buffer"].reshape(shape))
+                smb[i].copy_(old["second_momentum_buffer"].reshape(sshape))
+            self.state[p]["momentum_buffer"] = mb[i]
+            self.state[p]["second_momentum_buffer"] = smb[i]
+        st = {"params": [id(p) for p in members], "mb": mb, "smb": smb}
+        self._muon_stacks[key] = st
+        return st
+
+    def _step_muon(self, group: dict) -> None:
+        """NorMuon on every matrix this rank owns, batched by (shape, tensor-parallel split): one
+        Nesterov / Polar-Express / rescale / update sequence per shape group instead of per matrix."""
+        by_key: dict[tuple, list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]] = {}
+        for p, pm, gm in self._muon_units(group):
             tp_group, tp_dim = self._tp_of(p)
-            if "momentum_buffer" not in st:
-                rows, cols = self._full_shape(p, pm.shape)
-                st["momentum_buffer"] = torch.zeros(pm.shape, dtype=torch.float32, device=pm.device)
-                st["second_momentum_buffer"] = torch.zeros(
-                    (rows, 1) if rows >= cols else (1, cols), dtype=torch.float32, device=pm.device)
-            normuon_update(
-                pm, gm.float(), st["momentum_buffer"], st["second_momentum_buffer"],
+            key = (id(group), tuple(pm.shape), pm.dtype, tp_group is not None, tp_dim)
+            by_key.setdefault(key, []).append((p, pm, gm))
+        for key, units in by_key.items():
+            members = [u[0] for u in units]
+            shape = units[0][1].shape
+            st = self._muon_stack_state(key, members, shape, units[0][1].device)
+            grads = torch.stack([u[2].float() for u in units])
+            tp_group, tp_dim = self._tp_of(members[0])
+            normuon_update_batched(
+                [u[1] for u in units], grads, st["mb"], st["smb"],
                 lr=group["lr"], momentum=group["momentum"],
                 beta2=group["beta2"] if group.get("beta2") is not None else 0.0,
                 wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5), tp_group=tp_group, tp_dim=tp_dim,
@@ -314,6 +348,7 @@ class DistMuonAdamW(Optimizer):
         eng = self._engine
         self.state.clear()
         self._shard_state.clear()
+        self._muon_stacks.clear()
         for g, sg in zip(self.param_groups, saved_groups, strict=True):
             for k, v in sg.items():
                 if k != "params":

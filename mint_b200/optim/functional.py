@@ -84,6 +84,41 @@ def polar_express(g: torch.Tensor, ns_steps: int) -> torch.Tensor:
     return x
 
 
+@torch.no_grad()
+def polar_express_batched(g: torch.Tensor, ns_steps: int) -> torch.Tensor:
+    """``polar_express`` on a stack ``[n, rows, cols]`` of equally shaped matrices at once.
+
+    Each of the ``3 * ns_steps`` products is one batched tcgen05 GEMM launch for the whole stack
+    (the per-matrix form needs ``3 * ns_steps`` launches per matrix)."""
+    n, rows, cols = g.shape
+    tall = rows > cols
+    x = g.float()
+    norms = x.flatten(1).norm(dim=1).view(n, 1, 1)
+    x = x / (norms * 1.01 + 1e-6)
+    if g.is_cuda and _ext.kernels_enabled():
+        x = x.to(torch.bfloat16)
+        for a, b, c in POLAR_EXPRESS_COEFFS[:ns_steps]:
+            if tall:
+                A = matmul(x, x, trans_a=True)  # X^T X per matrix
+                B = matmul(A, A, alpha=c, beta=b, d=A)
+                x = matmul(x, B, alpha=1.0, beta=a, d=x)  # a X + X B
+            else:
+                A = matmul(x, x, trans_b=True)  # X X^T per matrix
+                B = matmul(A, A, alpha=c, beta=b, d=A)
+                x = matmul(B, x, alpha=1.0, beta=a, d=x)  # a X + B X
+        return x.float()
+    for a, b, c in POLAR_EXPRESS_COEFFS[:ns_steps]:
+        if tall:
+            A = x.mT @ x
+            B = b * A + c * (A @ A)
+            x = a * x + x @ B
+        else:
+            A = x @ x.mT
+            B = b * A + c * (A @ A)
+            x = a * x + B @ x
+    return x
+
+
 def _tp_gather(t: torch.Tensor, dim: int, group) -> torch.Tensor:  # noqa: ANN001
     import torch.distributed as dist  # noqa: PLC0415
 
@@ -139,3 +174,54 @@ def normuon_update(
     pf = p.float()
     mask = (g * pf) >= 0
     p.sub_((lr * g + lr * wd * pf * mask).to(p.dtype))
+
+
+@torch.no_grad()
+def normuon_update_batched(
+    params: list[torch.Tensor],
+    grads: torch.Tensor,
+    momentum_buffer: torch.Tensor,
+    second_momentum_buffer: torch.Tensor,
+    *,
+    lr: float,
+    momentum: float,
+    beta2: float,
+    wd: float,
+    ns_steps: int,
+    tp_group=None,  # noqa: ANN001
+    tp_dim: int = 0,
+) -> None:
+    """``normuon_update`` for ``n`` equally shaped matrices in one pass.
+
+    ``params`` are the ``n`` parameter matrices (views are fine), ``grads`` / ``momentum_buffer``
+    their stacked ``[n, rows, cols]`` fp32 gradients and momenta, ``second_momentum_buffer`` the
+    stacked ``[n, rows, 1]`` (tall or square) or ``[n, 1, cols]`` (wide) NorMuon statistics of the
+    full matrices. Under tensor parallelism (``tp_group``) the matrices are this rank's shards along
+    ``tp_dim`` and are gathered for orthogonalization as in ``normuon_update``. The result equals
+    ``n`` calls of ``normuon_update`` up to floating-point summation order."""
+    momentum_buffer.lerp_(grads, 1 - momentum)
+    g = grads.lerp(momentum_buffer, momentum)
+    n, shard_rows, shard_cols = g.shape
+    if tp_group is not None:
+        g = _tp_gather(g, 1 + tp_dim, tp_group)
+    _, rows, cols = g.shape
+    red_dim = -1 if rows >= cols else -2
+    lr = lr * max(1.0, rows / cols) ** 0.5
+    g = polar_express_batched(g, ns_steps)
+    v_mean = g.square().mean(dim=red_dim, keepdim=True)
+    red = g.size(red_dim)
+    v_norm = (v_mean.sum(dim=(1, 2), keepdim=True) * red).sqrt()
+    second_momentum_buffer.lerp_(v_mean, 1 - beta2)
+    step_scale = second_momentum_buffer.clamp_min(1e-10).rsqrt()
+    v_norm_new = ((v_mean * red) * step_scale.square()).sum(dim=(1, 2), keepdim=True).sqrt()
+    g = g * (step_scale * (v_norm / v_norm_new.clamp_min(1e-10)))
+    if tp_group is not None:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        r = dist.get_rank(tp_group)
+        size = shard_rows if tp_dim == 0 else shard_cols
+        g = g.narrow(1 + tp_dim, r * size, size)
+    pf = torch.stack([p.float() for p in params]) if len(params) > 1 else params[0].float().unsqueeze(0)
+    mask = (g * pf) >= 0
+    new = pf - (lr * g + lr * wd * pf * mask)
+    torch._foreach_copy_(params, list(new.to(params[0].dtype).unbind(0)))

@@ -34,6 +34,9 @@ CASES = [
     (2, 300, 4, 4, True, -1, True),
     (1, 256, 2, 1, False, -1, False),
     (1, 1024, 6, 6, True, 256, False),
+    (2, 640, 4, 2, True, -1, "unsorted"),
+    (1, 1024, 2, 2, True, 300, True),
+    (1, 384, 2, 2, False, -1, True),
 ]
 
 
@@ -44,7 +47,11 @@ def test_flash_attention_fwd_bwd(B, T, Hq, Hkv, causal, window, use_doc):
     q = torch.randn(B, T, Hq, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     k = torch.randn(B, T, Hkv, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     v = torch.randn(B, T, Hkv, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    doc = (torch.arange(T, device="cuda") // 70).expand(B, -1).contiguous() if use_doc else None
+    doc = None
+    if use_doc == "unsorted":  # ids repeat non-contiguously: per-element id comparison, no tile skipping
+        doc = ((torch.arange(T, device="cuda") // 70) % 3).expand(B, -1).contiguous()
+    elif use_doc:
+        doc = (torch.arange(T, device="cuda") // 70).expand(B, -1).contiguous()
     o = attention(q, k, v, causal=causal, window_left=window, doc_ids=doc)
     do = torch.randn_like(o)
     (o.float() * do.float()).sum().backward()

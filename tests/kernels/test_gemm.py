@@ -105,3 +105,21 @@ def test_gemm_column_slice_operand():
     matmul(dy[:, 768:1536], x, trans_a=True, out=out, accumulate=True)
     exp = dy[:, 768:1536].float().t() @ x.float()
     assert ((out - exp).norm() / exp.norm()).item() < 2e-3
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True)])
+@pytest.mark.parametrize("shape", [(5, 192, 320, 256), (3, 768, 768, 3072), (24, 128, 96, 64)])
+def test_gemm_batched(ta, tb, shape):
+    """3-D operands: one launch for a stack of equally shaped GEMMs (batched Polar Express), with
+    the beta * D epilogue reading each batch's own D."""
+    torch.manual_seed(2)
+    nb, M, N, K = shape
+    a = torch.randn((nb, K, M) if ta else (nb, M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((nb, N, K) if tb else (nb, K, N), device="cuda", dtype=torch.bfloat16)
+    d = torch.randn(nb, M, N, device="cuda", dtype=torch.bfloat16)
+    out = matmul(a, b, trans_a=ta, trans_b=tb, alpha=0.5, beta=-1.5, d=d, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    for i in range(nb):
+        exp = ref(a[i], b[i], ta, tb, 0.5, -1.5, d[i])
+        err = (out[i] - exp).abs().max().item()
+        assert err < 1e-2 * max(1.0, exp.abs().max().item() / 50), f"batch {i} max err {err}"
