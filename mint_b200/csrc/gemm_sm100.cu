@@ -12,6 +12,8 @@
 // The fp32 accumulator is double-buffered in tensor memory (2 x BN columns) so the epilogue of
 // tile t overlaps the MMAs of tile t+1. Every mbarrier wait is bounded (common.cuh); on a
 // timeout the kernel records a status code, drains its in-flight MMAs, frees TMEM and exits.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -74,6 +76,98 @@ __device__ __forceinline__ void work_item(const Params& p, int w, int kblocks, i
   tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
   kb0 = split * p.kbps;
   nkb = min(kblocks, kb0 + p.kbps) - kb0;
+}
+
+// Epilogue of one accumulator tile for one warp: its 32 TMEM lanes (rows row0 .. row0+31 of C) x BN
+// columns, in 32-column chunks: alpha / beta*D, conversion, a swizzled shared-memory staging buffer
+// (double-buffered per warp) and one TMA store (or TMA reduce-add) per chunk; TMA clips rows and
+// columns outside C.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tmc, uint32_t tmem_acc, int row0,
+                                              int col_base, int bi, float alpha, bool f32_out, uint8_t* bufs, int lane,
+                                              int& seq) {
+  const int row = row0 + lane;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tmem_acc + c * 32, r);
+    tmem_ld_wait();
+    const int col0 = col_base + c * 32;
+    if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
+    if (p.D != nullptr && p.beta != 0.0f && row < p.M) {
+      const bool full_chunk = col0 + 32 <= p.N;
+      if (p.d_fp32) {
+        const float* dp = static_cast<const float*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
+        if (full_chunk) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(dp + j);
+            v[j] += p.beta * d4.x;
+            v[j + 1] += p.beta * d4.y;
+            v[j + 2] += p.beta * d4.z;
+            v[j + 3] += p.beta * d4.w;
+          }
+        } else {
+          for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * dp[j];
+        }
+      } else {
+        const __nv_bfloat16* dp =
+            static_cast<const __nv_bfloat16*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
+        if (full_chunk) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            const uint4 u = *reinterpret_cast<const uint4*>(dp + j);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              v[j + 2 * e] += p.beta * f.x;
+              v[j + 2 * e + 1] += p.beta * f.y;
+            }
+          }
+        } else {
+          for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * __bfloat162float(dp[j]);
+        }
+      }
+    }
+    uint8_t* buf = bufs + (seq & 1) * 4096;
+    // the TMA store issued two chunks ago read this buffer: wait for it (keep one in flight)
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    if (f32_out) {
+      // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row `lane` at j ^ (lane % 8)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+    } else {
+      // 32 rows x 64 B, 64B swizzle: 16-byte chunk j of row `lane` at j ^ ((lane / 2) % 4)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 u;
+        u.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+        u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (p.atomic_out) {
+        tma_reduce_add_3d(tmc, buf, col0, row0, bi);
+      } else {
+        tma_store_3d(tmc, buf, col0, row0, bi);
+      }
+      bulk_commit();
+    }
+    ++seq;
+  }
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -229,88 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int bi, tm, tn, kb0_, nkb_;
       work_item(p, tile, kblocks, bi, tm, tn, kb0_, nkb_);
       const int row0 = tm * BM + q * 32;
-      const int row = row0 + lane;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = tn * BN + c * 32;
-        if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
-        if (p.D != nullptr && p.beta != 0.0f && row < p.M) {
-          const bool full_chunk = col0 + 32 <= p.N;
-          if (p.d_fp32) {
-            const float* dp = static_cast<const float*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
-            if (full_chunk) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 d4 = *reinterpret_cast<const float4*>(dp + j);
-                v[j] += p.beta * d4.x;
-                v[j + 1] += p.beta * d4.y;
-                v[j + 2] += p.beta * d4.z;
-                v[j + 3] += p.beta * d4.w;
-              }
-            } else {
-              for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * dp[j];
-            }
-          } else {
-            const __nv_bfloat16* dp =
-                static_cast<const __nv_bfloat16*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
-            if (full_chunk) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                const uint4 u = *reinterpret_cast<const uint4*>(dp + j);
-                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = __bfloat1622float2(h[e]);
-                  v[j + 2 * e] += p.beta * f.x;
-                  v[j + 2 * e + 1] += p.beta * f.y;
-                }
-              }
-            } else {
-              for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * __bfloat162float(dp[j]);
-            }
-          }
-        }
-        uint8_t* buf = bufs + (seq & 1) * 4096;
-        // the TMA store issued two chunks ago read this buffer: wait for it (keep one in flight)
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-        if (f32_out) {
-          // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row `lane` at j ^ (lane % 8)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          }
-        } else {
-          // 32 rows x 64 B, 64B swizzle: 16-byte chunk j of row `lane` at j ^ ((lane / 2) % 4)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 u;
-            u.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
-            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-            *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (p.atomic_out) {
-            tma_reduce_add_3d(&tmc, buf, col0, row0, bi);
-          } else {
-            tma_store_3d(&tmc, buf, col0, row0, bi);
-          }
-          bulk_commit();
-        }
-        ++seq;
-      }
+      epilogue_tile<BN>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN, row0, tn * BN, bi,
+                        alpha, f32_out, bufs, lane, seq);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -332,15 +346,258 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
             cudaStream_t stream) {
   using C_ = Cfg<BN>;
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};  // the attribute is per device
+  int dev = 0;
+  MINT_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!configured[dev & 63]) {
     MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes));
-    configured = true;
+    configured[dev & 63] = true;
   }
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * p.splits * p.batch;
   const int grid = tiles < sms ? static_cast<int>(tiles) : sms;
   kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, tc, p);
   MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+// ---------------------------------------------------------------------------------------------
+// CTA-pair kernel: a cluster of 2 CTAs on 2 SMs computes one 256 x BN tile with tcgen05.mma
+// cta_group::2. CTA r of the pair loads rows [128 r, 128 r + 128) of the A tile and rows
+// [BN/2 r, BN/2 r + BN/2) of the B tile into its own shared memory; the leader (r = 0) issues
+// the MMAs, which read both CTAs' halves and write 128 rows of the accumulator into each CTA's
+// tensor memory. Each SM thus streams 16 KB of A and BN/8 KB of B per 64-deep k-block instead
+// of 16 + BN/4 KB, halving the shared operand traffic the single-CTA kernel spends on B.
+// Barriers: full[s] and tempty[] live in the leader (the follower's TMA completes bytes on the
+// leader's full[s]; both epilogues arrive on the leader's tempty[]); empty[s] and tfull[] live in
+// both CTAs and the leader's MMA thread commits to each explicitly.
+template <int BN>
+struct Cfg2 {
+  static constexpr int kStages = 5;
+  static constexpr int kABytes = 128 * BK * 2;       // this CTA's 128 rows of A
+  static constexpr int kBBytes = (BN / 2) * BK * 2;  // this CTA's BN/2 rows of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarrierBytes = 1024;
+  static constexpr int kStagingBytes = 4 * 2 * 4096;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                     const __grid_constant__ CUtensorMap tmc, Params p) {
+  using C_ = Cfg2<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C_::kStages * C_::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::kStages * C_::kStageBytes);
+  uint64_t* empty = full + C_::kStages;
+  uint64_t* tfull = empty + C_::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* staging = smem + C_::kStages * C_::kStageBytes + C_::kBarrierBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cr = cluster_ctarank();
+  const bool leader = cr == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < C_::kStages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, C_::kTmemCols);
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialized before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m2 = (p.M + 255) / 256;
+  const int tiles_per_batch = tiles_m2 * p.tiles_n * p.splits;
+  const int num_tiles = tiles_per_batch * p.batch;
+  const int kblocks = (p.K + BK - 1) / BK;
+  // work item -> (batch, 256-row tile, column tile, k range)
+  auto item = [&](int w, int& bi, int& tm, int& tn, int& kb0, int& nkb) {
+    bi = w / tiles_per_batch;
+    w -= bi * tiles_per_batch;
+    const int tiles = tiles_m2 * p.tiles_n;
+    const int tile = w % tiles;
+    const int split = w / tiles;
+    tile_coords(tile, tiles_m2, p.tiles_n, tm, tn);
+    kb0 = split * p.kbps;
+    nkb = min(kblocks, kb0 + p.kbps) - kb0;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tma);
+      tma_prefetch_desc(&tmb);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int w = pair; w < num_tiles && ok; w += npairs) {
+        int bi, tm, tn, kb0, nkb;
+        item(w, bi, tm, tn, kb0, nkb);
+        const int m0 = tm * 256 + static_cast<int>(cr) * 128;
+        const int n0 = tn * BN + static_cast<int>(cr) * (BN / 2);
+        for (int kb = kb0; kb < kb0 + nkb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          // the leader's full[stage] counts both CTAs' bytes; only the leader arrives on it
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C_::kStageBytes);
+          const uint32_t bar = mapa_shared(&full[stage], 0);
+          uint8_t* a_dst = sA + stage * C_::kABytes;
+          uint8_t* b_dst = sB + stage * C_::kBBytes;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_3d_pair(a_dst, &tma, bar, k0, m0, bi);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) tma_load_3d_pair(a_dst + i * 8192, &tma, bar, m0 + i * 64, k0, bi);
+          }
+          if constexpr (!B_MN) {
+            tma_load_3d_pair(b_dst, &tmb, bar, k0, n0, bi);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 128; ++i) tma_load_3d_pair(b_dst + i * 8192, &tmb, bar, n0 + i * 64, k0, bi);
+          }
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = umma_idesc_bf16(256, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      bool ok = true;
+      for (int w = pair; w < num_tiles && ok; w += npairs, ++t) {
+        const int acc = t & 1;
+        const uint32_t acc_phase = (t >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, kStatusTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        int bi_, tm_, tn_, kb0, nkb;
+        item(w, bi_, tm_, tn_, kb0, nkb);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C_::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * C_::kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a_addr + k * 2048, 8192, 1024)
+                                        : umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, 8192, 1024)
+                                        : umma_desc_sw128(b_addr + k * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(mapa_shared(&empty[stage], 0));
+          umma_commit_pair(mapa_shared(&empty[stage], 1));
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) {
+          umma_commit_pair(mapa_shared(&tfull[acc], 0));
+          umma_commit_pair(mapa_shared(&tfull[acc], 1));
+        }
+      }
+      umma_commit_pair(mapa_shared(mma_done, 0));
+      mbar_wait(mma_done, 0, p.status, kStatusTimeoutMma, nullptr);
+    }
+  } else {
+    const int q = warp & 3;
+    uint8_t* bufs = staging + (warp - 2) * 2 * 4096;
+    float alpha = p.alpha;
+    if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
+    const bool f32_out = p.c_fp32 || p.atomic_out;
+    const uint32_t tempty_leader[2] = {mapa_shared(&tempty[0], 0), mapa_shared(&tempty[1], 0)};
+    int t = 0;
+    int seq = 0;
+    for (int w = pair; w < num_tiles; w += npairs, ++t) {
+      const int acc = t & 1;
+      const uint32_t acc_phase = (t >> 1) & 1;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      int bi, tm, tn, kb0_, nkb_;
+      item(w, bi, tm, tn, kb0_, nkb_);
+      const int row0 = tm * 256 + static_cast<int>(cr) * 128 + q * 32;
+      epilogue_tile<BN>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN, row0, tn * BN, bi,
+                        alpha, f32_out, bufs, lane, seq);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  // neither CTA releases its tensor memory or shared memory while the pair's MMAs may still use it
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C_::kTmemCols);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, int sms,
+                 cudaStream_t stream) {
+  using C_ = Cfg2<BN>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN>;
+  static bool configured[64] = {};
+  int dev = 0;
+  MINT_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!configured[dev & 63]) {
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes));
+    configured[dev & 63] = true;
+  }
+  const long long tiles = static_cast<long long>((p.M + 255) / 256) * p.tiles_n * p.splits * p.batch;
+  const int pairs = static_cast<int>(std::min<long long>(tiles, sms / 2));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C_::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MINT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p));
   count_launch();
 }
 
@@ -423,6 +680,12 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   const int64_t tiles256 = nb * ((M + 127) / 128) * ((N + 255) / 256);
   const bool use256 = N > 128 && tiles256 >= sms;
   const int BN = use256 ? 256 : 128;
+  // CTA pairs (256-row tiles on 2 SMs) once the pair tiles alone fill the GPU; MINT_GEMM_PAIR=0 disables
+  static const bool pair_enabled = [] {
+    const char* e = std::getenv("MINT_GEMM_PAIR");
+    return e == nullptr || e[0] != '0';
+  }();
+  const bool use_pair = pair_enabled && BN == 256 && M >= 256 && nb * ((M + 255) / 256) * ((N + 255) / 256) >= sms / 2;
   p.tiles_m = static_cast<int>((M + 127) / 128);
   p.tiles_n = static_cast<int>((N + BN - 1) / BN);
   const int kblocks = static_cast<int>((K + gemm::BK - 1) / gemm::BK);
@@ -451,7 +714,8 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
   const CUtensorMap ta = a_kmajor ? make_tmap_3d(A.data_ptr(), BF, 2, K, M, nb, lda, bstride(A), 64, 128, 1, SW128)
                                   : make_tmap_3d(A.data_ptr(), BF, 2, M, K, nb, lda, bstride(A), 64, 64, 1, SW128);
-  const CUtensorMap tb = b_kmajor ? make_tmap_3d(B.data_ptr(), BF, 2, K, N, nb, ldb, bstride(B), 64, BN, 1, SW128)
+  const uint32_t bbox = use_pair ? BN / 2 : BN;  // a CTA of a pair loads half of the B tile
+  const CUtensorMap tb = b_kmajor ? make_tmap_3d(B.data_ptr(), BF, 2, K, N, nb, ldb, bstride(B), 64, bbox, 1, SW128)
                                   : make_tmap_3d(B.data_ptr(), BF, 2, N, K, nb, ldb, bstride(B), 64, 64, 1, SW128);
   const bool f32c = p.c_fp32 != 0;
   const CUtensorMap tcm =
@@ -463,12 +727,20 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   else if (!a_mn && b_mn) gemm::launch<BNV, false, true>(ta, tb, tcm, p, sms, stream); \
   else if (a_mn && !b_mn) gemm::launch<BNV, true, false>(ta, tb, tcm, p, sms, stream); \
   else gemm::launch<BNV, true, true>(ta, tb, tcm, p, sms, stream);
-  if (BN == 256) {
+#define MINT_GEMM_DISPATCH_PAIR(BNV)                                                       \
+  if (!a_mn && !b_mn) gemm::launch_pair<BNV, false, false>(ta, tb, tcm, p, sms, stream);   \
+  else if (!a_mn && b_mn) gemm::launch_pair<BNV, false, true>(ta, tb, tcm, p, sms, stream); \
+  else if (a_mn && !b_mn) gemm::launch_pair<BNV, true, false>(ta, tb, tcm, p, sms, stream); \
+  else gemm::launch_pair<BNV, true, true>(ta, tb, tcm, p, sms, stream);
+  if (use_pair) {
+    MINT_GEMM_DISPATCH_PAIR(256)
+  } else if (BN == 256) {
     MINT_GEMM_DISPATCH(256)
   } else {
     MINT_GEMM_DISPATCH(128)
   }
 #undef MINT_GEMM_DISPATCH
+#undef MINT_GEMM_DISPATCH_PAIR
 }
 
 }  // namespace mint

@@ -123,3 +123,35 @@ def test_gemm_batched(ta, tb, shape):
         exp = ref(a[i], b[i], ta, tb, 0.5, -1.5, d[i])
         err = (out[i] - exp).abs().max().item()
         assert err < 1e-2 * max(1.0, exp.abs().max().item() / 50), f"batch {i} max err {err}"
+
+
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+def test_gemm_cta_pair_layouts(ta, tb):
+    """Shapes large enough for the CTA-pair kernel (256-row tiles on 2 SMs, tcgen05 cta_group::2),
+    with a ragged M and N so both CTAs of a pair see clipped rows and columns."""
+    torch.manual_seed(3)
+    M, N, K = 4100, 2336, 640
+    a = torch.randn((K, M) if ta else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((N, K) if tb else (K, N), device="cuda", dtype=torch.bfloat16)
+    d = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    out = matmul(a, b, trans_a=ta, trans_b=tb, alpha=0.25, beta=2.0, d=d, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    exp = ref(a, b, ta, tb, 0.25, 2.0, d)
+    rel = ((out.float() - exp).norm() / exp.norm()).item()
+    assert rel < 1e-2, f"rel err {rel}"
+
+
+def test_gemm_cta_pair_accumulate():
+    """Weight-gradient form (A MN-major, fp32 C accumulated through TMA reduce-adds) on the pair kernel."""
+    torch.manual_seed(4)
+    M, N, K = 4096, 2304, 512
+    a = torch.randn(K, M, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)
+    out = torch.randn(M, N, device="cuda", dtype=torch.float32)
+    start = out.clone()
+    matmul(a, b, trans_a=True, out=out, accumulate=True)
+    torch.cuda.synchronize()
+    exp = start + a.float().t() @ b.float()
+    err = (out - exp).abs().max().item()
+    assert err < 5e-2, f"max err {err}"
