@@ -19,6 +19,9 @@
 // written once dV has consumed P); dQ_i lands in the dP^T columns once dS is computed, so the MMA
 // issue order dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1} keeps the tensor pipe busy while the math warps
 // produce dS_i and drain dQ_i.
+#include <cstdio>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host_common.h"
 #include "attention_bwd_raw.h"
@@ -56,14 +59,18 @@ struct Smem {
   uint8_t q[2][kTileBytes];
   uint8_t dout[2][kTileBytes];
   uint8_t pds[kTileBytes];  // P^T, then dS^T of the same query tile
-  float lse2[2][kB];        // log2-scaled LSE of the current query tile (double-buffered)
-  float dlt[2][kB];         // delta of the current query tile
+  float lse2[kB];           // log2-scaled LSE of the current query tile
+  float dlt[kB];            // delta of the current query tile
   uint64_t kv_full, q_full[2], q_empty[2], do_full[2], do_empty[2];
   uint64_t s_full, dp_full, p_ready, dv_done, ds_ready, dq_full, dq_free, mma_done;
   uint64_t stg_full;  // the 8 math warps staged this tile's LSE / delta
+  uint64_t stg_free;  // the 8 math warps finished reading them
   uint32_t tmem_base;
   int abort_flag;
 };
+// dynamic shared memory = the struct + 1024 bytes of alignment slack; 232448 is the per-block opt-in limit
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared-memory layout exceeds the per-block limit");
+
 
 // K-major operand (row-contiguous 128 x 128 tile, 2 atoms along K): descriptor of K-step k
 __device__ __forceinline__ uint64_t kmaj(uint32_t base, int k) {
@@ -155,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&s.dq_full, 1);
     mbar_init(&s.dq_free, 8);
     mbar_init(&s.stg_full, 8);
+    mbar_init(&s.stg_free, 8);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -266,23 +274,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = hk * G + it / nq;
       const int q0 = (i0 + it % nq) * kB;
       const int q_last = min(p.T, q0 + kB) - 1;
-      // stage this query tile's LSE (log2 units) and delta; the buffer was last read two tiles ago,
-      // before every math warp arrived on the previous tile's staging barrier
+      // stage this query tile's LSE (log2 units) and delta once every math warp is done with the
+      // previous tile's values
+      if (it > 0 && !(ok = mbar_wait_warp(&s.stg_free, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag))) break;
       {
         const int c = mt & (kB - 1);
         const int qi = q0 + c;
         const long long rowbase = (static_cast<long long>(b) * p.Hq + h) * p.T;
         if (mt < kB) {
-          s.lse2[it & 1][c] = qi < p.T ? p.lse[rowbase + qi] * 1.4426950408889634f : INFINITY;
+          s.lse2[c] = qi < p.T ? p.lse[rowbase + qi] * 1.4426950408889634f : INFINITY;
         } else {
-          s.dlt[it & 1][c] = qi < p.T ? p.delta[rowbase + qi] : 0.f;
+          s.dlt[c] = qi < p.T ? p.delta[rowbase + qi] : 0.f;
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.stg_full);
       if (!(ok = mbar_wait_warp(&s.stg_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
-      const float* lse2 = s.lse2[it & 1] + cb;
-      const float* dlt = s.dlt[it & 1] + cb;
+      const float* lse2 = s.lse2 + cb;
+      const float* dlt = s.dlt + cb;
       if (!(ok = mbar_wait_warp(&s.s_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       tc_fence_after();
       float x[64];
@@ -324,6 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           x[c] = x[c] * (__uint_as_float(u[e]) - dlt[c]);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.stg_free);  // this warp's last read of lse2 / dlt for the tile
       // dS overwrites P only after dV has consumed it
       if (!(ok = mbar_wait_warp(&s.dv_done, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       store_half_row_sw128(s.pds, half, r, x);
@@ -489,13 +500,33 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   };
   const CUtensorMap tq = map(q, Hq), tk = map(k, Hkv), tv = map(v, Hkv), tdo = map(dout, Hq);
   const int smem = static_cast<int>(sizeof(fab::Smem)) + 1024;
-  static bool configured = false;
-  if (!configured) {
+  static const bool trace = std::getenv("MINT_TRACE_LAUNCH") != nullptr;
+  auto step = [&](const char* what) {
+    if (!trace) return;
+    const cudaError_t e = cudaDeviceSynchronize();
+    std::fprintf(stderr, "[mint trace] flash_attn_bwd %s: %s (smem %d)\n", what, cudaGetErrorString(e), smem);
+    std::fflush(stderr);
+  };
+  step("after delta kernel");
+  static bool configured[64] = {};
+  const int dev = q.get_device();
+  if (!configured[dev & 63]) {
+    check_smem_optin(smem, dev, "fa_bwd_kernel");
     MINT_CUDA_CHECK(cudaFuncSetAttribute(fab::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
+    configured[dev & 63] = true;
+  }
+  if (trace) {
+    cudaFuncAttributes fa{};
+    const cudaError_t e = cudaFuncGetAttributes(&fa, fab::fa_bwd_kernel);
+    std::fprintf(stderr, "[mint trace] fa_bwd_kernel attrs %s: regs %d local %zu maxThreads %d maxDynSmem %d\n",
+                 cudaGetErrorString(e), fa.numRegs, fa.localSizeBytes, fa.maxThreadsPerBlock,
+                 fa.maxDynamicSharedSizeBytes);
+    std::fflush(stderr);
   }
   dim3 grid((T + fab::kB - 1) / fab::kB, Hkv, B);
+  step("before main kernel");
   fab::fa_bwd_kernel<<<grid, fab::kThreads, smem, stream>>>(tq, tk, tv, tdo, p);
+  step("after main kernel launch");
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
   const long long n4 = q.numel() / 4;
@@ -550,6 +581,9 @@ void flash_attn_bwd_launch_raw(const FlashBwdRaw& a, cudaStream_t stream) {
 int flash_attn_bwd_smem_bytes() { return static_cast<int>(sizeof(fab::Smem)) + 1024; }
 
 void flash_attn_bwd_configure_current_device() {
+  int dev = 0;
+  MINT_CUDA_CHECK(cudaGetDevice(&dev));
+  check_smem_optin(flash_attn_bwd_smem_bytes(), dev, "fa_bwd_kernel");
   MINT_CUDA_CHECK(cudaFuncSetAttribute(fab::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        flash_attn_bwd_smem_bytes()));
 }

@@ -52,6 +52,9 @@ struct Smem {
   uint32_t tmem_base;
   int abort_flag;
 };
+// dynamic shared memory = the struct + 1024 bytes of alignment slack; 232448 is the per-block opt-in limit
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared-memory layout exceeds the per-block limit");
+
 
 // Key tiles a query tile visits. With sorted document ids, keys before the document of the tile's
 // first query and (non-causal) after the document of its last query are skipped.
@@ -461,10 +464,12 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k,
   const CUtensorMap tv = make_tmap_3d_bf16(v.data_ptr(), fa::kD, Hkv, static_cast<uint64_t>(B) * T, fa::kD,
                                            static_cast<uint64_t>(Hkv) * fa::kD, 64, 1, 128, true);
   const int smem = static_cast<int>(sizeof(fa::Smem)) + 1024;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};  // the attribute is per device
+  const int dev = q.get_device();
+  if (!configured[dev & 63]) {
+    check_smem_optin(smem, dev, "fa_fwd_kernel");
     MINT_CUDA_CHECK(cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
+    configured[dev & 63] = true;
   }
   dim3 grid((T + fa::kBM - 1) / fa::kBM, Hq, B);
   fa::fa_fwd_kernel<<<grid, fa::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);

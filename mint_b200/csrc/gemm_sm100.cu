@@ -34,6 +34,7 @@ struct Cfg {
   static constexpr int kBarrierBytes = 1024;
   static constexpr int kStagingBytes = 4 * 2 * 4096;  // 4 epilogue warps x 2 buffers x (32 x 32 fp32)
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
+  static_assert(kSmemBytes <= 232448, "shared-memory layout exceeds the per-block opt-in limit");
 };
 
 struct Params {
@@ -350,6 +351,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
   int dev = 0;
   MINT_CUDA_CHECK(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
+    check_smem_optin(C_::kSmemBytes, dev, "gemm");
     MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes));
     configured[dev & 63] = true;
   }
@@ -380,6 +382,7 @@ struct Cfg2 {
   static constexpr int kBarrierBytes = 1024;
   static constexpr int kStagingBytes = 4 * 2 * 4096;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
+  static_assert(kSmemBytes <= 232448, "shared-memory layout exceeds the per-block opt-in limit");
 };
 
 template <int BN, bool A_MN, bool B_MN>
@@ -580,6 +583,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
   int dev = 0;
   MINT_CUDA_CHECK(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
+    check_smem_optin(C_::kSmemBytes, dev, "gemm");
     MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes));
     configured[dev & 63] = true;
   }

@@ -64,6 +64,12 @@ int num_sms(int device) {
   return g_sms[device];
 }
 
+void check_smem_optin(int bytes, int device, const char* kernel) {
+  int limit = 0;
+  MINT_CUDA_CHECK(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  MINT_CHECK(bytes <= limit, kernel, " needs ", bytes, " bytes of dynamic shared memory; the device allows ", limit);
+}
+
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
                               uint32_t box_cols, bool swizzle128) {
   MINT_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");

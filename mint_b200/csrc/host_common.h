@@ -45,6 +45,11 @@ CUtensorMap make_tmap_3d(const void* base, int dtype, int esize, uint64_t d0, ui
 
 int num_sms(int device);
 
+// Raise a clear error when a kernel's dynamic shared memory exceeds the device's per-block opt-in
+// limit. Call before cudaFuncSetAttribute(MaxDynamicSharedMemorySize): on this driver an
+// over-limit request crashed the process instead of returning an error code.
+void check_smem_optin(int bytes, int device, const char* kernel);
+
 // Number of kernels launched by this extension since process start (bench.py's gpu_launches).
 void count_launch(int n = 1);
 int64_t launch_count();
