@@ -380,13 +380,15 @@ struct Cfg2 {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 1024;
-  static constexpr int kStagingBytes = 4 * 2 * 4096;
+  static constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each draining half of the columns
+  static constexpr int kThreads = (2 + kEpiWarps) * 32;
+  static constexpr int kStagingBytes = kEpiWarps * 2 * 4096;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
   static_assert(kSmemBytes <= 232448, "shared-memory layout exceeds the per-block opt-in limit");
 };
 
 template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                      const __grid_constant__ CUtensorMap tmc, Params p) {
   using C_ = Cfg2<BN>;
@@ -417,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 8);  // 4 epilogue warps in each CTA of the pair
+      mbar_init(&tempty[i], 2 * C_::kEpiWarps);  // every epilogue warp of both CTAs of the pair
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -539,7 +541,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(mma_done, 0, p.status, kStatusTimeoutMma, nullptr);
     }
   } else {
+    // warp w drains TMEM lane quadrant w % 4 (the lanes a warp may access), columns of half (w - 2) / 4
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     uint8_t* bufs = staging + (warp - 2) * 2 * 4096;
     float alpha = p.alpha;
     if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
@@ -555,8 +559,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int bi, tm, tn, kb0_, nkb_;
       item(w, bi, tm, tn, kb0_, nkb_);
       const int row0 = tm * 256 + static_cast<int>(cr) * 128 + q * 32;
-      epilogue_tile<BN>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN, row0, tn * BN, bi,
-                        alpha, f32_out, bufs, lane, seq);
+      epilogue_tile<BN / 2>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + half * (BN / 2),
+                            row0, tn * BN + half * (BN / 2), bi, alpha, f32_out, bufs, lane, seq);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
@@ -591,7 +595,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
   const int pairs = static_cast<int>(std::min<long long>(tiles, sms / 2));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(C_::kThreads, 1, 1);
   cfg.dynamicSmemBytes = C_::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
