@@ -7,7 +7,8 @@
     python benchmarks/kernels.py gemm --M 65536 --N 2304 --K 768              # y = x W^T
     python benchmarks/kernels.py gemm --M 768 --N 2304 --K 65536 --layout wgrad
     python benchmarks/kernels.py gemm --M 768 --N 3072 --K 768 --batch 24     # batched (Polar Express)
-    python benchmarks/kernels.py attn ... --once   # one untimed call per kernel (for ncu captures)
+    python benchmarks/kernels.py attn ... --once       # one untimed call per kernel (for ncu captures)
+    python benchmarks/kernels.py gemm ... --once-lib   # the same for the library path
 
 Timing: CUDA events on the launching stream, after warm-up, a synchronize on both sides, median
 of ``--iters`` runs; before each run a 256 MB buffer is rewritten so no run starts with the
@@ -93,6 +94,12 @@ def run_attn(a: argparse.Namespace) -> dict:
         C.flash_attn_bwd(do, q, k, v, o, lse, doc, causal, a.window, scale, *extra)
         torch.cuda.synchronize()
         return {"once": True}
+    if a.once_lib:  # the library path once (torch SDPA forward + backward), for profiler captures
+        qt, kt, vt = (t.transpose(1, 2).detach().requires_grad_() for t in (q, k, v))
+        ot = F.scaled_dot_product_attention(qt, kt, vt, is_causal=causal, enable_gqa=Hq != Hkv)
+        torch.autograd.grad(ot, (qt, kt, vt), do.transpose(1, 2))
+        torch.cuda.synchronize()
+        return {"once_lib": True}
     pairs = kept_pairs(T, causal, a.window, a.docs)
     fwd_flop = 4.0 * B * Hq * D * pairs
     res = {"B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "causal": causal, "window": a.window, "docs": a.docs}
@@ -150,8 +157,8 @@ def run_gemm(a: argparse.Namespace) -> dict:
 
         def lib():  # noqa: ANN202  (cuBLAS bf16 GEMM of the same shape, fp32 accumulation inside)
             return dy.mT @ x
-    if a.once:
-        ours()
+    if a.once or a.once_lib:
+        (lib if a.once_lib else ours)()
         torch.cuda.synchronize()
         return {"once": True}
     flop = 2.0 * M * N * K * nb
@@ -181,6 +188,7 @@ def main() -> None:
     for p in (at, gm):
         p.add_argument("--iters", type=int, default=10)
         p.add_argument("--once", action="store_true")
+        p.add_argument("--once-lib", action="store_true", help="run the library (cuBLAS / SDPA) path once")
     a = ap.parse_args()
     res = run_attn(a) if a.cmd == "attn" else run_gemm(a)
     _ext.check_device_status()

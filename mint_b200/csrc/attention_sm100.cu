@@ -6,11 +6,13 @@
 //                 S_j = Q K_j^T   (M=128 queries, N=128 keys, K=128)  -> TMEM S buffer j%2
 //                 O  += P_j V_j   (M=128, N=128 head dims, K=128 keys, P from shared memory)
 //               S_{j+1} is issued before PV_j so the softmax of tile j+1 overlaps PV_j.
-//   warps 4..7  softmax: each thread owns one query row (TMEM lane), loads its 128 scores with
-//               tcgen05.ld, applies causal / sliding-window / document / sequence-end masks,
-//               exp2 with a lazily updated running max (O is rescaled in TMEM only when the max
-//               grows by more than 2^8), writes P (bf16) in the 128B-swizzled K-major layout the
-//               PV MMA reads, and finally normalizes O and stores O and the log-sum-exp.
+//   warps 4..11 softmax, two per TMEM lane quadrant: each thread owns half (64 columns) of one
+//               query row, loads its scores with tcgen05.ld, applies causal / sliding-window /
+//               document / sequence-end masks, exchanges its partial row maximum with the other
+//               half through shared memory, exp2 with a lazily updated running max (its half of O
+//               is rescaled in TMEM only when the max grows by more than 2^8), writes its half of
+//               P (bf16) in the 128B-swizzled K-major layout the PV MMA reads, and finally
+//               normalizes its half of O and stores O and the log-sum-exp.
 // Tiles outside the causal / window band are never visited. All waits are bounded.
 #include "common.cuh"
 #include "host_common.h"
@@ -21,7 +23,7 @@ namespace fa {
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kD = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warps 4..11 softmax (2 per TMEM lane quadrant)
 constexpr int kTileBytes = kBM * kD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-wide swizzle atoms)
 constexpr int kAtomBytes = kTileBytes / 2;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -49,6 +51,9 @@ struct Smem {
   uint64_t p_full;
   uint64_t pv_done;
   uint64_t mma_done;
+  uint64_t mx_full;        // the 8 softmax warps published their partial row maxima (and, last, row sums)
+  float mx[2][2][kBM];     // [tile parity][column half][row] partial maxima of the current score tile
+  float lsum[2][kBM];      // [column half][row] partial row sums, exchanged once at the end
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -121,7 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
     }
-    mbar_init(&s.p_full, 4);
+    mbar_init(&s.p_full, 8);
+    mbar_init(&s.mx_full, 8);
     mbar_init(&s.pv_done, 1);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
@@ -193,7 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&s.mma_done, 0, p.status, kStatusTimeoutAttention, nullptr);
     }
   } else if (warp >= 4) {
+    // warp 4 + 4h + q: TMEM lane quadrant q (query rows q*32 .. q*32+31), score / O columns [64h, 64h + 64)
     const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int cb = half * 64;
     const int r = q * 32 + lane;
     const int qi = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
@@ -206,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the first key and the first row's document ends after the last key
     const int2 dfirst = doc_sorted ? db[q0] : make_int2(0, p.T);
     const int2 dlast = doc_sorted ? db[min(p.T, q0 + kBM) - 1] : make_int2(0, p.T);
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f;  // running max (shared by both halves of the row), this half's row sum
     bool ok = n > 0;
     int pv_waited = -1;  // index of the last PV whose completion this thread observed
     for (int t = 0; t < n && ok; ++t) {
@@ -216,11 +225,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float x[128];
+      float x[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t u[32];
-        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + c * 32, u);
+        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + cb + c * 32, u);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
@@ -231,16 +240,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (need_mask) {
         if (doc_sorted || p.doc == nullptr) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) {
-            const int kj = kb + c;
+          for (int c = 0; c < 64; ++c) {
+            const int kj = kb + cb + c;
             bool keep = kj < p.T && kj >= d_lo && kj < d_hi;
             if (p.causal) keep = keep && kj <= qi;
             if (p.window >= 0) keep = keep && qi - kj <= p.window;
             if (!keep) x[c] = -INFINITY;
           }
         } else {
-          for (int c = 0; c < 128; ++c) {
-            const int kj = kb + c;
+          for (int c = 0; c < 64; ++c) {
+            const int kj = kb + cb + c;
             bool keep = kj < p.T;
             if (p.causal) keep = keep && kj <= qi;
             if (p.window >= 0) keep = keep && qi - kj <= p.window;
@@ -251,12 +260,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mt = fmaxf(mt, x[c]);
+      for (int c = 0; c < 64; ++c) mt = fmaxf(mt, x[c]);
+      // combine with the other half of the row; the buffer of this parity was last read two tiles
+      // ago, before every softmax warp arrived on the previous tile's exchange
+      s.mx[t & 1][half][r] = mt;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.mx_full);
+      if (!mbar_wait_warp(&s.mx_full, t & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
+        ok = false;
+        break;
+      }
+      mt = fmaxf(mt, s.mx[t & 1][half ^ 1][r]);
       const float m_new = fmaxf(m, mt);
-      // tcgen05.ld/st are warp-collective: the rescale decision must be uniform across the warp
+      // tcgen05.ld/st are warp-collective: the rescale decision must be uniform across the warp; both
+      // warps of a lane quadrant see the same row maxima and so decide alike
       const bool grow = m != -INFINITY && m_new > m + kRescaleThreshold;
       if (t > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds PV_0..PV_{t-1}: wait for PV_{t-1}, then rescale the rows in tensor memory
+        // O holds PV_0..PV_{t-1}: wait for PV_{t-1}, then rescale this half of the rows in TMEM
         if (pv_waited < t - 1) {
           if (!mbar_wait_warp(&s.pv_done, (t - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
             ok = false;
@@ -268,25 +288,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float alpha = (m == -INFINITY || m_new == -INFINITY) ? 0.f : exp2f(m - m_new);
         l *= alpha;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t u[16];
-          tmem_ld_32x32b_x16(tmem_o + lane_off + c * 16, u);
+          tmem_ld_32x32b_x16(tmem_o + lane_off + cb + c * 16, u);
           tmem_ld_wait();
           uint32_t w[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-          tmem_st_32x32b_x16(tmem_o + lane_off + c * 16, w);
+          tmem_st_32x32b_x16(tmem_o + lane_off + cb + c * 16, w);
         }
         tmem_st_wait();
         m = m_new;
       } else if (m == -INFINITY) {
         m = m_new;  // nothing accumulated in this row yet
       }
-      // P = exp2(x - m) in bf16, row sum in fp32
-      uint32_t pk[64];
+      // P = exp2(x - m) in bf16, this half's row sum in fp32
+      uint32_t pk[32];
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < 32; ++c) {
         const float a = (m == -INFINITY) ? 0.f : exp2f(x[2 * c] - m);
         const float bb = (m == -INFINITY) ? 0.f : exp2f(x[2 * c + 1] - m);
         rs += a + bb;
@@ -301,14 +321,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pv_waited = t - 1;
       }
-      // 128B-swizzled K-major store of this row: atom a (64 keys), 16B chunk c at c ^ (row % 8)
+      // 128B-swizzled K-major store of this half row: swizzle atom `half` (64 keys), 16B chunk c at c ^ (row % 8)
 #pragma unroll
-      for (int a = 0; a < 2; ++a) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 v4 = make_uint4(pk[a * 32 + c * 4], pk[a * 32 + c * 4 + 1], pk[a * 32 + c * 4 + 2], pk[a * 32 + c * 4 + 3]);
-          *reinterpret_cast<uint4*>(s.p + a * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
-        }
+      for (int c = 0; c < 8; ++c) {
+        uint4 v4 = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+        *reinterpret_cast<uint4*>(s.p + half * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -318,39 +335,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && n > 0 && pv_waited < n - 1) {
       ok = mbar_wait_warp(&s.pv_done, (n - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag);
     }
+    // row sum over both halves (a final exchange round on mx_full, phase n)
+    if (ok && n > 0) {
+      s.lsum[half][r] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.mx_full);
+      ok = mbar_wait_warp(&s.mx_full, n & 1, p.status, kStatusTimeoutAttention, abort_flag);
+      if (ok) l += s.lsum[half ^ 1][r];
+    }
     ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
+    if (ok && n > 0) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = qi < p.T;
-      __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + (row_ok ? qi : 0)) * p.Hq + h) * kD;
-      {
+      __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + (row_ok ? qi : 0)) * p.Hq + h) * kD + cb;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t u[32];
-          tmem_ld_32x32b_x32(tmem_o + lane_off + c * 32, u);  // warp-collective: every lane loads
-          tmem_ld_wait();
-          if (!row_ok) continue;
+      for (int c = 0; c < 2; ++c) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tmem_o + lane_off + cb + c * 32, u);  // warp-collective: every lane loads
+        tmem_ld_wait();
+        if (!row_ok) continue;
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 v4;
-            v4.x = pack_bf16x2(__uint_as_float(u[e]) * inv, __uint_as_float(u[e + 1]) * inv);
-            v4.y = pack_bf16x2(__uint_as_float(u[e + 2]) * inv, __uint_as_float(u[e + 3]) * inv);
-            v4.z = pack_bf16x2(__uint_as_float(u[e + 4]) * inv, __uint_as_float(u[e + 5]) * inv);
-            v4.w = pack_bf16x2(__uint_as_float(u[e + 6]) * inv, __uint_as_float(u[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v4;
-          }
-        }
-        // natural-log LSE of the scaled scores: (m + log2 l) * ln 2
-        if (row_ok) {
-          p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] =
-              l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+        for (int e = 0; e < 32; e += 8) {
+          uint4 v4;
+          v4.x = pack_bf16x2(__uint_as_float(u[e]) * inv, __uint_as_float(u[e + 1]) * inv);
+          v4.y = pack_bf16x2(__uint_as_float(u[e + 2]) * inv, __uint_as_float(u[e + 3]) * inv);
+          v4.z = pack_bf16x2(__uint_as_float(u[e + 4]) * inv, __uint_as_float(u[e + 5]) * inv);
+          v4.w = pack_bf16x2(__uint_as_float(u[e + 6]) * inv, __uint_as_float(u[e + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c * 32 + e) = v4;
         }
       }
+      // natural-log LSE of the scaled scores: (m + log2 l) * ln 2
+      if (row_ok && half == 0) {
+        p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] =
+            l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+      }
     } else if (n == 0 && qi < p.T) {
-      __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + qi) * p.Hq + h) * kD;
-      for (int c = 0; c < kD; ++c) orow[c] = __float2bfloat16_rn(0.f);
-      p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] = -INFINITY;
+      __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + qi) * p.Hq + h) * kD + cb;
+      for (int c = 0; c < 64; ++c) orow[c] = __float2bfloat16_rn(0.f);
+      if (half == 0) p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] = -INFINITY;
     }
   }
 
