@@ -51,6 +51,7 @@ struct Params {
   int atomic_out;  // C (fp32) += alpha * acc with 16-byte vector reductions
   int batch;       // independent GEMMs sharing shapes (operands / C addressed as 3-D TMA maps)
   long long sd;    // batch stride of D in elements
+  int diag;        // timing diagnostics (MINT_GEMM_DIAG): 1 = epilogue stores nothing, 2 = no MMAs issued
   uint32_t* status;
 };
 
@@ -134,6 +135,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         }
       }
     }
+    if (p.diag == 1) continue;
     uint8_t* buf = bufs + (seq & 1) * 4096;
     // the TMA store issued two chunks ago read this buffer: wait for it (keep one in flight)
     if (lane == 0) bulk_wait_read<1>();
@@ -290,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         : umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : umma_desc_sw128(b_addr + k * 32, 16, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (p.diag != 2) umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == C_::kStages) {
@@ -523,7 +525,7 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
                                         : umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : umma_desc_sw128(b_addr + k * 32, 16, 1024);
-            umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (p.diag != 2) umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair(mapa_shared(&empty[stage], 0));
           umma_commit_pair(mapa_shared(&empty[stage], 1));
@@ -656,6 +658,11 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   p.beta = static_cast<float>(beta);
   p.c_fp32 = C.scalar_type() == at::kFloat;
   p.batch = static_cast<int>(nb);
+  static const int diag = [] {
+    const char* e = std::getenv("MINT_GEMM_DIAG");
+    return e == nullptr ? 0 : std::atoi(e);
+  }();
+  p.diag = diag;
   p.status = status_ptr(dev);
   if (D_.has_value() && D_->defined() && beta != 0.0) {
     const at::Tensor D = batched ? *D_ : D_->unsqueeze(0);
