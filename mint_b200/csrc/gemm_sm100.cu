@@ -51,7 +51,8 @@ struct Params {
   int atomic_out;  // C (fp32) += alpha * acc with 16-byte vector reductions
   int batch;       // independent GEMMs sharing shapes (operands / C addressed as 3-D TMA maps)
   long long sd;    // batch stride of D in elements
-  int diag;        // timing diagnostics (MINT_GEMM_DIAG): 1 = epilogue stores nothing, 2 = no MMAs issued
+  int diag;        // timing diagnostics (MINT_GEMM_DIAG bits): 1 skip the epilogue body, 2 skip the MMAs,
+                   // 4 skip the TMA loads (results are then meaningless; for isolating pipeline stages)
   uint32_t* status;
 };
 
@@ -89,6 +90,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
                                               int col_base, int bi, float alpha, bool f32_out, uint8_t* bufs, int lane,
                                               int& seq) {
   const int row = row0 + lane;
+  if (p.diag & 1) return;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     uint32_t r[32];
@@ -135,7 +137,6 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         }
       }
     }
-    if (p.diag == 1) continue;
     uint8_t* buf = bufs + (seq & 1) * 4096;
     // the TMA store issued two chunks ago read this buffer: wait for it (keep one in flight)
     if (lane == 0) bulk_wait_read<1>();
@@ -232,6 +233,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (p.diag & 4) {
+            mbar_arrive(&full[stage]);
+            if (++stage == C_::kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[stage], C_::kStageBytes);
           uint8_t* a_dst = sA + stage * C_::kABytes;
           uint8_t* b_dst = sB + stage * C_::kBBytes;
@@ -292,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         : umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : umma_desc_sw128(b_addr + k * 32, 16, 1024);
-            if (p.diag != 2) umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (!(p.diag & 2)) umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == C_::kStages) {
@@ -376,13 +385,15 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
 // both CTAs and the leader's MMA thread commits to each explicitly.
 template <int BN>
 struct Cfg2 {
-  static constexpr int kStages = 5;
+  static constexpr int kStages = 6;                  // 192 KB of operands in flight per SM
   static constexpr int kABytes = 128 * BK * 2;       // this CTA's 128 rows of A
   static constexpr int kBBytes = (BN / 2) * BK * 2;  // this CTA's BN/2 rows of B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 1024;
-  static constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each draining half of the columns
+  // epilogue warps: 4 (one per TMEM lane quadrant) or 8 (two per quadrant, half the columns each);
+  // measured alike, so the shared memory goes to a sixth operand stage instead
+  static constexpr int kEpiWarps = 4;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
   static constexpr int kStagingBytes = kEpiWarps * 2 * 4096;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
@@ -467,6 +478,14 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
             break;
           }
           // the leader's full[stage] counts both CTAs' bytes; only the leader arrives on it
+          if (p.diag & 4) {
+            if (leader) mbar_arrive(&full[stage]);
+            if (++stage == C_::kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C_::kStageBytes);
           const uint32_t bar = mapa_shared(&full[stage], 0);
           uint8_t* a_dst = sA + stage * C_::kABytes;
@@ -525,7 +544,7 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
                                         : umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : umma_desc_sw128(b_addr + k * 32, 16, 1024);
-            if (p.diag != 2) umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (!(p.diag & 2)) umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair(mapa_shared(&empty[stage], 0));
           umma_commit_pair(mapa_shared(&empty[stage], 1));
@@ -545,7 +564,8 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
   } else {
     // warp w drains TMEM lane quadrant w % 4 (the lanes a warp may access), columns of half (w - 2) / 4
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = C_::kEpiWarps == 8 ? (warp - 2) >> 2 : 0;
+    constexpr int kCols = C_::kEpiWarps == 8 ? BN / 2 : BN;
     uint8_t* bufs = staging + (warp - 2) * 2 * 4096;
     float alpha = p.alpha;
     if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
@@ -561,8 +581,8 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
       int bi, tm, tn, kb0_, nkb_;
       item(w, bi, tm, tn, kb0_, nkb_);
       const int row0 = tm * 256 + static_cast<int>(cr) * 128 + q * 32;
-      epilogue_tile<BN / 2>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + half * (BN / 2),
-                            row0, tn * BN + half * (BN / 2), bi, alpha, f32_out, bufs, lane, seq);
+      epilogue_tile<kCols>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + half * kCols,
+                           row0, tn * BN + half * kCols, bi, alpha, f32_out, bufs, lane, seq);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
