@@ -81,10 +81,53 @@ __device__ __forceinline__ void work_item(const Params& p, int w, int kblocks, i
   nkb = min(kblocks, kb0 + p.kbps) - kb0;
 }
 
+// v[j] += beta * D[j] for the first n (<= 64) columns of one output row at element offset `off`
+// (fp32 or bf16 D). Fully unrolled with constant indices so v stays in registers.
+__device__ __forceinline__ void add_beta_d(const Params& p, long long off, float (&v)[64], int n) {
+  if (p.d_fp32) {
+    const float* dp = static_cast<const float*>(p.D) + off;
+    if (n == 64) {
+#pragma unroll
+      for (int j = 0; j < 64; j += 4) {
+        const float4 d4 = *reinterpret_cast<const float4*>(dp + j);
+        v[j] += p.beta * d4.x;
+        v[j + 1] += p.beta * d4.y;
+        v[j + 2] += p.beta * d4.z;
+        v[j + 3] += p.beta * d4.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        if (j < n) v[j] += p.beta * dp[j];
+      }
+    }
+  } else {
+    const __nv_bfloat16* dp = static_cast<const __nv_bfloat16*>(p.D) + off;
+    if (n == 64) {
+#pragma unroll
+      for (int j = 0; j < 64; j += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(dp + j);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          v[j + 2 * e] += p.beta * f.x;
+          v[j + 2 * e + 1] += p.beta * f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        if (j < n) v[j] += p.beta * __bfloat162float(dp[j]);
+      }
+    }
+  }
+}
+
 // Epilogue of one accumulator tile for one warp: its 32 TMEM lanes (rows row0 .. row0+31 of C) x BN
-// columns, in 32-column chunks: alpha / beta*D, conversion, a swizzled shared-memory staging buffer
-// (double-buffered per warp) and one TMA store (or TMA reduce-add) per chunk; TMA clips rows and
-// columns outside C.
+// columns in 64-column groups: two tcgen05.ld per wait, alpha / beta*D, conversion into a 128B-
+// swizzled shared-memory staging tile (double-buffered per warp, 4 KB) and TMA stores (one 32 x 64
+// bf16 box, or two 32 x 32 fp32 boxes / TMA reduce-adds) that clip rows and columns outside C.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tmc, uint32_t tmem_acc, int row0,
                                               int col_base, int bi, float alpha, bool f32_out, uint8_t* bufs, int lane,
@@ -92,85 +135,69 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
   const int row = row0 + lane;
   if (p.diag & 1) return;
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(tmem_acc + c * 32, r);
+  for (int g = 0; g < BN / 64; ++g) {
+    uint32_t r0[32], r1[32];
+    tmem_ld_32x32b_x32(tmem_acc + g * 64, r0);
+    tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, r1);
     tmem_ld_wait();
-    const int col0 = col_base + c * 32;
+    const int col0 = col_base + g * 64;
     if (col0 >= p.N || row0 >= p.M) continue;  // warp-uniform
-    float v[32];
+    float v[64];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
-    if (p.D != nullptr && p.beta != 0.0f && row < p.M) {
-      const bool full_chunk = col0 + 32 <= p.N;
-      if (p.d_fp32) {
-        const float* dp = static_cast<const float*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
-        if (full_chunk) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(dp + j);
-            v[j] += p.beta * d4.x;
-            v[j + 1] += p.beta * d4.y;
-            v[j + 2] += p.beta * d4.z;
-            v[j + 3] += p.beta * d4.w;
-          }
-        } else {
-          for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * dp[j];
-        }
-      } else {
-        const __nv_bfloat16* dp =
-            static_cast<const __nv_bfloat16*>(p.D) + bi * p.sd + static_cast<long long>(row) * p.ldd + col0;
-        if (full_chunk) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            const uint4 u = *reinterpret_cast<const uint4*>(dp + j);
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __bfloat1622float2(h[e]);
-              v[j + 2 * e] += p.beta * f.x;
-              v[j + 2 * e + 1] += p.beta * f.y;
-            }
-          }
-        } else {
-          for (int j = 0; j < 32 && col0 + j < p.N; ++j) v[j] += p.beta * __bfloat162float(dp[j]);
-        }
-      }
+    for (int j = 0; j < 32; ++j) {
+      v[j] = alpha * __uint_as_float(r0[j]);
+      v[32 + j] = alpha * __uint_as_float(r1[j]);
     }
-    uint8_t* buf = bufs + (seq & 1) * 4096;
-    // the TMA store issued two chunks ago read this buffer: wait for it (keep one in flight)
-    if (lane == 0) bulk_wait_read<1>();
-    __syncwarp();
+    if (p.D != nullptr && p.beta != 0.0f && row < p.M) {
+      add_beta_d(p, bi * p.sd + static_cast<long long>(row) * p.ldd + col0, v, min(64, p.N - col0));
+    }
     if (f32_out) {
-      // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row `lane` at j ^ (lane % 8)
+      // two 32 x 32 fp32 boxes (128 B rows, 128B swizzle: chunk j of row `lane` at j ^ (lane % 8))
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      for (int hh = 0; hh < 2; ++hh) {
+        if (col0 + hh * 32 >= p.N) break;
+        uint8_t* buf = bufs + (seq & 1) * 4096;
+        if (lane == 0) bulk_wait_read<1>();  // the store issued two boxes ago read this buffer
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_float4(v[hh * 32 + 4 * j], v[hh * 32 + 4 * j + 1], v[hh * 32 + 4 * j + 2], v[hh * 32 + 4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (p.atomic_out) {
+            tma_reduce_add_3d(tmc, buf, col0 + hh * 32, row0, bi);
+          } else {
+            tma_store_3d(tmc, buf, col0 + hh * 32, row0, bi);
+          }
+          bulk_commit();
+        }
+        ++seq;
       }
     } else {
-      // 32 rows x 64 B, 64B swizzle: 16-byte chunk j of row `lane` at j ^ ((lane / 2) % 4)
+      // one 32 x 64 bf16 box (128 B rows, 128B swizzle)
+      uint8_t* buf = bufs + (seq & 1) * 4096;
+      if (lane == 0) bulk_wait_read<1>();
+      __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 8; ++j) {
         uint4 u;
         u.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
         u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
         u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
         u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-        *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
+        *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
       }
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      if (p.atomic_out) {
-        tma_reduce_add_3d(tmc, buf, col0, row0, bi);
-      } else {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
         tma_store_3d(tmc, buf, col0, row0, bi);
+        bulk_commit();
       }
-      bulk_commit();
+      ++seq;
     }
-    ++seq;
   }
 }
 
@@ -753,9 +780,9 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   const CUtensorMap tb = b_kmajor ? make_tmap_3d(B.data_ptr(), BF, 2, K, N, nb, ldb, bstride(B), 64, bbox, 1, SW128)
                                   : make_tmap_3d(B.data_ptr(), BF, 2, N, K, nb, ldb, bstride(B), 64, 64, 1, SW128);
   const bool f32c = p.c_fp32 != 0;
-  const CUtensorMap tcm =
-      make_tmap_3d(C.data_ptr(), f32c ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : BF, f32c ? 4 : 2, N, M, nb, C.stride(1),
-                   bstride(C), 32, 32, 1, f32c ? SW128 : CU_TENSOR_MAP_SWIZZLE_64B);
+  // store boxes: 32 rows x 128 bytes (32 fp32 or 64 bf16 columns), 128B swizzle
+  const CUtensorMap tcm = make_tmap_3d(C.data_ptr(), f32c ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : BF, f32c ? 4 : 2, N, M,
+                                       nb, C.stride(1), bstride(C), f32c ? 32 : 64, 32, 1, SW128);
   const bool a_mn = !a_kmajor, b_mn = !b_kmajor;
 #define MINT_GEMM_DISPATCH(BNV)                                                       \
   if (!a_mn && !b_mn) gemm::launch<BNV, false, false>(ta, tb, tcm, p, sms, stream);   \
