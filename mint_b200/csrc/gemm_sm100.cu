@@ -739,32 +739,47 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
     return;
   }
   const int sms = num_sms(dev);
-  const int64_t tiles256 = nb * ((M + 127) / 128) * ((N + 255) / 256);
-  const bool use256 = N > 128 && tiles256 >= sms;
-  const int BN = use256 ? 256 : 128;
-  // CTA pairs (256-row tiles on 2 SMs) once the pair tiles alone fill the GPU; MINT_GEMM_PAIR=0 disables
+  const int kblocks = static_cast<int>((K + gemm::BK - 1) / gemm::BK);
+  // CTA pairs (256-row tiles on 2 SMs) when their work items -- tiles, times the split-K factor an
+  // accumulating GEMM may add -- fill at least 90% of the pairs; MINT_GEMM_PAIR=0 disables them
   static const bool pair_enabled = [] {
     const char* e = std::getenv("MINT_GEMM_PAIR");
     return e == nullptr || e[0] != '0';
   }();
-  const bool use_pair = pair_enabled && BN == 256 && M >= 256 && nb * ((M + 255) / 256) * ((N + 255) / 256) >= sms / 2;
+  const int pairs = sms / 2;
+  const int64_t pair_tiles = nb * ((M + 255) / 256) * ((N + 255) / 256);
+  int pair_splits = 1;
+  if (accumulate && pair_tiles < pairs && kblocks >= 8) {
+    pair_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((pairs + pair_tiles - 1) / pair_tiles,
+                                                                          kblocks / 4)));
+  }
+  const bool use_pair = pair_enabled && M >= 256 && N > 128 && pair_tiles * pair_splits * 10 >= pairs * 9;
+  int BN = 256;
+  if (!use_pair) {
+    const int64_t tiles256 = nb * ((M + 127) / 128) * ((N + 255) / 256);
+    BN = (N > 128 && tiles256 >= sms) ? 256 : 128;
+  }
   p.tiles_m = static_cast<int>((M + 127) / 128);
   p.tiles_n = static_cast<int>((N + BN - 1) / BN);
-  const int kblocks = static_cast<int>((K + gemm::BK - 1) / gemm::BK);
   p.splits = 1;
   p.kbps = kblocks;
   if (accumulate) {
     MINT_CHECK(p.c_fp32, "accumulating GEMM needs an fp32 C");
     MINT_CHECK(p.D == nullptr, "accumulating GEMM adds into C; D is not used");
     p.atomic_out = 1;
-    const int64_t tiles = nb * p.tiles_m * p.tiles_n;
-    if (tiles < sms && kblocks >= 8) {
-      // enough (tile, split) work items for ~2 waves, each split with >= 4 k-blocks
-      int splits = static_cast<int>(std::min<int64_t>((2 * sms + tiles - 1) / tiles, kblocks / 4));
-      splits = std::max(splits, 1);
-      p.kbps = (kblocks + splits - 1) / splits;
-      p.splits = (kblocks + p.kbps - 1) / p.kbps;
+    int splits = 1;
+    if (use_pair) {
+      splits = pair_splits;
+    } else {
+      const int64_t tiles = nb * p.tiles_m * p.tiles_n;
+      if (tiles < sms && kblocks >= 8) {
+        // enough (tile, split) work items for ~2 waves, each split with >= 4 k-blocks
+        splits = static_cast<int>(std::min<int64_t>((2 * sms + tiles - 1) / tiles, kblocks / 4));
+      }
     }
+    splits = std::max(splits, 1);
+    p.kbps = (kblocks + splits - 1) / splits;
+    p.splits = (kblocks + p.kbps - 1) / p.kbps;
   }
   MINT_CHECK(static_cast<int64_t>(p.tiles_m) * p.tiles_n * p.splits * nb < (1ll << 31), "too many GEMM tiles");
   // 3-D maps {inner, outer, batch}; for a single GEMM the batch stride only has to be 16-byte aligned

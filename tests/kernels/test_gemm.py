@@ -155,3 +155,19 @@ def test_gemm_cta_pair_accumulate():
     exp = start + a.float().t() @ b.float()
     err = (out - exp).abs().max().item()
     assert err < 5e-2, f"max err {err}"
+
+
+def test_gemm_cta_pair_split_k_accumulate():
+    """A weight-gradient shape with too few 256 x 256 tiles to fill the GPU: CTA pairs plus split-K,
+    each split's partial tile TMA-reduce-added into the fp32 gradient."""
+    torch.manual_seed(5)
+    M, N, K = 2304, 768, 8192
+    a = torch.randn(K, M, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)
+    out = torch.randn(M, N, device="cuda", dtype=torch.float32)
+    start = out.clone()
+    matmul(a, b, trans_a=True, out=out, accumulate=True)
+    torch.cuda.synchronize()
+    exp = start + a.float().t() @ b.float()
+    rel = ((out - exp).norm() / exp.norm()).item()
+    assert rel < 1e-4, f"rel err {rel}"
