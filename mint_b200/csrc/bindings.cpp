@@ -44,6 +44,13 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
                                        double scale, const c10::optional<at::Tensor>& dbounds);
 at::Tensor doc_bounds(const at::Tensor& doc);
+void gemm_ag(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool b_kmajor, const std::vector<int64_t>& src_ptrs,
+             const at::Tensor& arrive, const std::vector<int64_t>& arrive_peers, at::Tensor& rowflag, at::Tensor& claim,
+             int64_t rank, int64_t world, int64_t seg, int64_t seq);
+void gemm_rs(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, bool b_kmajor,
+             const std::vector<int64_t>& push_ptrs, const at::Tensor& recv, const std::vector<int64_t>& flag_ptrs,
+             const at::Tensor& flags, const at::Tensor& arrive, const std::vector<int64_t>& arrive_peers, int64_t rank,
+             int64_t world, int64_t seg, int64_t seq);
 }  // namespace mint
 
 static int64_t read_status(bool reset) {
@@ -80,5 +87,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_bwd", &mint::flash_attn_bwd, "tcgen05 FlashAttention backward -> (dq, dk, dv)",
         py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("doc"),
         py::arg("causal"), py::arg("window"), py::arg("scale"), py::arg("dbounds") = py::none());
+  m.def("gemm_ag", &mint::gemm_ag, "tensor-parallel all-gather of A's rows fused into a CTA-pair tcgen05 GEMM");
+  m.def("gemm_rs", &mint::gemm_rs, "CTA-pair tcgen05 GEMM with the reduce-scatter of its output rows fused in");
   m.def("doc_bounds", &mint::doc_bounds, "[B, T, 2] int32 document run [start, end) of every token");
 }

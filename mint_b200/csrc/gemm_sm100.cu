@@ -401,6 +401,188 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
 }
 
 // ---------------------------------------------------------------------------------------------
+// Tensor-parallel communication fused into the CTA-pair GEMM (rows of A / C are tokens).
+// A rank's token chunk is made of segments of `seg` rows: segment s of rank p holds gathered rows
+// [(s * world + p) * seg, ... + seg) (sequence parallelism shards every sequence of a batch).
+//   COMM 1, all-gather -> GEMM: A is this rank's symmetric gathered buffer; its own chunk is already
+//     in place. Copy warps pull the peers' chunks (128-row blocks, claimed dynamically) over NVLink
+//     into it and publish a per-block flag; the TMA producer waits for a block's flag before
+//     loading it. This rank's own rows are scheduled first, so compute starts at once.
+//   COMM 2, GEMM -> reduce-scatter: tiles of peers' chunks are computed first and pushed from the
+//     epilogue into the owner's receive slot (peer stores) with a per-warp flag; this rank's own
+//     tiles come last and their epilogue adds the received partials before the TMA store of the
+//     reduced rows (C then covers only this rank's chunk, in local row order).
+// Every call has a sequence number `seq`; flags hold the seq of the call that set them and are
+// never reset. At its start each rank writes seq into every peer's arrive[rank]; no rank reads or
+// writes a peer's buffers of call seq before seeing that peer arrive at seq.
+struct CommParams {
+  int rank, world, seg, seq;
+  int* arrive_local;             // [world] (symmetric): arrive_local[p] = latest call rank p entered
+  int* arrive_peer[8];           // peers' arrive arrays
+  const uint8_t* ag_src[8];      // AG: peers' gathered buffers (same layout and offset as ours)
+  uint8_t* ag_dst;               // AG: our gathered buffer (the A operand)
+  long long ag_row_bytes;        // AG: bytes per row of A
+  int* rowflag;                  // AG: [M / 128] local flags (seq when a block landed)
+  unsigned long long* claim;     // AG: work counter, zero at launch
+  __nv_bfloat16* rs_push[8];     // RS: peer p's receive slot for this rank ([Mc, N], rows of chunk p)
+  const __nv_bfloat16* rs_recv;  // RS: our receive slots [world][Mc, N]
+  int* rs_flag_peer[8];          // RS: peer p's flags for this rank [Mc / 128][tiles_n][4]
+  const int* rs_flag_local;      // RS: our flags [world][Mc / 128][tiles_n][4]
+  long long mc;                  // rows per chunk (M / world)
+};
+
+__device__ __forceinline__ int chunk_of_row(const CommParams& c, long long g) {
+  return static_cast<int>((g / c.seg) % c.world);
+}
+__device__ __forceinline__ long long local_row_of(const CommParams& c, long long g) {
+  return (g / (static_cast<long long>(c.seg) * c.world)) * c.seg + g % c.seg;
+}
+__device__ __forceinline__ long long gathered_row_of(const CommParams& c, int p, long long l) {
+  return ((l / c.seg) * c.world + p) * c.seg + l % c.seg;
+}
+// 256-row tile ordinal -> tile index: own chunk first (all-gather) or last (reduce-scatter)
+__device__ __forceinline__ int comm_tile_m(const CommParams& c, int o, int tiles_m2, bool own_first) {
+  const int tpc = tiles_m2 / c.world;  // 256-row tiles per chunk
+  const int cp = o / tpc;
+  const int p = (c.rank + (own_first ? 0 : 1) + cp) % c.world;
+  const long long l = static_cast<long long>(o % tpc) * 256;  // local row of the tile's first row
+  return static_cast<int>(gathered_row_of(c, p, l) / 256);
+}
+
+// RS epilogue of one warp's 32 rows x BN columns: push to the owner, or reduce and store.
+template <int BN>
+__device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommParams& c, const CUtensorMap* tmc,
+                                                 uint32_t tmem_acc, long long grow0, int tn, int q, float alpha,
+                                                 uint8_t* bufs, int lane, int& seq, volatile int* abort_flag) {
+  const int chunk = chunk_of_row(c, grow0);
+  const long long lrow0 = local_row_of(c, grow0);
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const long long fidx = ((lrow0 / 128) * tiles_n + tn) * 4 + q;
+  const long long fslot = (c.mc / 128) * tiles_n * 4;  // flags per source rank
+  const int col_base = tn * BN;
+  if (chunk != c.rank) {
+    // the owner entered this call: its receive slot is free
+    bool ok = true;
+    if (lane == 0) ok = wait_flag(&c.arrive_local[chunk], c.seq, true, p.status, kStatusTimeoutPeer, abort_flag);
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+    __nv_bfloat16* dst = c.rs_push[chunk];
+#pragma unroll 1
+    for (int g = 0; g < BN / 64; ++g) {
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32(tmem_acc + g * 64, r0);
+      tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, r1);
+      tmem_ld_wait();
+      const int col0 = col_base + g * 64;
+      if (col0 >= p.N) continue;
+      uint8_t* buf = bufs + (seq & 1) * 4096;
+      if (lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 u;
+        u.x = pack_bf16x2(alpha * __uint_as_float(r0[8 * j]), alpha * __uint_as_float(r0[8 * j + 1]));
+        u.y = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 2]), alpha * __uint_as_float(r0[8 * j + 3]));
+        u.z = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 4]), alpha * __uint_as_float(r0[8 * j + 5]));
+        u.w = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 6]), alpha * __uint_as_float(r0[8 * j + 7]));
+        *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+        u.x = pack_bf16x2(alpha * __uint_as_float(r1[8 * j]), alpha * __uint_as_float(r1[8 * j + 1]));
+        u.y = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 2]), alpha * __uint_as_float(r1[8 * j + 3]));
+        u.z = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 4]), alpha * __uint_as_float(r1[8 * j + 5]));
+        u.w = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 6]), alpha * __uint_as_float(r1[8 * j + 7]));
+        *reinterpret_cast<uint4*>(buf + lane * 128 + (((j + 4) ^ (lane & 7)) << 4)) = u;
+      }
+      __syncwarp();
+      // read back row-contiguously: 8 lanes cover one row's 128 bytes, 4 rows per instruction
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int rr = k * 4 + (lane >> 3);
+        const int j = lane & 7;
+        const long long row = lrow0 + rr;
+        const int col = col0 + j * 8;
+        const uint4 u = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((j ^ (rr & 7)) << 4));
+        if (row < c.mc && col < p.N) *reinterpret_cast<uint4*>(dst + row * p.N + col) = u;
+      }
+      ++seq;
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) st_release_sys(c.rs_flag_peer[chunk] + fidx, c.seq);
+    return true;
+  }
+  // own rows: wait for every peer's partial of these 32 rows, then reduce and store
+  bool ok = true;
+  if (lane == 0) {
+    for (int src = 0; src < c.world && ok; ++src) {
+      if (src == c.rank) continue;
+      ok = wait_flag(c.rs_flag_local + src * fslot + fidx, c.seq, true, p.status, kStatusTimeoutPeer, abort_flag);
+    }
+  }
+  if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+  const long long lrow = lrow0 + lane;
+#pragma unroll 1
+  for (int g = 0; g < BN / 64; ++g) {
+    uint32_t r0[32], r1[32];
+    tmem_ld_32x32b_x32(tmem_acc + g * 64, r0);
+    tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, r1);
+    tmem_ld_wait();
+    const int col0 = col_base + g * 64;
+    if (col0 >= p.N) continue;
+    float v[64];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      v[j] = alpha * __uint_as_float(r0[j]);
+      v[32 + j] = alpha * __uint_as_float(r1[j]);
+    }
+    if (lrow < c.mc && col0 + 64 <= p.N) {
+      for (int src = 0; src < c.world; ++src) {
+        if (src == c.rank) continue;
+        const __nv_bfloat16* rp = c.rs_recv + src * c.mc * p.N + lrow * p.N + col0;
+#pragma unroll
+        for (int j = 0; j < 64; j += 8) {
+          const uint4 u = *reinterpret_cast<const uint4*>(rp + j);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            v[j + 2 * e] += f.x;
+            v[j + 2 * e + 1] += f.y;
+          }
+        }
+      }
+    } else if (lrow < c.mc) {
+      for (int src = 0; src < c.world; ++src) {
+        if (src == c.rank) continue;
+        const __nv_bfloat16* rp = c.rs_recv + src * c.mc * p.N + lrow * p.N + col0;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          if (col0 + j < p.N) v[j] += __bfloat162float(rp[j]);
+        }
+      }
+    }
+    uint8_t* buf = bufs + (seq & 1) * 4096;
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 u;
+      u.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+      u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+      u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+      u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+      *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tmc, buf, col0, static_cast<int>(lrow0), 0);
+      bulk_commit();
+    }
+    ++seq;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------------------------
 // CTA-pair kernel: a cluster of 2 CTAs on 2 SMs computes one 256 x BN tile with tcgen05.mma
 // cta_group::2. CTA r of the pair loads rows [128 r, 128 r + 128) of the A tile and rows
 // [BN/2 r, BN/2 r + BN/2) of the B tile into its own shared memory; the leader (r = 0) issues
@@ -422,15 +604,21 @@ struct Cfg2 {
   // measured alike, so the shared memory goes to a sixth operand stage instead
   static constexpr int kEpiWarps = 4;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
+  static constexpr int kCopyWarps = 2;  // all-gather mode: warps pulling peers' rows
   static constexpr int kStagingBytes = kEpiWarps * 2 * 4096;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
   static_assert(kSmemBytes <= 232448, "shared-memory layout exceeds the per-block opt-in limit");
 };
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
+template <int BN, int COMM>
+constexpr int pair_threads() {
+  return Cfg2<BN>::kThreads + (COMM == 1 ? Cfg2<BN>::kCopyWarps * 32 : 0);
+}
+
+template <int BN, bool A_MN, bool B_MN, int COMM>
+__global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
-                     const __grid_constant__ CUtensorMap tmc, Params p) {
+                     const __grid_constant__ CUtensorMap tmc, Params p, const __grid_constant__ CommParams c) {
   using C_ = Cfg2<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -466,6 +654,14 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, C_::kTmemCols);
+  if (COMM != 0 && blockIdx.x == 0 && threadIdx.x == 64) {
+    // this rank entered call seq: its inputs of the call are in place (stream order) and the buffers
+    // peers write into for this call are no longer read by an earlier call
+    __threadfence_system();
+    for (int q = 0; q < c.world; ++q) {
+      if (q != c.rank) st_release_sys(c.arrive_peer[q] + c.rank, c.seq);
+    }
+  }
   tc_fence_before();
   cluster_sync_all();  // barriers of both CTAs initialized before any cross-CTA signal
   tc_fence_after();
@@ -483,6 +679,7 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
     const int tile = w % tiles;
     const int split = w / tiles;
     tile_coords(tile, tiles_m2, p.tiles_n, tm, tn);
+    if constexpr (COMM != 0) tm = comm_tile_m(c, tm, tiles_m2, COMM == 1);
     kb0 = split * p.kbps;
     nkb = min(kblocks, kb0 + p.kbps) - kb0;
   };
@@ -499,6 +696,16 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
         item(w, bi, tm, tn, kb0, nkb);
         const int m0 = tm * 256 + static_cast<int>(cr) * 128;
         const int n0 = tn * BN + static_cast<int>(cr) * (BN / 2);
+        if constexpr (COMM == 1) {
+          // a peer's rows: wait until a copy warp has landed this 128-row block in our buffer
+          if (chunk_of_row(c, m0) != c.rank) {
+            if (!wait_flag(c.rowflag + m0 / 128, c.seq, false, p.status, kStatusTimeoutPeer, abort_flag)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+          }
+        }
         for (int kb = kb0; kb < kb0 + nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer, abort_flag)) {
             ok = false;
@@ -588,6 +795,39 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
       umma_commit_pair(mapa_shared(mma_done, 0));
       mbar_wait(mma_done, 0, p.status, kStatusTimeoutMma, nullptr);
     }
+  } else if (COMM == 1 && warp >= 2 + C_::kEpiWarps) {
+    // copy warps: pull 128-row blocks of the peers' chunks into our gathered buffer, peers in
+    // rotation order after this rank, blocks in the order the tile schedule consumes them
+    const long long blocks_per_chunk = c.mc / 128;
+    const long long units = (c.world - 1) * blocks_per_chunk;
+    const long long n16 = 128 * c.ag_row_bytes / 16;
+    for (;;) {
+      long long unit = 0;
+      if (lane == 0) unit = static_cast<long long>(atomicAdd(c.claim, 1ull));
+      unit = __shfl_sync(0xffffffffu, unit, 0);
+      if (unit >= units || *abort_flag) break;
+      const int src = (c.rank + 1 + static_cast<int>(unit / blocks_per_chunk)) % c.world;
+      const long long g0 = gathered_row_of(c, src, (unit % blocks_per_chunk) * 128);
+      bool ok = true;
+      if (lane == 0) ok = wait_flag(c.arrive_local + src, c.seq, true, p.status, kStatusTimeoutPeer, abort_flag);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const uint4* from = reinterpret_cast<const uint4*>(c.ag_src[src] + g0 * c.ag_row_bytes);
+      uint4* to = reinterpret_cast<uint4*>(c.ag_dst + g0 * c.ag_row_bytes);
+      for (long long i = lane; i < n16; i += 32 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (i + u * 32 < n16) v[u] = from[i + u * 32];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (i + u * 32 < n16) to[i + u * 32] = v[u];
+        }
+      }
+      fence_proxy_async_global();
+      __syncwarp();
+      if (lane == 0) st_release_gpu(c.rowflag + g0 / 128, c.seq);
+    }
   } else {
     // warp w drains TMEM lane quadrant w % 4 (the lanes a warp may access), columns of half (w - 2) / 4
     const int q = warp & 3;
@@ -608,6 +848,15 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
       int bi, tm, tn, kb0_, nkb_;
       item(w, bi, tm, tn, kb0_, nkb_);
       const int row0 = tm * 256 + static_cast<int>(cr) * 128 + q * 32;
+      if constexpr (COMM == 2) {
+        const bool ok = epilogue_tile_rs<BN>(p, c, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
+                                             row0, tn, q, alpha, bufs, lane, seq, abort_flag);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+        if (!ok) break;
+        continue;
+      }
       epilogue_tile<kCols>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + half * kCols,
                            row0, tn * BN + half * kCols, bi, alpha, f32_out, bufs, lane, seq);
       tc_fence_before();
@@ -627,11 +876,11 @@ __global__ void __launch_bounds__(Cfg2<BN>::kThreads, 1)
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int COMM = 0>
 void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, int sms,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const CommParams& comm = CommParams{}) {
   using C_ = Cfg2<BN>;
-  auto kern = gemm_pair_kernel<BN, A_MN, B_MN>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, COMM>;
   static bool configured[64] = {};
   int dev = 0;
   MINT_CUDA_CHECK(cudaGetDevice(&dev));
@@ -644,7 +893,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
   const int pairs = static_cast<int>(std::min<long long>(tiles, sms / 2));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(C_::kThreads, 1, 1);
+  cfg.blockDim = dim3(pair_threads<BN, COMM>(), 1, 1);
   cfg.dynamicSmemBytes = C_::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -654,7 +903,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  MINT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p));
+  MINT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p, comm));
   count_launch();
 }
 
@@ -818,6 +1067,142 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   }
 #undef MINT_GEMM_DISPATCH
 #undef MINT_GEMM_DISPATCH_PAIR
+}
+
+namespace {
+
+gemm::Params comm_params_base(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, bool b_kmajor, int dev,
+                              int64_t& M, int64_t& N, int64_t& K) {
+  check_contig(A, "A");
+  check_cuda(B, "B");
+  check_contig(C, "C");
+  MINT_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "fused TP GEMM expects 2-D operands");
+  MINT_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16,
+             "fused TP GEMM operands must be bf16");
+  MINT_CHECK(B.stride(1) == 1, "B needs unit inner stride");
+  M = A.size(0);
+  K = A.size(1);
+  N = b_kmajor ? B.size(0) : B.size(1);
+  MINT_CHECK((b_kmajor ? B.size(1) : B.size(0)) == K, "fused TP GEMM K mismatch");
+  MINT_CHECK((K * 2) % 16 == 0 && (N * 2) % 16 == 0, "fused TP GEMM needs K and N multiples of 8");
+  gemm::Params p{};
+  p.C = C.data_ptr();
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.ldc = C.stride(0);
+  p.alpha = 1.f;
+  p.batch = 1;
+  p.splits = 1;
+  p.tiles_m = static_cast<int>((M + 127) / 128);
+  p.tiles_n = static_cast<int>((N + 255) / 256);
+  p.kbps = static_cast<int>((K + gemm::BK - 1) / gemm::BK);
+  p.status = status_ptr(dev);
+  return p;
+}
+
+gemm::CommParams comm_common(int64_t rank, int64_t world, int64_t seg, int64_t seq, int64_t M, const at::Tensor& arrive,
+                             const std::vector<int64_t>& arrive_peers) {
+  MINT_CHECK(world >= 2 && world <= 8 && rank >= 0 && rank < world, "fused TP needs 2..8 ranks");
+  MINT_CHECK(seg % 256 == 0 && M % (seg * world) == 0, "fused TP needs segments of a multiple of 256 rows and M a ",
+             "multiple of segment x world (M=", M, " seg=", seg, " world=", world, ")");
+  MINT_CHECK(static_cast<int64_t>(arrive_peers.size()) == world, "one arrive pointer per rank");
+  check_contig(arrive, "arrive");
+  MINT_CHECK(arrive.scalar_type() == at::kInt && arrive.numel() >= world, "arrive must be int32 [world]");
+  gemm::CommParams c{};
+  c.rank = static_cast<int>(rank);
+  c.world = static_cast<int>(world);
+  c.seg = static_cast<int>(seg);
+  c.seq = static_cast<int>(seq);
+  c.mc = M / world;
+  c.arrive_local = arrive.data_ptr<int>();
+  for (int q = 0; q < world; ++q) c.arrive_peer[q] = reinterpret_cast<int*>(arrive_peers[q]);
+  return c;
+}
+
+}  // namespace
+
+// C[M, N] = A[M, K] @ op(B) with the all-gather of A's rows over the tensor-parallel group fused in:
+// A is this rank's symmetric gathered buffer holding its own chunk; `src_ptrs[p]` is rank p's
+// gathered buffer (the same layout), from which this kernel pulls rank p's chunk over NVLink.
+void gemm_ag(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool b_kmajor, const std::vector<int64_t>& src_ptrs,
+             const at::Tensor& arrive, const std::vector<int64_t>& arrive_peers, at::Tensor& rowflag, at::Tensor& claim,
+             int64_t rank, int64_t world, int64_t seg, int64_t seq) {
+  c10::cuda::CUDAGuard guard(A.device());
+  const int dev = A.get_device();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int64_t M, N, K;
+  gemm::Params p = comm_params_base(A, B, C, b_kmajor, dev, M, N, K);
+  MINT_CHECK(C.size(0) == M && C.size(1) == N, "C must be [M, N]");
+  gemm::CommParams c = comm_common(rank, world, seg, seq, M, arrive, arrive_peers);
+  MINT_CHECK(static_cast<int64_t>(src_ptrs.size()) == world, "one source pointer per rank");
+  for (int q = 0; q < world; ++q) c.ag_src[q] = reinterpret_cast<const uint8_t*>(src_ptrs[q]);
+  c.ag_dst = static_cast<uint8_t*>(A.data_ptr());
+  c.ag_row_bytes = K * 2;
+  check_contig(rowflag, "rowflag");
+  MINT_CHECK(rowflag.scalar_type() == at::kInt && rowflag.numel() >= M / 128, "rowflag must be int32 [M / 128]");
+  check_contig(claim, "claim");
+  MINT_CHECK(claim.scalar_type() == at::kLong && claim.numel() >= 1, "claim must be int64 [1]");
+  c.rowflag = rowflag.data_ptr<int>();
+  c.claim = reinterpret_cast<unsigned long long*>(claim.data_ptr<int64_t>());
+  MINT_CUDA_CHECK(cudaMemsetAsync(c.claim, 0, sizeof(unsigned long long), stream));
+  constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMap ta = make_tmap_3d(A.data_ptr(), BF, 2, K, M, 1, K, M * K, 64, 128, 1, SW128);
+  const uint64_t ldb = B.stride(0);
+  const CUtensorMap tb = b_kmajor ? make_tmap_3d(B.data_ptr(), BF, 2, K, N, 1, ldb, N * ldb, 64, 128, 1, SW128)
+                                  : make_tmap_3d(B.data_ptr(), BF, 2, N, K, 1, ldb, K * ldb, 64, 64, 1, SW128);
+  const CUtensorMap tc = make_tmap_3d(C.data_ptr(), BF, 2, N, M, 1, C.stride(0), M * C.stride(0), 64, 32, 1, SW128);
+  const int sms = num_sms(dev);
+  if (b_kmajor) {
+    gemm::launch_pair<256, false, false, 1>(ta, tb, tc, p, sms, stream, c);
+  } else {
+    gemm::launch_pair<256, false, true, 1>(ta, tb, tc, p, sms, stream, c);
+  }
+}
+
+// out[M / world, N] = this rank's chunk of sum over the group of (A[M, K] @ op(B)): the GEMM with
+// the reduce-scatter of its output rows fused in. `push_ptrs[p]` is rank p's receive slot for this
+// rank ([M / world, N] bf16), `flag_ptrs[p]` rank p's flag block for this rank; `recv` / `flags` are
+// this rank's own receive slots [world, M / world, N] and flags [world, M / world / 128, tiles_n, 4].
+void gemm_rs(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, bool b_kmajor,
+             const std::vector<int64_t>& push_ptrs, const at::Tensor& recv, const std::vector<int64_t>& flag_ptrs,
+             const at::Tensor& flags, const at::Tensor& arrive, const std::vector<int64_t>& arrive_peers, int64_t rank,
+             int64_t world, int64_t seg, int64_t seq) {
+  c10::cuda::CUDAGuard guard(A.device());
+  const int dev = A.get_device();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int64_t M, N, K;
+  gemm::Params p = comm_params_base(A, B, out, b_kmajor, dev, M, N, K);
+  gemm::CommParams c = comm_common(rank, world, seg, seq, M, arrive, arrive_peers);
+  MINT_CHECK(out.size(0) == c.mc && out.size(1) == N && out.stride(0) == N, "out must be contiguous [M / world, N]");
+  check_contig(recv, "recv");
+  MINT_CHECK(recv.scalar_type() == at::kBFloat16 && recv.numel() >= world * c.mc * N, "recv must be bf16 [world, Mc, N]");
+  check_contig(flags, "flags");
+  const int64_t tiles_n = (N + 255) / 256;
+  MINT_CHECK(flags.scalar_type() == at::kInt && flags.numel() >= world * (c.mc / 128) * tiles_n * 4,
+             "flags must be int32 [world, Mc / 128, tiles_n, 4]");
+  MINT_CHECK(static_cast<int64_t>(push_ptrs.size()) == world && static_cast<int64_t>(flag_ptrs.size()) == world,
+             "one push / flag pointer per rank");
+  for (int q = 0; q < world; ++q) {
+    c.rs_push[q] = reinterpret_cast<__nv_bfloat16*>(push_ptrs[q]);
+    c.rs_flag_peer[q] = reinterpret_cast<int*>(flag_ptrs[q]);
+  }
+  c.rs_recv = reinterpret_cast<const __nv_bfloat16*>(recv.data_ptr());
+  c.rs_flag_local = flags.data_ptr<int>();
+  constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMap ta = make_tmap_3d(A.data_ptr(), BF, 2, K, M, 1, A.stride(0), M * A.stride(0), 64, 128, 1, SW128);
+  const uint64_t ldb = B.stride(0);
+  const CUtensorMap tb = b_kmajor ? make_tmap_3d(B.data_ptr(), BF, 2, K, N, 1, ldb, N * ldb, 64, 128, 1, SW128)
+                                  : make_tmap_3d(B.data_ptr(), BF, 2, N, K, 1, ldb, K * ldb, 64, 64, 1, SW128);
+  const CUtensorMap tc = make_tmap_3d(out.data_ptr(), BF, 2, N, c.mc, 1, N, c.mc * N, 64, 32, 1, SW128);
+  const int sms = num_sms(dev);
+  if (b_kmajor) {
+    gemm::launch_pair<256, false, false, 2>(ta, tb, tc, p, sms, stream, c);
+  } else {
+    gemm::launch_pair<256, false, true, 2>(ta, tb, tc, p, sms, stream, c);
+  }
 }
 
 }  // namespace mint
