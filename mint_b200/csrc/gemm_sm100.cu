@@ -427,7 +427,8 @@ struct CommParams {
   __nv_bfloat16* rs_push[8];     // RS: peer p's receive slot for this rank ([Mc, N], rows of chunk p)
   const __nv_bfloat16* rs_recv;  // RS: our receive slots [world][Mc, N]
   int* rs_flag_peer[8];          // RS: peer p's flags for this rank [Mc / 128][tiles_n][4]
-  const int* rs_flag_local;      // RS: our flags [world][Mc / 128][tiles_n][4]
+  const int* rs_flag_local;      // RS: our flags [world][rs_flag_stride], block of source s at s * stride
+  long long rs_flag_stride;      // RS: flags per source rank (>= Mc / 128 * tiles_n * 4)
   long long mc;                  // rows per chunk (M / world)
 };
 
@@ -458,7 +459,6 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
   const long long lrow0 = local_row_of(c, grow0);
   const int tiles_n = (p.N + BN - 1) / BN;
   const long long fidx = ((lrow0 / 128) * tiles_n + tn) * 4 + q;
-  const long long fslot = (c.mc / 128) * tiles_n * 4;  // flags per source rank
   const int col_base = tn * BN;
   if (chunk != c.rank) {
     // the owner entered this call: its receive slot is free
@@ -514,7 +514,8 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
   if (lane == 0) {
     for (int src = 0; src < c.world && ok; ++src) {
       if (src == c.rank) continue;
-      ok = wait_flag(c.rs_flag_local + src * fslot + fidx, c.seq, true, p.status, kStatusTimeoutPeer, abort_flag);
+      ok = wait_flag(c.rs_flag_local + src * c.rs_flag_stride + fidx, c.seq, true, p.status, kStatusTimeoutPeer,
+                     abort_flag);
     }
   }
   if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
@@ -1164,7 +1165,7 @@ void gemm_ag(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool b_kma
 // out[M / world, N] = this rank's chunk of sum over the group of (A[M, K] @ op(B)): the GEMM with
 // the reduce-scatter of its output rows fused in. `push_ptrs[p]` is rank p's receive slot for this
 // rank ([M / world, N] bf16), `flag_ptrs[p]` rank p's flag block for this rank; `recv` / `flags` are
-// this rank's own receive slots [world, M / world, N] and flags [world, M / world / 128, tiles_n, 4].
+// this rank's own receive slots [world, M / world, N] and flag blocks [world, stride].
 void gemm_rs(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, bool b_kmajor,
              const std::vector<int64_t>& push_ptrs, const at::Tensor& recv, const std::vector<int64_t>& flag_ptrs,
              const at::Tensor& flags, const at::Tensor& arrive, const std::vector<int64_t>& arrive_peers, int64_t rank,
@@ -1180,8 +1181,10 @@ void gemm_rs(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, bool b_k
   MINT_CHECK(recv.scalar_type() == at::kBFloat16 && recv.numel() >= world * c.mc * N, "recv must be bf16 [world, Mc, N]");
   check_contig(flags, "flags");
   const int64_t tiles_n = (N + 255) / 256;
-  MINT_CHECK(flags.scalar_type() == at::kInt && flags.numel() >= world * (c.mc / 128) * tiles_n * 4,
-             "flags must be int32 [world, Mc / 128, tiles_n, 4]");
+  MINT_CHECK(flags.scalar_type() == at::kInt && flags.dim() == 2 && flags.size(0) == world &&
+                 flags.size(1) >= (c.mc / 128) * tiles_n * 4,
+             "flags must be int32 [world, >= Mc / 128 * tiles_n * 4]");
+  c.rs_flag_stride = flags.size(1);
   MINT_CHECK(static_cast<int64_t>(push_ptrs.size()) == world && static_cast<int64_t>(flag_ptrs.size()) == world,
              "one push / flag pointer per rank");
   for (int q = 0; q < world; ++q) {

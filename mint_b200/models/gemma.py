@@ -29,6 +29,7 @@ from mint_b200.nn.norm import RMSNorm
 from mint_b200.ops.cross_entropy import lm_head_cross_entropy
 from mint_b200.ops.embedding import embedding
 from mint_b200.ops.linear import linear
+from mint_b200.parallel import fused as fused_tp
 from mint_b200.parallel import tp as tpc
 from mint_b200.utils.logger import logger
 
@@ -134,6 +135,8 @@ class Gemma(nn.Module):
     ) -> torch.Tensor:
         if self._before_forward is not None:
             self._before_forward()
+        if tpc.active(self.tp):
+            fused_tp.begin_forward(self.tp, input_ids.device)
         h = self._embed(input_ids)
         for i, block in enumerate(self.blocks):
             kv_cache = kv_caches[i] if kv_caches is not None else None

@@ -19,6 +19,7 @@ from mint_b200.nn.norm import RMSNorm
 from mint_b200.nn.pos import PosEmbeddings, RoPE
 from mint_b200.ops.linear import linear
 from mint_b200.ops.rope import qk_norm_rope
+from mint_b200.parallel import fused as fused_tp
 from mint_b200.parallel import tp as tpc
 
 
@@ -53,6 +54,16 @@ class GroupedQueryAttention(nn.Module):
             self.pos_embeddings.fused_kind in ("rope", "none")
         )
 
+    def _norm_rope(self, qkv: torch.Tensor, start_pos: int):  # noqa: ANN202
+        """QK-RMSNorm + RoPE on the fused projection ``[B, T, (hq + 2 hkv) * hd]`` -> q, k, v."""
+        pe = self.pos_embeddings
+        cos, sin = pe.tables() if isinstance(pe, RoPE) else (None, None)
+        q, k, v = qk_norm_rope(
+            qkv, self.n_heads, self.n_kv_heads, self.head_dim, self.q_norm.scale, self.k_norm.scale, cos, sin,
+            start_pos=start_pos, eps=self.q_norm.eps,
+        )
+        return q, k, v, None
+
     def _project(self, x: torch.Tensor, dt: torch.dtype, start_pos: int):  # noqa: ANN202
         bsz, seqlen = x.shape[0], x.shape[1]
         hq, hkv, hd = self.n_heads, self.n_kv_heads, self.head_dim
@@ -63,11 +74,7 @@ class GroupedQueryAttention(nn.Module):
                 cos, sin = pe.tables()
             else:
                 cos = sin = None
-            q, k, v = qk_norm_rope(
-                qkv, hq, hkv, hd, self.q_norm.scale, self.k_norm.scale, cos, sin,
-                start_pos=start_pos, eps=self.q_norm.eps,
-            )
-            return q, k, v, None
+            return self._norm_rope(qkv, start_pos)
         q = self.wq(x).view(bsz, seqlen, hq, hd)
         k = self.wk(x).view(bsz, seqlen, hkv, hd)
         v = self.wv(x).view(bsz, seqlen, hkv, hd)
@@ -85,9 +92,17 @@ class GroupedQueryAttention(nn.Module):
         doc_ids: torch.Tensor | None = None,
     ) -> torch.Tensor:
         dt = compute_dtype(x)
-        x = tpc.enter_column_parallel(x, self.tp)
-        bsz, seqlen = x.shape[0], x.shape[1]
-        q, k, v, bias = self._project(x, dt, start_pos)
+        # sequence-parallel TP on CUDA: all-gather -> QKV GEMM and wo GEMM -> reduce-scatter as fused kernels
+        fuse = (kv_cache is None and self._fusable() and type(self.wo) is nn.Linear and dt == torch.bfloat16
+                and fused_tp.enabled(self.tp, x))
+        if fuse:
+            bsz, seqlen = x.shape[0], x.shape[1] * self.tp.size
+            qkv = fused_tp.column_parallel_linear(x, (self.wq.weight, self.wk.weight, self.wv.weight), self.tp)
+            q, k, v, bias = self._norm_rope(qkv, start_pos)
+        else:
+            x = tpc.enter_column_parallel(x, self.tp)
+            bsz, seqlen = x.shape[0], x.shape[1]
+            q, k, v, bias = self._project(x, dt, start_pos)
         if bias is not None and bias.shape[1] != q.shape[2] and self.tp is not None and self.tp.size > 1:
             per = q.shape[2]
             bias = bias[:, self.tp.rank * per : (self.tp.rank + 1) * per]
@@ -97,6 +112,8 @@ class GroupedQueryAttention(nn.Module):
             base_attn_mask=base_attn_mask, doc_ids=doc_ids, bias=bias, start_pos=start_pos,
         )
         out = out.reshape(bsz, seqlen, -1)
+        if fuse:
+            return fused_tp.row_parallel_linear(out, self.wo.weight, self.tp)
         if type(self.wo) is nn.Linear:
             y = linear(out, self.wo.weight, compute_dtype=dt)
         else:

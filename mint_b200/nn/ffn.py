@@ -11,6 +11,7 @@ from torch import nn
 from mint_b200.nn.base import compute_dtype
 from mint_b200.ops.glu import geglu
 from mint_b200.ops.linear import linear
+from mint_b200.parallel import fused as fused_tp
 from mint_b200.parallel import tp as tpc
 
 
@@ -27,6 +28,10 @@ class GLU(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = compute_dtype(x)
+        if self._fusable() and dt == torch.bfloat16 and fused_tp.enabled(self.tp, x):
+            # all-gather -> fc1||fc2 GEMM and fc3 GEMM -> reduce-scatter as fused kernels
+            ab = fused_tp.column_parallel_linear(x, (self.fc1.weight, self.fc2.weight), self.tp)
+            return fused_tp.row_parallel_linear(geglu(ab), self.fc3.weight, self.tp)
         x = tpc.enter_column_parallel(x, self.tp)
         if self._fusable():
             ab = linear(x, self.fc1.weight, self.fc2.weight, compute_dtype=dt)

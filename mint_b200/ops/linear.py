@@ -57,6 +57,35 @@ def _cast_weight(weights: tuple[torch.Tensor, ...], dtype: torch.dtype) -> torch
     return out
 
 
+def weight_grads(weights: tuple[torch.Tensor, ...], want: list[bool], dy2: torch.Tensor,
+                 x2: torch.Tensor) -> list[torch.Tensor | None]:
+    """Gradients of ``y = x @ cat(weights)^T`` w.r.t. each weight from ``dy2 [M, sum N_i]`` and
+    ``x2 [M, K]``. Weights managed by the gradient engine get theirs accumulated straight into their
+    fp32 bucket views (split-K GEMMs, then the engine's ready hook) and return None; the others are
+    returned as tensors."""
+    grads: list[torch.Tensor | None] = [None] * len(weights)
+    fused = [want[i] and _main_grad(w) is not None for i, w in enumerate(weights)]
+    if any(fused):
+        off = 0
+        for i, w in enumerate(weights):
+            rows = w.shape[0]
+            if fused[i]:
+                mg = _main_grad(w)
+                matmul(dy2[:, off : off + rows], x2, trans_a=True, out=mg.view(rows, -1), accumulate=True)
+                w._mint_grad_ready()
+            off += rows
+    if any(want[i] and not fused[i] for i in range(len(weights))):
+        gdtype = weights[0].dtype if weights[0].dtype in (torch.float32, torch.bfloat16) else torch.float32
+        dw = matmul(dy2, x2, trans_a=True, out_dtype=gdtype)
+        off = 0
+        for i, w in enumerate(weights):
+            rows = w.shape[0]
+            if want[i] and not fused[i]:
+                grads[i] = dw[off : off + rows]
+            off += rows
+    return grads
+
+
 class _LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, dtype, *weights):  # noqa: ANN001, ANN205
@@ -88,28 +117,8 @@ class _LinearFn(torch.autograd.Function):
             dx = matmul(dy2, w, out_dtype=ctx.dtype).view(ctx.x_shape)
             if dx.dtype != ctx.x_dtype:
                 dx = dx.to(ctx.x_dtype)
-        grads: list[torch.Tensor | None] = [None] * len(weights)
         want = [ctx.needs_input_grad[2 + i] for i in range(len(weights))]
-        fused = [want[i] and _main_grad(w) is not None for i, w in enumerate(weights)]
-        if any(fused):
-            # weight-gradient GEMMs accumulate straight into the gradient engine's fp32 buckets
-            off = 0
-            for i, w in enumerate(weights):
-                rows = w.shape[0]
-                if fused[i]:
-                    mg = _main_grad(w)
-                    matmul(dy2[:, off : off + rows], x2, trans_a=True, out=mg.view(rows, -1), accumulate=True)
-                    w._mint_grad_ready()
-                off += rows
-        if any(want[i] and not fused[i] for i in range(len(weights))):
-            gdtype = weights[0].dtype if weights[0].dtype in (torch.float32, torch.bfloat16) else torch.float32
-            dw = matmul(dy2, x2, trans_a=True, out_dtype=gdtype)
-            off = 0
-            for i, w in enumerate(weights):
-                rows = w.shape[0]
-                if want[i] and not fused[i]:
-                    grads[i] = dw[off : off + rows]
-                off += rows
+        grads = weight_grads(weights, want, dy2, x2)
         return (dx, None, *grads)
 
 

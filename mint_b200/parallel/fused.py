@@ -1,0 +1,260 @@
+"""Tensor-parallel linears with their collectives fused into the GEMM over NVLink peer memory.
+
+The reference all-gathers the sequence-parallel activation before every column-parallel linear and
+reduce-scatters after every row-parallel one with separate NCCL calls (mint/utils/parallel.py:264-319,
+387-424). Here, on CUDA with symmetric memory, each of these is one sm_100a kernel
+(``mint_b200/csrc/gemm_sm100.cu``, CTA-pair tcgen05 GEMM):
+
+* column-parallel forward -- all-gather -> GEMM: this rank's sequence shard is placed in a symmetric
+  gathered buffer, copy warps of the GEMM pull the peers' shards over NVLink while the tensor cores
+  start on the local rows; the gathered input is kept for the weight gradient;
+  backward -- GEMM -> reduce-scatter for the input gradient, local GEMM for the weight gradient;
+* row-parallel forward -- GEMM -> reduce-scatter: partial output tiles of the peers' rows are pushed
+  into their receive buffers from the epilogue, this rank's rows are reduced in its epilogue;
+  backward -- all-gather of the output gradient -> GEMM for the input gradient, local GEMM for the
+  weight gradient on the gathered output gradient.
+
+Sequence-parallel activations are ``[B, T / tp, d]`` (a shard of every sequence); the gathered
+layout is ``[B, T, d]`` (rows of rank p's shard of sequence b at rows ``b*T + p*T/tp ...``).
+Gradients are those of the NCCL path in ``mint_b200.parallel.tp``; only the transport differs.
+
+Buffers: symmetric allocations (``torch.distributed._symmetric_memory``) are made collectively the
+first time a call of a given index in the forward pass needs them and reused in later steps. Flags
+carry a call sequence number and are never reset; a call touches a peer's buffers of that call only
+after the peer announced it entered the call, which also keeps the two-slot ring of transient
+buffers safe to reuse.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from mint_b200.ops import _ext
+from mint_b200.ops.linear import _cast_weight, weight_grads
+
+
+class _Symm:
+    """One symmetric buffer: the local tensor and every rank's address of it."""
+
+    def __init__(self, nbytes: int, group: Any, device: torch.device) -> None:
+        import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415
+
+        self.nbytes = nbytes
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, group)
+        me = self.handle.buffer_ptrs[self.handle.rank]
+        off = self.buf.data_ptr() - me
+        self.ptrs = [int(p) + off for p in self.handle.buffer_ptrs]
+
+    def view(self, shape: tuple[int, ...], dtype: torch.dtype, offset: int = 0) -> torch.Tensor:
+        n = 1
+        for d in shape:
+            n *= d
+        esz = torch.empty((), dtype=dtype).element_size()
+        assert offset + n * esz <= self.nbytes
+        return self.buf[offset : offset + n * esz].view(dtype).view(shape)
+
+
+class TPComm:
+    """Symmetric buffers, flags and call sequence numbers of one tensor-parallel group."""
+
+    MAX_FLAG_BLOCKS = 1 << 16  # (rows / 128) x column tiles x 4 per source rank
+
+    def __init__(self, group: Any, device: torch.device) -> None:
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = device
+        self.seq = 0
+        # control block: arrive[world] int32, then reduce-scatter flags [world][MAX_FLAG_BLOCKS] int32
+        ctrl_bytes = 256 + self.world * self.MAX_FLAG_BLOCKS * 4
+        self.ctrl = _Symm(ctrl_bytes, group, device)
+        self.arrive = self.ctrl.view((self.world,), torch.int32)
+        self.arrive_ptrs = list(self.ctrl.ptrs)
+        self.rs_flags = self.ctrl.view((self.world * self.MAX_FLAG_BLOCKS,), torch.int32, offset=256)
+        self.rowflag = torch.zeros(1 << 16, dtype=torch.int32, device=device)
+        self.claim = torch.zeros(1, dtype=torch.int64, device=device)
+        self._saved: list[_Symm] = []  # gathered inputs kept for backward, by call index in the pass
+        self._saved_idx = 0
+        self._ring: list[_Symm | None] = [None, None]
+        self._ring_idx = 0
+
+    # -------------------------------------------------------------- buffers
+    def begin_forward(self) -> None:
+        """A new forward pass starts: its saved gathered inputs reuse the previous pass's buffers."""
+        self._saved_idx = 0
+
+    def _saved_buffer(self, nbytes: int) -> _Symm:
+        i = self._saved_idx
+        self._saved_idx += 1
+        if i < len(self._saved) and self._saved[i].nbytes >= nbytes:
+            return self._saved[i]
+        b = _Symm(nbytes, self.group, self.device)  # collective: every rank reaches call i alike
+        if i < len(self._saved):
+            self._saved[i] = b
+        else:
+            self._saved.append(b)
+        return b
+
+    def _ring_buffer(self, nbytes: int) -> _Symm:
+        i = self._ring_idx
+        self._ring_idx ^= 1
+        b = self._ring[i]
+        if b is None or b.nbytes < nbytes:
+            b = _Symm(nbytes, self.group, self.device)
+            self._ring[i] = b
+        return b
+
+    def next_seq(self) -> int:
+        self.seq += 1
+        return self.seq
+
+    # -------------------------------------------------------------- fused GEMMs
+    def gemm_ag(self, gathered: _Symm, rows: int, K: int, w: torch.Tensor, b_kmajor: bool, seg: int) -> torch.Tensor:
+        """``C = gathered[rows, K] @ op(w)`` with the peers' row chunks pulled in by the kernel."""
+        C = _ext.require()
+        A = gathered.view((rows, K), torch.bfloat16)
+        n = w.shape[0] if b_kmajor else w.shape[1]
+        out = torch.empty(rows, n, dtype=torch.bfloat16, device=A.device)
+        C.gemm_ag(A, w, out, b_kmajor, gathered.ptrs, self.arrive, self.arrive_ptrs, self.rowflag, self.claim,
+                  self.rank, self.world, seg, self.next_seq())
+        return out
+
+    def gemm_rs(self, A: torch.Tensor, w: torch.Tensor, b_kmajor: bool, seg: int) -> torch.Tensor:
+        """This rank's rows of ``sum over ranks (A @ op(w))`` (reduce-scatter fused into the GEMM)."""
+        C = _ext.require()
+        rows = A.shape[0]
+        mc = rows // self.world
+        n = w.shape[0] if b_kmajor else w.shape[1]
+        tiles_n = (n + 255) // 256
+        fslot = (mc // 128) * tiles_n * 4
+        if fslot > self.MAX_FLAG_BLOCKS:
+            raise ValueError(f"fused reduce-scatter of {rows} x {n} exceeds the flag block")
+        recv = self._ring_buffer(self.world * mc * n * 2)
+        recv_t = recv.view((self.world, mc, n), torch.bfloat16)
+        slot_bytes = mc * n * 2
+        push = [recv.ptrs[p] + self.rank * slot_bytes for p in range(self.world)]
+        flag_ptrs = [self.ctrl.ptrs[p] + 256 + self.rank * self.MAX_FLAG_BLOCKS * 4 for p in range(self.world)]
+        flags = self.rs_flags.view(self.world, self.MAX_FLAG_BLOCKS)
+        out = torch.empty(mc, n, dtype=torch.bfloat16, device=A.device)
+        C.gemm_rs(A, w, out, b_kmajor, push, recv_t, flag_ptrs, flags, self.arrive, self.arrive_ptrs,
+                  self.rank, self.world, seg, self.next_seq())
+        return out
+
+
+_COMMS: dict[Any, TPComm] = {}
+
+
+def get_comm(group: Any, device: torch.device) -> TPComm:
+    key = (id(group), device.index)
+    comm = _COMMS.get(key)
+    if comm is None:
+        comm = TPComm(group, device)
+        _COMMS[key] = comm
+    return comm
+
+
+# ------------------------------------------------------------------------------------------ autograd
+def _bf16_2d(t: torch.Tensor) -> torch.Tensor:
+    t2 = t.reshape(-1, t.shape[-1])
+    if t2.dtype != torch.bfloat16 or not t2.is_contiguous():
+        t2 = t2.to(torch.bfloat16).contiguous()
+    return t2
+
+
+class _ColumnParallelFn(torch.autograd.Function):
+    """``y [B, T, N/tp] = all_gather_T(x [B, T/tp, K]) @ cat(weights)^T``."""
+
+    @staticmethod
+    def forward(ctx, x, comm, *weights):  # noqa: ANN001, ANN205
+        B, seg, K = x.shape
+        world, rank = comm.world, comm.rank
+        T = seg * world
+        rows = B * T
+        gathered = comm._saved_buffer(rows * K * 2)
+        G = gathered.view((B, world, seg, K), torch.bfloat16)
+        G[:, rank].copy_(x)  # this rank's shard in place; the kernel pulls the others
+        w = _cast_weight(weights, torch.bfloat16)
+        y = comm.gemm_ag(gathered, rows, K, w, True, seg)
+        ctx.comm, ctx.weights, ctx.shape, ctx.x_dtype = comm, weights, (B, seg, K), x.dtype
+        ctx.save_for_backward(gathered.view((rows, K), torch.bfloat16))
+        return y.view(B, T, -1)
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        (G,) = ctx.saved_tensors
+        comm, weights = ctx.comm, ctx.weights
+        B, seg, K = ctx.shape
+        dy2 = _bf16_2d(dy)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            w = _cast_weight(weights, torch.bfloat16)  # [N, K]: op(B) = w read MN-major
+            dx = comm.gemm_rs(dy2, w, False, seg).view(B, seg, K).to(ctx.x_dtype)
+        want = [ctx.needs_input_grad[2 + i] for i in range(len(weights))]
+        grads = weight_grads(weights, want, dy2, G)
+        return (dx, None, *grads)
+
+
+class _RowParallelFn(torch.autograd.Function):
+    """``y [B, T/tp, N] = reduce_scatter_T(x [B, T, K/tp] @ w^T)``."""
+
+    @staticmethod
+    def forward(ctx, x, comm, w):  # noqa: ANN001, ANN205
+        B, T, K = x.shape
+        seg = T // comm.world
+        x2 = _bf16_2d(x)
+        wc = _cast_weight((w,), torch.bfloat16)
+        y = comm.gemm_rs(x2, wc, True, seg)
+        ctx.comm, ctx.w, ctx.shape, ctx.x_dtype = comm, w, (B, T, K), x.dtype
+        ctx.save_for_backward(x2)
+        return y.view(B, seg, -1)
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        (x2,) = ctx.saved_tensors
+        comm, w = ctx.comm, ctx.w
+        B, T, K = ctx.shape
+        world, rank = comm.world, comm.rank
+        seg = T // world
+        n = dy.shape[-1]
+        rows = B * T
+        gathered = comm._ring_buffer(rows * n * 2)
+        G = gathered.view((B, world, seg, n), torch.bfloat16)
+        G[:, rank].copy_(dy)
+        dx = None
+        wc = _cast_weight((w,), torch.bfloat16)  # [N, K/tp] = op(B) read MN-major
+        dy_full = comm.gemm_ag(gathered, rows, n, wc, False, seg) if ctx.needs_input_grad[0] else None
+        if dy_full is not None:
+            dx = dy_full.view(B, T, K).to(ctx.x_dtype)
+        grads = weight_grads((w,), [ctx.needs_input_grad[2]], gathered.view((rows, n), torch.bfloat16), x2)
+        return (dx, None, *grads)
+
+
+def enabled(tp: Any, x: torch.Tensor) -> bool:
+    """Fused collectives apply to CUDA sequence-parallel TP groups whose shards are whole 256-row tiles."""
+    if os.environ.get("MINT_FUSED_TP", "1") == "0" or tp is None or tp.size < 2 or not tp.sp or not x.is_cuda:
+        return False
+    if not _ext.kernels_enabled() or not hasattr(_ext.require(), "gemm_ag"):
+        return False
+    return x.dim() == 3 and x.shape[1] % 256 == 0
+
+
+def column_parallel_linear(x: torch.Tensor, weights: tuple[torch.Tensor, ...], tp: Any) -> torch.Tensor:
+    """Sequence-parallel input ``[B, T/tp, K]`` -> ``[B, T, sum N_i / tp]``."""
+    return _ColumnParallelFn.apply(x, get_comm(tp.group, x.device), *weights)
+
+
+def row_parallel_linear(x: torch.Tensor, w: torch.Tensor, tp: Any) -> torch.Tensor:
+    """``[B, T, K/tp]`` -> sequence-parallel output ``[B, T/tp, N]``."""
+    return _RowParallelFn.apply(x, get_comm(tp.group, x.device), w)
+
+
+def begin_forward(tp: Any, device: torch.device) -> None:
+    comm = _COMMS.get((id(tp.group), device.index)) if tp is not None else None
+    if comm is not None:
+        comm.begin_forward()
