@@ -423,6 +423,7 @@ struct CommParams {
   uint8_t* ag_dst;               // AG: our gathered buffer (the A operand)
   long long ag_row_bytes;        // AG: bytes per row of A
   int* rowflag;                  // AG: [M / 128] local flags (seq when a block landed)
+  int* blockcnt;                 // AG: [M / 128] local piece counters (+kAgPieces per block per call, never reset)
   unsigned long long* claim;     // AG: work counter, zero at launch
   __nv_bfloat16* rs_push[8];     // RS: peer p's receive slot for this rank ([Mc, N], rows of chunk p)
   const __nv_bfloat16* rs_recv;  // RS: our receive slots [world][Mc, N]
@@ -451,10 +452,26 @@ __device__ __forceinline__ int comm_tile_m(const CommParams& c, int o, int tiles
 }
 
 // RS epilogue of one warp's 32 rows x BN columns: push to the owner, or reduce and store.
+constexpr int kRsPend = 16;  // pushed tiles whose flags a warp may hold back before one fence
+
+// Publish the flags of the tiles this warp pushed since its last flush: one system-scope fence
+// orders all their peer stores before the releases.
+__device__ __forceinline__ void rs_flush(const CommParams& c, int* pend, int& npend, int lane) {
+  if (npend == 0) return;
+  __threadfence_system();
+  __syncwarp();
+  if (lane == 0) {
+    for (int i = 0; i < npend; ++i) st_release_sys(c.rs_flag_peer[pend[2 * i]] + pend[2 * i + 1], c.seq);
+  }
+  __syncwarp();
+  npend = 0;
+}
+
 template <int BN>
 __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommParams& c, const CUtensorMap* tmc,
                                                  uint32_t tmem_acc, long long grow0, int tn, int q, float alpha,
-                                                 uint8_t* bufs, int lane, int& seq, volatile int* abort_flag) {
+                                                 uint8_t* bufs, int lane, int& seq, volatile int* abort_flag,
+                                                 int* pend, int& npend) {
   const int chunk = chunk_of_row(c, grow0);
   const long long lrow0 = local_row_of(c, grow0);
   const int tiles_n = (p.N + BN - 1) / BN;
@@ -504,12 +521,17 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
       }
       ++seq;
     }
-    __threadfence_system();
+    if (lane == 0) {
+      pend[2 * npend] = chunk;
+      pend[2 * npend + 1] = static_cast<int>(fidx);
+    }
     __syncwarp();
-    if (lane == 0) st_release_sys(c.rs_flag_peer[chunk] + fidx, c.seq);
+    if (++npend == kRsPend) rs_flush(c, pend, npend, lane);
     return true;
   }
-  // own rows: wait for every peer's partial of these 32 rows, then reduce and store
+  // own rows: publish what this warp pushed (peers may be waiting on it), then wait for every
+  // peer's partial of these 32 rows, reduce and store
+  rs_flush(c, pend, npend, lane);
   bool ok = true;
   if (lane == 0) {
     for (int src = 0; src < c.world && ok; ++src) {
@@ -583,6 +605,8 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
   return true;
 }
 
+constexpr int kAgPieces = 8;  // a 128-row block is copied as 8 pieces of 16 rows by different warps
+
 // ---------------------------------------------------------------------------------------------
 // CTA-pair kernel: a cluster of 2 CTAs on 2 SMs computes one 256 x BN tile with tcgen05.mma
 // cta_group::2. CTA r of the pair loads rows [128 r, 128 r + 128) of the A tile and rows
@@ -600,7 +624,7 @@ struct Cfg2 {
   static constexpr int kBBytes = (BN / 2) * BK * 2;  // this CTA's BN/2 rows of B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kBarrierBytes = 1024;
+  static constexpr int kBarrierBytes = 1024;  // barriers, TMEM slot, abort flag; bytes 256..767 RS flag queues
   // epilogue warps: 4 (one per TMEM lane quadrant) or 8 (two per quadrant, half the columns each);
   // measured alike, so the shared memory goes to a sixth operand stage instead
   static constexpr int kEpiWarps = 4;
@@ -797,37 +821,44 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
       mbar_wait(mma_done, 0, p.status, kStatusTimeoutMma, nullptr);
     }
   } else if (COMM == 1 && warp >= 2 + C_::kEpiWarps) {
-    // copy warps: pull 128-row blocks of the peers' chunks into our gathered buffer, peers in
-    // rotation order after this rank, blocks in the order the tile schedule consumes them
+    // copy warps: pull the peers' chunks into our gathered buffer in 16-row pieces (claimed
+    // dynamically, peers in rotation order after this rank, blocks in the order the tile schedule
+    // consumes them); the warp finishing the last piece of a 128-row block publishes its flag
     const long long blocks_per_chunk = c.mc / 128;
-    const long long units = (c.world - 1) * blocks_per_chunk;
-    const long long n16 = 128 * c.ag_row_bytes / 16;
+    const long long units = (c.world - 1) * blocks_per_chunk * kAgPieces;
+    const long long n16 = 16 * c.ag_row_bytes / 16;  // 16-byte words per piece
     for (;;) {
       long long unit = 0;
       if (lane == 0) unit = static_cast<long long>(atomicAdd(c.claim, 1ull));
       unit = __shfl_sync(0xffffffffu, unit, 0);
       if (unit >= units || *abort_flag) break;
-      const int src = (c.rank + 1 + static_cast<int>(unit / blocks_per_chunk)) % c.world;
-      const long long g0 = gathered_row_of(c, src, (unit % blocks_per_chunk) * 128);
+      const long long blk = unit / kAgPieces;
+      const int piece = static_cast<int>(unit % kAgPieces);
+      const int src = (c.rank + 1 + static_cast<int>(blk / blocks_per_chunk)) % c.world;
+      const long long g0 = gathered_row_of(c, src, (blk % blocks_per_chunk) * 128);
       bool ok = true;
       if (lane == 0) ok = wait_flag(c.arrive_local + src, c.seq, true, p.status, kStatusTimeoutPeer, abort_flag);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      const uint4* from = reinterpret_cast<const uint4*>(c.ag_src[src] + g0 * c.ag_row_bytes);
-      uint4* to = reinterpret_cast<uint4*>(c.ag_dst + g0 * c.ag_row_bytes);
-      for (long long i = lane; i < n16; i += 32 * 8) {
-        uint4 v[8];
+      const long long r0 = g0 + piece * 16;
+      const uint4* from = reinterpret_cast<const uint4*>(c.ag_src[src] + r0 * c.ag_row_bytes);
+      uint4* to = reinterpret_cast<uint4*>(c.ag_dst + r0 * c.ag_row_bytes);
+      for (long long i = lane; i < n16; i += 32 * 16) {
+        uint4 v[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
           if (i + u * 32 < n16) v[u] = from[i + u * 32];
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
           if (i + u * 32 < n16) to[i + u * 32] = v[u];
         }
       }
       fence_proxy_async_global();
       __syncwarp();
-      if (lane == 0) st_release_gpu(c.rowflag + g0 / 128, c.seq);
+      if (lane == 0) {
+        const int old = atom_add_acq_rel_gpu(c.blockcnt + g0 / 128, 1);
+        if ((old + 1) % kAgPieces == 0) st_release_gpu(c.rowflag + g0 / 128, c.seq);
+      }
     }
   } else {
     // warp w drains TMEM lane quadrant w % 4 (the lanes a warp may access), columns of half (w - 2) / 4
@@ -839,6 +870,9 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
     if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
     const bool f32_out = p.c_fp32 || p.atomic_out;
     const uint32_t tempty_leader[2] = {mapa_shared(&tempty[0], 0), mapa_shared(&tempty[1], 0)};
+    // reduce-scatter: flags of pushed tiles held back until a fence (in the barrier region's spare bytes)
+    int* pend = reinterpret_cast<int*>(smem + C_::kStages * C_::kStageBytes + 256) + (warp - 2) * 2 * kRsPend;
+    int npend = 0;
     int t = 0;
     int seq = 0;
     for (int w = pair; w < num_tiles; w += npairs, ++t) {
@@ -851,7 +885,7 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
       const int row0 = tm * 256 + static_cast<int>(cr) * 128 + q * 32;
       if constexpr (COMM == 2) {
         const bool ok = epilogue_tile_rs<BN>(p, c, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
-                                             row0, tn, q, alpha, bufs, lane, seq, abort_flag);
+                                             row0, tn, q, alpha, bufs, lane, seq, abort_flag, pend, npend);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
@@ -864,6 +898,7 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
     }
+    if constexpr (COMM == 2) rs_flush(c, pend, npend, lane);
     if (lane == 0) bulk_wait_all();
     __syncwarp();
   }
@@ -1145,6 +1180,8 @@ void gemm_ag(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool b_kma
   check_contig(claim, "claim");
   MINT_CHECK(claim.scalar_type() == at::kLong && claim.numel() >= 1, "claim must be int64 [1]");
   c.rowflag = rowflag.data_ptr<int>();
+  c.blockcnt = rowflag.data_ptr<int>() + rowflag.numel() / 2;  // second half of the flag tensor
+  MINT_CHECK(rowflag.numel() / 2 >= M / 128, "rowflag must hold 2 x M / 128 int32 (flags, piece counters)");
   c.claim = reinterpret_cast<unsigned long long*>(claim.data_ptr<int64_t>());
   MINT_CUDA_CHECK(cudaMemsetAsync(c.claim, 0, sizeof(unsigned long long), stream));
   constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
