@@ -155,6 +155,136 @@ __global__ void __launch_bounds__(256) add_rmsnorm_bwd_kernel(
   }
 }
 
+// Register-resident variant of add_rmsnorm_bwd_kernel for D = 32 * VPT <= 768 (VPT a multiple of 8): one
+// warp per row, lane l owns columns {l * 8 + 256 * c + e : c < VPT / 8, e < 8}, so every operand is
+// read once with 16-byte vector loads and the scale gradients accumulate in registers across rows.
+template <int VPT>
+__global__ void __launch_bounds__(256) add_rmsnorm_bwd_reg_kernel(
+    const float* __restrict__ dh, const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ a,
+    const float* __restrict__ h, const float* __restrict__ rstd_a, const float* __restrict__ rstd_h,
+    const float* __restrict__ post, const float* __restrict__ pre, float* __restrict__ dres,
+    __nv_bfloat16* __restrict__ da, float* __restrict__ dpost, float* __restrict__ dpre, int rows) {
+  constexpr int D = VPT * 32;
+  constexpr int NC = VPT / 8;  // 8-element chunks per lane
+  __shared__ float s_red[8][2 * D];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float post1[VPT], pre1[VPT], acc_post[VPT], acc_pre[VPT];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = lane * 8 + c * 256 + e;
+      post1[c * 8 + e] = 1.f + post[j];
+      pre1[c * 8 + e] = pre != nullptr ? 1.f + pre[j] : 1.f;
+      acc_post[c * 8 + e] = 0.f;
+      acc_pre[c * 8 + e] = 0.f;
+    }
+  }
+  const int nwarps = blockDim.x >> 5;
+  for (int row = blockIdx.x * nwarps + warp; row < rows; row += gridDim.x * nwarps) {
+    const long long off = static_cast<long long>(row) * D;
+    float g[VPT];  // gradient into h (then the post-norm output gradient)
+    if (dy != nullptr) {
+      float y[VPT], hv[VPT];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const int j = lane * 8 + c * 256;
+        const uint4 u = *reinterpret_cast<const uint4*>(dy + off + j);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(b2[e]);
+          y[c * 8 + 2 * e] = f.x;
+          y[c * 8 + 2 * e + 1] = f.y;
+        }
+        const float4 h0 = *reinterpret_cast<const float4*>(h + off + j);
+        const float4 h1 = *reinterpret_cast<const float4*>(h + off + j + 4);
+        hv[c * 8 + 0] = h0.x; hv[c * 8 + 1] = h0.y; hv[c * 8 + 2] = h0.z; hv[c * 8 + 3] = h0.w;
+        hv[c * 8 + 4] = h1.x; hv[c * 8 + 5] = h1.y; hv[c * 8 + 6] = h1.z; hv[c * 8 + 7] = h1.w;
+      }
+      const float rh = rstd_h[row];
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) dot += y[i] * pre1[i] * hv[i];
+      dot = warp_sum(dot) * (1.f / D);
+      const float k3 = rh * rh * rh * dot;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        g[i] = rh * pre1[i] * y[i] - hv[i] * k3;
+        acc_pre[i] += y[i] * hv[i] * rh;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) g[i] = 0.f;
+    }
+    if (dh != nullptr) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const int j = lane * 8 + c * 256;
+        const float4 d0 = *reinterpret_cast<const float4*>(dh + off + j);
+        const float4 d1 = *reinterpret_cast<const float4*>(dh + off + j + 4);
+        g[c * 8 + 0] += d0.x; g[c * 8 + 1] += d0.y; g[c * 8 + 2] += d0.z; g[c * 8 + 3] += d0.w;
+        g[c * 8 + 4] += d1.x; g[c * 8 + 5] += d1.y; g[c * 8 + 6] += d1.z; g[c * 8 + 7] += d1.w;
+      }
+    }
+    float av[VPT];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int j = lane * 8 + c * 256;
+      *reinterpret_cast<float4*>(dres + off + j) = make_float4(g[c * 8], g[c * 8 + 1], g[c * 8 + 2], g[c * 8 + 3]);
+      *reinterpret_cast<float4*>(dres + off + j + 4) =
+          make_float4(g[c * 8 + 4], g[c * 8 + 5], g[c * 8 + 6], g[c * 8 + 7]);
+      const uint4 u = *reinterpret_cast<const uint4*>(a + off + j);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(b2[e]);
+        av[c * 8 + 2 * e] = f.x;
+        av[c * 8 + 2 * e + 1] = f.y;
+      }
+    }
+    const float ra = rstd_a[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) dot += g[i] * post1[i] * av[i];
+    dot = warp_sum(dot) * (1.f / D);
+    const float k3 = ra * ra * ra * dot;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      uint4 o;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i0 = c * 8 + 2 * e, i1 = i0 + 1;
+        w[e] = pack_bf16x2(ra * post1[i0] * g[i0] - av[i0] * k3, ra * post1[i1] * g[i1] - av[i1] * k3);
+        acc_post[i0] += g[i0] * av[i0] * ra;
+        acc_post[i1] += g[i1] * av[i1] * ra;
+      }
+      *reinterpret_cast<uint4*>(da + off + lane * 8 + c * 256) = o;
+    }
+  }
+  // column sums over this block's warps, then one atomic per column
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = lane * 8 + c * 256 + e;
+      s_red[warp][j] = acc_post[c * 8 + e];
+      s_red[warp][D + j] = acc_pre[c * 8 + e];
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float tp = 0.f, tq = 0.f;
+    for (int w = 0; w < nwarps; ++w) {
+      tp += s_red[w][j];
+      tq += s_red[w][D + j];
+    }
+    atomicAdd(&dpost[j], tp);
+    if (dpre != nullptr) atomicAdd(&dpre[j], tq);
+  }
+}
+
 // One warp per (token, head) row of q or k; v heads are copied. Rows ordered token-major.
 // qkv [M, (Hq + 2 Hkv) * Dh]; q [M, Hq, Dh]; k, v [M, Hkv, Dh]. Position of token m = start + (m % T).
 __global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
@@ -554,6 +684,26 @@ std::vector<at::Tensor> add_rmsnorm_bwd(const c10::optional<at::Tensor>& dh, con
   }
   const float* dh_p = (dh.has_value() && dh->defined()) ? dh->data_ptr<float>() : nullptr;
   const bool has_dy = dy.has_value() && dy->defined() && has_pre;
+  if ((!has_dy || dy->scalar_type() == at::kBFloat16) && D % 256 == 0 && D <= 768) {
+    // register-resident kernel: 8 warps per block, ~2 blocks per SM
+    const int grid_r = std::min<int>((rows + 7) / 8, num_sms(h.get_device()) * 2);
+#define MINT_ARN_BWD_REG(VPT)                                                                                   \
+  add_rmsnorm_bwd_reg_kernel<VPT><<<grid_r, 256, 0, st>>>(                                                     \
+      dh_p, has_dy ? reinterpret_cast<const __nv_bfloat16*>(dy->data_ptr()) : nullptr,                          \
+      reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()), h.data_ptr<float>(), rstd_a.data_ptr<float>(),      \
+      has_pre ? rstd_h.data_ptr<float>() : nullptr, post.data_ptr<float>(), has_pre ? pre->data_ptr<float>() : nullptr, \
+      dres.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(da.data_ptr()), dpost.data_ptr<float>(),         \
+      has_pre ? dpre.data_ptr<float>() : nullptr, rows)
+    switch (D / 32) {
+      case 8: MINT_ARN_BWD_REG(8); break;
+      case 16: MINT_ARN_BWD_REG(16); break;
+      default: MINT_ARN_BWD_REG(24); break;
+    }
+#undef MINT_ARN_BWD_REG
+    MINT_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+    return {dres, da, dpost, dpre};
+  }
   if (!has_dy || dy->scalar_type() == at::kBFloat16) {
     add_rmsnorm_bwd_kernel<__nv_bfloat16><<<grid, nw * 32, sm, st>>>(
         dh_p, has_dy ? reinterpret_cast<const __nv_bfloat16*>(dy->data_ptr()) : nullptr,

@@ -164,3 +164,23 @@ def test_adamw_kernel():
         pc.add_(mc / denom, alpha=-(0.01 / (1 - 0.8**step)))
     assert (p.cpu() - pc).abs().max() < 1e-5
     assert math.isfinite(p.sum().item())
+
+
+@pytest.mark.parametrize("D", [256, 768, 1024])
+def test_add_rmsnorm_without_pre(D):
+    """h = res + rmsnorm(a) only (the block's post-FFN residual): register-resident backward for
+    D <= 768, the general kernel above."""
+    torch.manual_seed(2)
+    res = torch.randn(300, D, device="cuda", requires_grad=True)
+    a = torch.randn(300, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    post = (0.1 * torch.randn(D, device="cuda")).requires_grad_()
+    h, _ = add_rmsnorm(res, a, post, None)
+    gh = torch.randn_like(h)
+    (h * gh).sum().backward()
+    out = [t.grad.clone() for t in (res, a, post)]
+    r2, a2 = res.detach().clone().requires_grad_(), a.detach().float().clone().requires_grad_()
+    p2 = post.detach().clone().requires_grad_()
+    h2 = r2 + rms_ref(a2, p2)
+    (h2 * gh).sum().backward()
+    for got, want in zip(out, (r2.grad, a2.grad, p2.grad)):
+        assert ((got.float() - want).norm() / want.norm()) < 2e-2
