@@ -285,6 +285,81 @@ __global__ void __launch_bounds__(256) add_rmsnorm_bwd_reg_kernel(
   }
 }
 
+// Register-resident rmsnorm_bwd for fp32 x, bf16 dy, fp32 dx and D = 32 * VPT <= 768 (VPT a
+// multiple of 8): one warp per row, lane l owns columns {l * 8 + 256 * c + e}, 16-byte vector loads,
+// each operand read once, the scale gradient accumulated in registers across rows.
+template <int VPT>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                              const float* __restrict__ x,
+                                                              const float* __restrict__ rstd,
+                                                              const float* __restrict__ scale, float* __restrict__ dx,
+                                                              float* __restrict__ dscale, int rows) {
+  constexpr int D = VPT * 32;
+  constexpr int NC = VPT / 8;
+  __shared__ float s_red[8][D];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float w1[VPT], acc[VPT];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      w1[c * 8 + e] = 1.f + scale[lane * 8 + c * 256 + e];
+      acc[c * 8 + e] = 0.f;
+    }
+  }
+  const int nwarps = blockDim.x >> 5;
+  for (int row = blockIdx.x * nwarps + warp; row < rows; row += gridDim.x * nwarps) {
+    const long long off = static_cast<long long>(row) * D;
+    float g[VPT], xv[VPT];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int j = lane * 8 + c * 256;
+      const uint4 u = *reinterpret_cast<const uint4*>(dy + off + j);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(b2[e]);
+        g[c * 8 + 2 * e] = f.x;
+        g[c * 8 + 2 * e + 1] = f.y;
+      }
+      const float4 x0 = *reinterpret_cast<const float4*>(x + off + j);
+      const float4 x1 = *reinterpret_cast<const float4*>(x + off + j + 4);
+      xv[c * 8 + 0] = x0.x; xv[c * 8 + 1] = x0.y; xv[c * 8 + 2] = x0.z; xv[c * 8 + 3] = x0.w;
+      xv[c * 8 + 4] = x1.x; xv[c * 8 + 5] = x1.y; xv[c * 8 + 6] = x1.z; xv[c * 8 + 7] = x1.w;
+    }
+    const float r = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) dot += g[i] * w1[i] * xv[i];
+    dot = warp_sum(dot) * (1.f / D);
+    const float k3 = r * r * r * dot;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float d[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = c * 8 + e;
+        d[e] = r * w1[i] * g[i] - xv[i] * k3;
+        acc[i] += g[i] * xv[i] * r;
+      }
+      const int j = lane * 8 + c * 256;
+      *reinterpret_cast<float4*>(dx + off + j) = make_float4(d[0], d[1], d[2], d[3]);
+      *reinterpret_cast<float4*>(dx + off + j + 4) = make_float4(d[4], d[5], d[6], d[7]);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s_red[warp][lane * 8 + c * 256 + e] = acc[c * 8 + e];
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float t = 0.f;
+    for (int w = 0; w < nwarps; ++w) t += s_red[w][j];
+    atomicAdd(&dscale[j], t);
+  }
+}
+
 // One warp per (token, head) row of q or k; v heads are copied. Rows ordered token-major.
 // qkv [M, (Hq + 2 Hkv) * Dh]; q [M, Hq, Dh]; k, v [M, Hkv, Dh]. Position of token m = start + (m % T).
 __global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
@@ -608,6 +683,22 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, c
       reinterpret_cast<const TDY*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), rstd.data_ptr<float>(), \
       scale.data_ptr<float>(), reinterpret_cast<TDX*>(dx.data_ptr()), dscale.data_ptr<float>(), rows, D)
   const bool xf = x.scalar_type() == at::kFloat, dyf = dy.scalar_type() == at::kFloat, dxf = dx_dt == at::kFloat;
+  if (xf && !dyf && dxf && D % 256 == 0 && D <= 768) {
+    const int grid_r = std::min<int>((rows + 7) / 8, num_sms(x.get_device()) * 2);
+#define MINT_RMS_BWD_REG(VPT)                                                                                       \
+  rmsnorm_bwd_reg_kernel<VPT><<<grid_r, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),        \
+                                                      x.data_ptr<float>(), rstd.data_ptr<float>(), scale.data_ptr<float>(), \
+                                                      dx.data_ptr<float>(), dscale.data_ptr<float>(), rows)
+    switch (D / 32) {
+      case 8: MINT_RMS_BWD_REG(8); break;
+      case 16: MINT_RMS_BWD_REG(16); break;
+      default: MINT_RMS_BWD_REG(24); break;
+    }
+#undef MINT_RMS_BWD_REG
+    MINT_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+    return {dx, dscale};
+  }
   if (xf && dyf && dxf) LAUNCH(float, float, float);
   else if (xf && !dyf && dxf) LAUNCH(float, __nv_bfloat16, float);
   else if (!xf && !dyf && !dxf) LAUNCH(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
