@@ -121,7 +121,8 @@ __device__ __forceinline__ void load_row64(uint32_t taddr, float (&x)[64]) {
 
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo, BwdParams p) {
+                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                  const __grid_constant__ CUtensorMap tdq, BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -314,7 +315,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 64; ++c) x[c] = exp2f(x[c] * p.scale_log2 - lse2[c]);
       }
-      // the shared P/dS tile is free: dK_{i-1} / dQ_{i-1} (dq_full_{i-1}) finished reading dS_{i-1}
+      // the shared P/dS tile is free: dK_{i-1} / dQ_{i-1} (dq_full_{i-1}) finished reading dS_{i-1}, and
+      // this warp's dQ_{i-1} reduce-adds (staged in the same bytes it now writes) read their source
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
       store_half_row_sw128(s.pds, half, r, x);
       fence_proxy_async_smem();
       tc_fence_before();
@@ -344,26 +348,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&s.ds_ready);
       if (!(ok = mbar_wait_warp(&s.dq_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       tc_fence_after();
-      // dQ rows: TMEM lane = query index within the tile; this warp drains 64 of the 128 head dims
-      const int qi = q0 + r;
-      float* dst = p.dq_acc + ((static_cast<long long>(b) * p.T + (qi < p.T ? qi : 0)) * p.Hq + h) * kD + cb;
+      // dQ rows: TMEM lane = query index within the tile; this warp drains 64 of the 128 head dims.
+      // The P/dS tile is free now (the dK / dQ MMAs that read dS completed): each warp stages its
+      // 32 rows x 32 columns of dQ in its own 4 KB of it (the bytes it writes P rows into) and
+      // reduce-adds them into the fp32 accumulator with one TMA bulk reduction per box.
+      uint8_t* stage = s.pds + (warp - 4) * 4096;
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t u[32];
         tmem_ld_32x32b_x32(t_dq + lane_off + cb + c2 * 32, u);
         tmem_ld_wait();
-        if (qi < p.T) {
+        if (c2 > 0 && lane == 0) bulk_wait_read<0>();  // the first box's reduction read the stage
+        __syncwarp();
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            red_add_v4(dst + c2 * 32 + e, __uint_as_float(u[e]) * p.scale, __uint_as_float(u[e + 1]) * p.scale,
-                       __uint_as_float(u[e + 2]) * p.scale, __uint_as_float(u[e + 3]) * p.scale);
-          }
+        for (int j = 0; j < 8; ++j) {
+          *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(u[4 * j]) * p.scale, __uint_as_float(u[4 * j + 1]) * p.scale,
+                          __uint_as_float(u[4 * j + 2]) * p.scale, __uint_as_float(u[4 * j + 3]) * p.scale);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_4d(&tdq, stage, cb + c2 * 32, h, q0 + q * 32, b);  // rows past T are clipped
+          bulk_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.dq_free);
     }
+    if (lane == 0) bulk_wait_all();  // dQ reductions done before the shared memory is released
+    __syncwarp();
     // dK / dV rows: TMEM lane = key index (tcgen05.ld is warp-collective: every lane loads)
     ok = __all_sync(0xffffffffu, ok);
     const bool key_ok = kj < p.T;
@@ -444,6 +459,15 @@ __global__ void fa_cast_kernel(const float* __restrict__ src, __nv_bfloat16* __r
 
 }  // namespace fab
 
+// fp32 dQ accumulator [B, T, Hq, 128] as a 4-D TMA map {d, h, t, b}: reduce-add boxes of 32 rows
+// (consecutive t of one head) x 32 dims, clipped at the end of each sequence.
+static CUtensorMap dq_acc_map(float* dq_acc, int B, int T, int Hq) {
+  const uint64_t dims[4] = {128, static_cast<uint64_t>(Hq), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
+  const uint64_t strides[3] = {128, static_cast<uint64_t>(Hq) * 128, static_cast<uint64_t>(T) * Hq * 128};
+  const uint32_t box[4] = {32, 1, 32, 1};
+  return make_tmap_4d(dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
@@ -499,6 +523,7 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                              static_cast<uint64_t>(H) * fab::kD, 64, 1, 128, true);
   };
   const CUtensorMap tq = map(q, Hq), tk = map(k, Hkv), tv = map(v, Hkv), tdo = map(dout, Hq);
+  const CUtensorMap tdq = dq_acc_map(dq_acc.data_ptr<float>(), B, T, Hq);
   const int smem = static_cast<int>(sizeof(fab::Smem)) + 1024;
   static const bool trace = std::getenv("MINT_TRACE_LAUNCH") != nullptr;
   auto step = [&](const char* what) {
@@ -525,7 +550,7 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   }
   dim3 grid((T + fab::kB - 1) / fab::kB, Hkv, B);
   step("before main kernel");
-  fab::fa_bwd_kernel<<<grid, fab::kThreads, smem, stream>>>(tq, tk, tv, tdo, p);
+  fab::fa_bwd_kernel<<<grid, fab::kThreads, smem, stream>>>(tq, tk, tv, tdo, tdq, p);
   step("after main kernel launch");
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
@@ -567,8 +592,9 @@ void flash_attn_bwd_launch_raw(const FlashBwdRaw& a, cudaStream_t stream) {
     return make_tmap_3d_bf16(base, fab::kD, H, bt, fab::kD, static_cast<uint64_t>(H) * fab::kD, 64, 1, 128, true);
   };
   const CUtensorMap tq = map(a.q, a.Hq), tk = map(a.k, a.Hkv), tv = map(a.v, a.Hkv), tdo = map(a.dout, a.Hq);
+  const CUtensorMap tdq = dq_acc_map(a.dq_acc, a.B, a.T, a.Hq);
   dim3 grid((a.T + fab::kB - 1) / fab::kB, a.Hkv, a.B);
-  fab::fa_bwd_kernel<<<grid, fab::kThreads, flash_attn_bwd_smem_bytes(), stream>>>(tq, tk, tv, tdo, p);
+  fab::fa_bwd_kernel<<<grid, fab::kThreads, flash_attn_bwd_smem_bytes(), stream>>>(tq, tk, tv, tdo, tdq, p);
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
   const long long n4 = rows * fab::kD / 4;

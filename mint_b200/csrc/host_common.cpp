@@ -138,4 +138,23 @@ CUtensorMap make_tmap_3d(const void* base, int dtype, int esize, uint64_t d0, ui
   return map;
 }
 
+CUtensorMap make_tmap_4d(const void* base, int dtype, int esize, const uint64_t (&dims)[4], const uint64_t (&strides)[3],
+                         const uint32_t (&box)[4], int swizzle) {
+  MINT_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  CUtensorMap map;
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t st[3];
+  for (int i = 0; i < 3; ++i) {
+    MINT_CHECK((strides[i] * esize) % 16 == 0, "TMA strides must be multiples of 16 bytes");
+    st[i] = strides[i] * esize;
+  }
+  cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&map, static_cast<CUtensorMapDataType>(dtype), 4, const_cast<void*>(base), d, st, bx, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, static_cast<CUtensorMapSwizzle>(swizzle),
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MINT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (4d) failed (", static_cast<int>(r), ")");
+  return map;
+}
+
 }  // namespace mint

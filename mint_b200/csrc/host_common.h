@@ -43,6 +43,10 @@ CUtensorMap make_tmap_2d(const void* base, int dtype, int esize, uint64_t rows, 
 CUtensorMap make_tmap_3d(const void* base, int dtype, int esize, uint64_t d0, uint64_t d1, uint64_t d2,
                          uint64_t stride1, uint64_t stride2, uint32_t box0, uint32_t box1, uint32_t box2, int swizzle);
 
+// 4-D tensor map of any dtype: dims (innermost first), strides in elements for dims 1..3.
+CUtensorMap make_tmap_4d(const void* base, int dtype, int esize, const uint64_t (&dims)[4], const uint64_t (&strides)[3],
+                         const uint32_t (&box)[4], int swizzle);
+
 int num_sms(int device);
 
 // Raise a clear error when a kernel's dynamic shared memory exceeds the device's per-block opt-in
