@@ -114,6 +114,21 @@ class Gemma(nn.Module):
                     nn.init.normal_(p, std=self.config.init_std)
 
     # ------------------------------------------------------------------ forward pieces
+    def _chainable(self) -> bool:
+        """Blocks can pass the next norm's output along (see GQAGluBlock.forward_chain): plain blocks
+        and norms without a shift, residual stream in fp32, parameters not sharded by ZeRO-3."""
+        eng = getattr(self, "_grad_engine", None)
+        if eng is not None and eng.level == 3 and eng.dp > 1:
+            return False  # ZeRO-3 materializes a block's parameters only inside that block's own call
+        norms = [self.norm] + [n for b in self.blocks if type(b) is GQAGluBlock
+                               for n in (b.pre_attn_norm, b.post_attn_norm, b.pre_ffn_norm, b.post_ffn_norm)]
+        return (
+            len(self.blocks) > 0
+            and all(type(b) is GQAGluBlock for b in self.blocks)
+            and all(getattr(n, "shift", None) is None for n in norms)
+            and self.tok_embeddings.weight.dtype == torch.float32
+        )
+
     def _embed(self, input_ids: torch.Tensor) -> torch.Tensor:
         tp = self.tp
         w = self.tok_embeddings.weight
@@ -138,6 +153,23 @@ class Gemma(nn.Module):
         if tpc.active(self.tp):
             fused_tp.begin_forward(self.tp, input_ids.device)
         h = self._embed(input_ids)
+        if kv_caches is None and self._chainable():
+            # each block's closing residual-add kernel also applies the following norm
+            blocks = list(self.blocks)
+            xn = blocks[0].pre_attn_norm(h, out_dtype=compute_dtype(h))
+            for i, block in enumerate(blocks):
+                nxt = blocks[i + 1].pre_attn_norm if i + 1 < len(blocks) else self.norm
+                kwargs = {"start_pos": start_pos, "base_attn_mask": attn_mask, "doc_ids": doc_ids, "xn": xn,
+                          "next_norm": nxt, "chain": True}
+                if self.gradient_checkpointing and self.training:
+                    h, xn = checkpoint(block, h, use_reentrant=False, **kwargs)
+                else:
+                    h, xn = block(h, **kwargs)
+            hn = xn
+            tp = self.tp
+            if tpc.active(tp):
+                hn = tpc.gather_seq(hn, tp) if tp.sp else tpc.copy_to_tp(hn, tp)
+            return hn
         for i, block in enumerate(self.blocks):
             kv_cache = kv_caches[i] if kv_caches is not None else None
             kwargs = {"kv_cache": kv_cache, "start_pos": start_pos, "base_attn_mask": attn_mask, "doc_ids": doc_ids}

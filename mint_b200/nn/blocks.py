@@ -73,7 +73,12 @@ class GQAGluBlock(nn.Module):
         start_pos: int = 0,
         base_attn_mask: torch.Tensor | None = None,
         doc_ids: torch.Tensor | None = None,
-    ) -> torch.Tensor:
+        xn: torch.Tensor | None = None,
+        next_norm: RMSNorm | None = None,
+        chain: bool = False,
+    ) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+        if chain:
+            return self.forward_chain(x, xn, next_norm, start_pos, base_attn_mask, doc_ids)
         dt = compute_dtype(x)
         h = self.pre_attn_norm(x, out_dtype=dt)
         a = self.gqa(h, kv_cache=kv_cache, start_pos=start_pos, base_attn_mask=base_attn_mask, doc_ids=doc_ids)
@@ -82,3 +87,24 @@ class GQAGluBlock(nn.Module):
         f = self.ffn(hn)
         out, _ = add_rmsnorm(h, f, self.post_ffn_norm.scale, None, eps=self.post_ffn_norm.eps)
         return out
+
+    def forward_chain(
+        self,
+        x: torch.Tensor,
+        xn: torch.Tensor,
+        next_norm: RMSNorm | None,
+        start_pos: int = 0,
+        base_attn_mask: torch.Tensor | None = None,
+        doc_ids: torch.Tensor | None = None,
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """``forward`` with the pre-attention norm of this block's input already applied (``xn``) and
+        the norm that follows the block (the next block's pre-attention norm, or the model's final
+        norm) folded into the closing residual-add kernel. Returns ``(out, next_norm(out))``: every
+        residual tensor then feeds one fused op, so its gradient needs no separate accumulation."""
+        dt = compute_dtype(x)
+        a = self.gqa(xn, kv_cache=None, start_pos=start_pos, base_attn_mask=base_attn_mask, doc_ids=doc_ids)
+        h, hn = add_rmsnorm(x, a, self.post_attn_norm.scale, self.pre_ffn_norm.scale,
+                            eps=self.post_attn_norm.eps, y_dtype=dt)
+        f = self.ffn(hn)
+        return add_rmsnorm(h, f, self.post_ffn_norm.scale, next_norm.scale if next_norm is not None else None,
+                           eps=self.post_ffn_norm.eps, y_dtype=dt)

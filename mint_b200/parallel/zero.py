@@ -515,8 +515,13 @@ class GradEngine:
             def post(_m, _args, out, grp=grp):  # noqa: ANN001, ANN202
                 if grp not in self._in_backward:  # a recompute inside backward keeps the params
                     self.free_group(grp)
-                if torch.is_grad_enabled() and isinstance(out, torch.Tensor) and out.requires_grad:
-                    return _BackwardGather.apply(out, self, grp)
+                if not torch.is_grad_enabled():
+                    return out
+                if isinstance(out, torch.Tensor):
+                    return _BackwardGather.apply(out, self, grp) if out.requires_grad else out
+                if isinstance(out, tuple):  # every output re-gathers before the block's backward
+                    return tuple(_BackwardGather.apply(o, self, grp) if isinstance(o, torch.Tensor) and o.requires_grad
+                                 else o for o in out)
                 return out
 
             blk.register_forward_pre_hook(pre)
