@@ -410,10 +410,6 @@ __global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
 
 // head_dim 128 specialization: lane l owns elements 4l..4l+3 (8-byte accesses); the rotation
 // partner (j +- 64) lives in lane l ^ 16.
-// head_dim 128: each warp handles kQkRows consecutive (token, head) rows, lane l owning elements
-// 4l .. 4l+3; all rows' loads are issued before any arithmetic so a warp keeps 1 KB in flight.
-constexpr int kQkRows = 4;
-
 __global__ void __launch_bounds__(256) qk_norm_rope_fwd128_kernel(
     const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ qs, const float* __restrict__ ks,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ q,
@@ -422,55 +418,43 @@ __global__ void __launch_bounds__(256) qk_norm_rope_fwd128_kernel(
   constexpr int Dh = 128;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = Hq + 2 * Hkv;
-  const long long total = static_cast<long long>(M) * H;
-  const long long item0 = (static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp) * kQkRows;
-  uint2 raw[kQkRows];
-#pragma unroll
-  for (int i = 0; i < kQkRows; ++i) {
-    if (item0 + i < total) raw[i] = *reinterpret_cast<const uint2*>(qkv + (item0 + i) * Dh + lane * 4);
+  const long long item = static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp;
+  if (item >= static_cast<long long>(M) * H) return;
+  const int m = static_cast<int>(item / H);
+  const int hh = static_cast<int>(item % H);
+  const uint2 raw = *reinterpret_cast<const uint2*>(qkv + item * Dh + lane * 4);
+  if (hh >= Hq + Hkv) {
+    *reinterpret_cast<uint2*>(v + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh + lane * 4) = raw;
+    return;
   }
-  const float4 scq = *reinterpret_cast<const float4*>(qs + lane * 4);
-  const float4 sck = *reinterpret_cast<const float4*>(ks + lane * 4);
+  const bool is_q = hh < Hq;
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  const float2 x01 = __bfloat1622float2(h2[0]), x23 = __bfloat1622float2(h2[1]);
+  float x[4] = {x01.x, x01.y, x23.x, x23.y};
+  const float r = rsqrtf(warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]) / Dh + eps);
+  const float4 sc = *reinterpret_cast<const float4*>((is_q ? qs : ks) + lane * 4);
+  x[0] *= r * (1.f + sc.x);
+  x[1] *= r * (1.f + sc.y);
+  x[2] *= r * (1.f + sc.z);
+  x[3] *= r * (1.f + sc.w);
+  float o[4] = {x[0], x[1], x[2], x[3]};
+  if (use_rope) {
+    const int pos = start + (m % T);
+    const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
+    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
-  for (int i = 0; i < kQkRows; ++i) {
-    const long long item = item0 + i;
-    if (item >= total) break;  // warp-uniform
-    const int m = static_cast<int>(item / H);
-    const int hh = static_cast<int>(item % H);
-    if (hh >= Hq + Hkv) {
-      *reinterpret_cast<uint2*>(v + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh + lane * 4) = raw[i];
-      continue;
+    for (int e = 0; e < 4; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+      o[e] = lane < 16 ? x[e] * cc[e] - partner * ss[e] : partner * ss[e] + x[e] * cc[e];
     }
-    const bool is_q = hh < Hq;
-    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
-    const float2 x01 = __bfloat1622float2(h2[0]), x23 = __bfloat1622float2(h2[1]);
-    float x[4] = {x01.x, x01.y, x23.x, x23.y};
-    const float r = rsqrtf(warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]) / Dh + eps);
-    const float4 sc = is_q ? scq : sck;
-    x[0] *= r * (1.f + sc.x);
-    x[1] *= r * (1.f + sc.y);
-    x[2] *= r * (1.f + sc.z);
-    x[3] *= r * (1.f + sc.w);
-    float o[4] = {x[0], x[1], x[2], x[3]};
-    if (use_rope) {
-      const int pos = start + (m % T);
-      const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-      const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
-        o[e] = lane < 16 ? x[e] * cc[e] - partner * ss[e] : partner * ss[e] + x[e] * cc[e];
-      }
-    }
-    uint2 out;
-    out.x = pack_bf16x2(o[0], o[1]);
-    out.y = pack_bf16x2(o[2], o[3]);
-    __nv_bfloat16* dst =
-        is_q ? q + (static_cast<long long>(m) * Hq + hh) * Dh : k + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh;
-    *reinterpret_cast<uint2*>(dst + lane * 4) = out;
-    if (lane == 0) (is_q ? rq : rk)[static_cast<long long>(m) * (is_q ? Hq : Hkv) + (is_q ? hh : hh - Hq)] = r;
   }
+  uint2 out;
+  out.x = pack_bf16x2(o[0], o[1]);
+  out.y = pack_bf16x2(o[2], o[3]);
+  __nv_bfloat16* dst = is_q ? q + (static_cast<long long>(m) * Hq + hh) * Dh : k + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh;
+  *reinterpret_cast<uint2*>(dst + lane * 4) = out;
+  if (lane == 0) (is_q ? rq : rk)[static_cast<long long>(m) * (is_q ? Hq : Hkv) + (is_q ? hh : hh - Hq)] = r;
 }
 
 __global__ void __launch_bounds__(256) qk_norm_rope_bwd128_kernel(
@@ -480,83 +464,66 @@ __global__ void __launch_bounds__(256) qk_norm_rope_bwd128_kernel(
     const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dqs,
     float* __restrict__ dks, int M, int T, int Hq, int Hkv, int start, int use_rope) {
   constexpr int Dh = 128;
+  __shared__ float s_acc[kRowsPerBlock][2][Dh];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float accq[4] = {0.f, 0.f, 0.f, 0.f}, acck[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    s_acc[warp][0][lane * 4 + e] = 0.f;
+    s_acc[warp][1][lane * 4 + e] = 0.f;
+  }
   const int H = Hq + 2 * Hkv;
   const long long total = static_cast<long long>(M) * H;
   const float4 scq = *reinterpret_cast<const float4*>(qs + lane * 4);
   const float4 sck = *reinterpret_cast<const float4*>(ks + lane * 4);
-  const long long stride = static_cast<long long>(gridDim.x) * kRowsPerBlock;
-  for (long long base = static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp; base < total;
-       base += stride * kQkRows) {
-    uint2 graw[kQkRows], xraw[kQkRows];
-    // loads of all rows first
-#pragma unroll
-    for (int i = 0; i < kQkRows; ++i) {
-      const long long item = base + i * stride;
-      if (item >= total) break;
-      const int m = static_cast<int>(item / H);
-      const int hh = static_cast<int>(item % H);
-      const __nv_bfloat16* gsrc =
-          hh < Hq ? dq + (static_cast<long long>(m) * Hq + hh) * Dh
-                  : (hh < Hq + Hkv ? dk + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh
-                                   : dv + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh);
-      graw[i] = *reinterpret_cast<const uint2*>(gsrc + lane * 4);
-      if (hh < Hq + Hkv) xraw[i] = *reinterpret_cast<const uint2*>(qkv + item * Dh + lane * 4);
+  for (long long item = static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp; item < total;
+       item += static_cast<long long>(gridDim.x) * kRowsPerBlock) {
+    const int m = static_cast<int>(item / H);
+    const int hh = static_cast<int>(item % H);
+    __nv_bfloat16* out = dqkv + item * Dh + lane * 4;
+    if (hh >= Hq + Hkv) {
+      *reinterpret_cast<uint2*>(out) =
+          *reinterpret_cast<const uint2*>(dv + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh + lane * 4);
+      continue;
     }
-#pragma unroll
-    for (int i = 0; i < kQkRows; ++i) {
-      const long long item = base + i * stride;
-      if (item >= total) break;  // warp-uniform
-      const int m = static_cast<int>(item / H);
-      const int hh = static_cast<int>(item % H);
-      __nv_bfloat16* out = dqkv + item * Dh + lane * 4;
-      if (hh >= Hq + Hkv) {
-        *reinterpret_cast<uint2*>(out) = graw[i];
-        continue;
-      }
-      const bool is_q = hh < Hq;
-      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&graw[i]);
-      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xraw[i]);
-      const float2 g01 = __bfloat1622float2(g2[0]), g23 = __bfloat1622float2(g2[1]);
-      const float2 x01 = __bfloat1622float2(x2[0]), x23 = __bfloat1622float2(x2[1]);
-      float g[4] = {g01.x, g01.y, g23.x, g23.y};
-      const float x[4] = {x01.x, x01.y, x23.x, x23.y};
-      if (use_rope) {
-        const int pos = start + (m % T);
-        const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-        const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-        const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
-        float gn[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float partner = __shfl_xor_sync(0xffffffffu, g[e], 16);
-          gn[e] = lane < 16 ? g[e] * cc[e] + partner * ss[e] : -partner * ss[e] + g[e] * cc[e];
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) g[e] = gn[e];
-      }
-      const float4 sc = is_q ? scq : sck;
-      const float w[4] = {1.f + sc.x, 1.f + sc.y, 1.f + sc.z, 1.f + sc.w};
-      const float r = is_q ? rq[static_cast<long long>(m) * Hq + hh] : rk[static_cast<long long>(m) * Hkv + (hh - Hq)];
-      const float dot = warp_sum(g[0] * w[0] * x[0] + g[1] * w[1] * x[1] + g[2] * w[2] * x[2] + g[3] * w[3] * x[3]) / Dh;
-      float d[4];
+    const bool is_q = hh < Hq;
+    const __nv_bfloat16* gsrc = is_q ? dq + (static_cast<long long>(m) * Hq + hh) * Dh
+                                     : dk + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh;
+    const uint2 graw = *reinterpret_cast<const uint2*>(gsrc + lane * 4);
+    const uint2 xraw = *reinterpret_cast<const uint2*>(qkv + item * Dh + lane * 4);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&graw);
+    const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xraw);
+    const float2 g01 = __bfloat1622float2(g2[0]), g23 = __bfloat1622float2(g2[1]);
+    const float2 x01 = __bfloat1622float2(x2[0]), x23 = __bfloat1622float2(x2[1]);
+    float g[4] = {g01.x, g01.y, g23.x, g23.y};
+    const float x[4] = {x01.x, x01.y, x23.x, x23.y};
+    if (use_rope) {
+      const int pos = start + (m % T);
+      const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
+      const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
+      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+      float gn[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        d[e] = r * w[e] * g[e] - x[e] * r * r * r * dot;
-        if (is_q) accq[e] += g[e] * x[e] * r; else acck[e] += g[e] * x[e] * r;
+        const float partner = __shfl_xor_sync(0xffffffffu, g[e], 16);
+        gn[e] = lane < 16 ? g[e] * cc[e] + partner * ss[e] : -partner * ss[e] + g[e] * cc[e];
       }
-      uint2 o;
-      o.x = pack_bf16x2(d[0], d[1]);
-      o.y = pack_bf16x2(d[2], d[3]);
-      *reinterpret_cast<uint2*>(out) = o;
-    }
-  }
-  __shared__ float s_acc[kRowsPerBlock][2][Dh];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    s_acc[warp][0][lane * 4 + e] = accq[e];
-    s_acc[warp][1][lane * 4 + e] = acck[e];
+      for (int e = 0; e < 4; ++e) g[e] = gn[e];
+    }
+    const float4 sc = is_q ? scq : sck;
+    const float w[4] = {1.f + sc.x, 1.f + sc.y, 1.f + sc.z, 1.f + sc.w};
+    const float r = is_q ? rq[static_cast<long long>(m) * Hq + hh] : rk[static_cast<long long>(m) * Hkv + (hh - Hq)];
+    const float dot = warp_sum(g[0] * w[0] * x[0] + g[1] * w[1] * x[1] + g[2] * w[2] * x[2] + g[3] * w[3] * x[3]) / Dh;
+    float d[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      d[e] = r * w[e] * g[e] - x[e] * r * r * r * dot;
+      s_acc[warp][is_q ? 0 : 1][lane * 4 + e] += g[e] * x[e] * r;
+    }
+    uint2 o;
+    o.x = pack_bf16x2(d[0], d[1]);
+    o.y = pack_bf16x2(d[2], d[3]);
+    *reinterpret_cast<uint2*>(out) = o;
   }
   __syncthreads();
   for (int j = threadIdx.x; j < 2 * Dh; j += blockDim.x) {
@@ -869,8 +836,7 @@ std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, int64_t n_q, int
   auto st = at::cuda::getCurrentCUDAStream();
   const int grid = static_cast<int>((items + kRowsPerBlock - 1) / kRowsPerBlock);
   if (Dh == 128) {
-    const int grid128 = static_cast<int>((items + kRowsPerBlock * kQkRows - 1) / (kRowsPerBlock * kQkRows));
-    qk_norm_rope_fwd128_kernel<<<grid128, 256, 0, st>>>(
+    qk_norm_rope_fwd128_kernel<<<grid, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qs.data_ptr<float>(), ks.data_ptr<float>(),
         cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q.data_ptr()),
         reinterpret_cast<__nv_bfloat16*>(k.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v.data_ptr()),
