@@ -1033,11 +1033,19 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   }();
   const int pairs = sms / 2;
   const int64_t pair_tiles = nb * ((M + 255) / 256) * ((N + 255) / 256);
-  int pair_splits = 1;
-  if (accumulate && pair_tiles < pairs && kblocks >= 8) {
-    pair_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((pairs + pair_tiles - 1) / pair_tiles,
-                                                                          kblocks / 4)));
-  }
+  // split-K factor of an accumulating GEMM: the smallest that fills >= 90% of every wave of workers
+  // (each split keeps >= 4 k-blocks)
+  auto pick_splits = [&](int64_t tiles, int workers) -> int {
+    if (tiles >= workers || kblocks < 8) return 1;
+    const int64_t max_s = std::max<int64_t>(1, kblocks / 4);
+    for (int64_t sp = 1; sp <= max_s; ++sp) {
+      const int64_t items = tiles * sp;
+      const int64_t waves = (items + workers - 1) / workers;
+      if (items * 10 >= waves * workers * 9) return static_cast<int>(sp);
+    }
+    return static_cast<int>(std::min<int64_t>(max_s, (workers + tiles - 1) / tiles));
+  };
+  const int pair_splits = accumulate ? pick_splits(pair_tiles, pairs) : 1;
   const bool use_pair = pair_enabled && M >= 256 && N > 128 && pair_tiles * pair_splits * 10 >= pairs * 9;
   int BN = 256;
   if (!use_pair) {
@@ -1056,11 +1064,7 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
     if (use_pair) {
       splits = pair_splits;
     } else {
-      const int64_t tiles = nb * p.tiles_m * p.tiles_n;
-      if (tiles < sms && kblocks >= 8) {
-        // enough (tile, split) work items for ~2 waves, each split with >= 4 k-blocks
-        splits = static_cast<int>(std::min<int64_t>((2 * sms + tiles - 1) / tiles, kblocks / 4));
-      }
+      splits = pick_splits(nb * p.tiles_m * p.tiles_n, sms);
     }
     splits = std::max(splits, 1);
     p.kbps = (kblocks + splits - 1) / splits;
