@@ -44,6 +44,12 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
                                        double scale, const c10::optional<at::Tensor>& dbounds);
 at::Tensor doc_bounds(const at::Tensor& doc);
+void zero_reduce_scatter(const std::vector<int64_t>& bucket_ptrs, at::Tensor& shard, double scale,
+                         const c10::optional<at::Tensor>& sumsq, const std::vector<int64_t>& flag_ptrs,
+                         const at::Tensor& flags_local, int64_t rank, int64_t world, int64_t seq);
+void zero_all_gather(const at::Tensor& shard, const std::vector<int64_t>& bucket_ptrs, int64_t rank, int64_t world);
+void zero_barrier(const std::vector<int64_t>& flag_ptrs, const at::Tensor& flags_local, int64_t rank, int64_t world,
+                  int64_t seq);
 void gemm_ag(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool b_kmajor, const std::vector<int64_t>& src_ptrs,
              const at::Tensor& arrive, const std::vector<int64_t>& arrive_peers, at::Tensor& rowflag, at::Tensor& claim,
              int64_t rank, int64_t world, int64_t seg, int64_t seq);
@@ -89,5 +95,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("causal"), py::arg("window"), py::arg("scale"), py::arg("dbounds") = py::none());
   m.def("gemm_ag", &mint::gemm_ag, "tensor-parallel all-gather of A's rows fused into a CTA-pair tcgen05 GEMM");
   m.def("gemm_rs", &mint::gemm_rs, "CTA-pair tcgen05 GEMM with the reduce-scatter of its output rows fused in");
+  m.def("zero_reduce_scatter", &mint::zero_reduce_scatter,
+        "ZeRO gradient reduce-scatter over NVLink peer memory, 1/dp scale and squared norm fused");
+  m.def("zero_all_gather", &mint::zero_all_gather, "ZeRO parameter all-gather: push this rank's shard to every peer");
+  m.def("zero_barrier", &mint::zero_barrier, "stream-ordered barrier of a ZeRO group over NVLink peer flags");
   m.def("doc_bounds", &mint::doc_bounds, "[B, T, 2] int32 document run [start, end) of every token");
 }

@@ -1,0 +1,185 @@
+// ZeRO data-parallel collectives over NVLink peer memory (symmetric buffers mapped into every rank).
+//
+// zero_reduce_scatter: this rank's shard of sum over ranks of a flat fp32 gradient bucket, scaled by
+//   1/dp, written into the shard buffer; the shard's squared norm is added to a device scalar (the
+//   global gradient norm for clipping then needs one scalar all-reduce instead of a pass over the
+//   shards). The kernel announces that its own bucket is final, waits for every peer's
+//   announcement and pulls the peers' slices of its shard with 16-byte loads.
+// zero_all_gather: pushes this rank's (updated) shard of a flat parameter bucket into every
+//   peer's copy of the bucket; zero_barrier (one block, after the pushes of all buckets) announces
+//   it and waits until every peer's shards have landed in this rank's copies.
+// Flags hold a call sequence number and are never reset; every wait is bounded (common.cuh) and
+// records kStatusTimeoutPeer in the device status word when it gives up.
+// Reference: the per-parameter NCCL reduce_scatter_tensor / all_gather_into_tensor of
+// mint/utils/parallel.py:237-261 and mint/optim/dist/muon_adamw.py:215-222.
+#include <vector>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace mint {
+namespace zc {
+
+constexpr int kMaxRanks = 8;
+
+struct Peers {
+  const float* src[kMaxRanks];  // every rank's bucket (reduce-scatter) or shard destination (all-gather)
+  float* dst[kMaxRanks];
+  int* flag_peer[kMaxRanks];    // rank p's flag slot for this rank
+};
+
+// Announce (one thread of block 0) and wait (one thread per block) for every peer at `seq`.
+__device__ __forceinline__ bool announce_and_wait(const Peers& pe, const int* flag_local, int rank, int world, int seq,
+                                                  uint32_t* status, volatile int* abort_flag) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    __threadfence_system();
+    for (int q = 0; q < world; ++q) {
+      if (q != rank) st_release_sys(pe.flag_peer[q] + rank, seq);
+    }
+  }
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int q = 0; q < world && ok; ++q) {
+      if (q != rank) ok = wait_flag(flag_local + q, seq, true, status, kStatusTimeoutPeer, abort_flag);
+    }
+    ok_s = ok ? 1 : 0;
+  }
+  __syncthreads();
+  return ok_s != 0;
+}
+
+__global__ void __launch_bounds__(256) zero_reduce_scatter_kernel(Peers pe, float* __restrict__ shard, long long off,
+                                                                  long long n, float scale, float* __restrict__ sumsq,
+                                                                  const int* flag_local, int rank, int world, int seq,
+                                                                  uint32_t* status) {
+  __shared__ int abort_s;
+  if (threadIdx.x == 0) abort_s = 0;
+  __syncthreads();
+  if (!announce_and_wait(pe, flag_local, rank, world, seq, status, &abort_s)) return;
+  float acc = 0.f;
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < world; ++q) {
+      const float4 v = reinterpret_cast<const float4*>(pe.src[q] + off)[i];
+      t.x += v.x;
+      t.y += v.y;
+      t.z += v.z;
+      t.w += v.w;
+    }
+    t.x *= scale;
+    t.y *= scale;
+    t.z *= scale;
+    t.w *= scale;
+    reinterpret_cast<float4*>(shard)[i] = t;
+    acc += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+  }
+  acc = warp_sum(acc);
+  __shared__ float part[8];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0 && sumsq != nullptr) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += part[w];
+    atomicAdd(sumsq, t);
+  }
+}
+
+__global__ void __launch_bounds__(256) zero_push_kernel(Peers pe, const float* __restrict__ shard, long long off,
+                                                        long long n, int rank, int world) {
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(shard)[i];
+    for (int q = 0; q < world; ++q) {
+      if (q != rank) reinterpret_cast<float4*>(pe.dst[q] + off)[i] = v;
+    }
+  }
+}
+
+// One block: the push kernel before it (stream order) has completed, so announce, then wait until
+// every peer announced that its shard landed in this rank's bucket.
+__global__ void zero_signal_kernel(Peers pe, const int* flag_local, int rank, int world, int seq, uint32_t* status) {
+  __shared__ int abort_s;
+  if (threadIdx.x == 0) abort_s = 0;
+  __syncthreads();
+  announce_and_wait(pe, flag_local, rank, world, seq, status, &abort_s);
+}
+
+}  // namespace zc
+
+namespace {
+zc::Peers make_peers(const std::vector<int64_t>& src, const std::vector<int64_t>& dst,
+                     const std::vector<int64_t>& flags, int64_t world) {
+  MINT_CHECK(world >= 2 && world <= zc::kMaxRanks, "fused ZeRO collectives need 2..8 ranks");
+  zc::Peers pe{};
+  for (int q = 0; q < world; ++q) {
+    if (!src.empty()) pe.src[q] = reinterpret_cast<const float*>(src[q]);
+    if (!dst.empty()) pe.dst[q] = reinterpret_cast<float*>(dst[q]);
+    pe.flag_peer[q] = reinterpret_cast<int*>(flags[q]);
+  }
+  return pe;
+}
+
+int grid_for(long long n4, int dev) {
+  const long long want = (n4 + 255) / 256;
+  const long long cap = static_cast<long long>(num_sms(dev)) * 2;
+  return static_cast<int>(std::max<long long>(1, std::min(want, cap)));
+}
+}  // namespace
+
+// shard = scale * sum over ranks of bucket_p[rank * shard_len : (rank + 1) * shard_len]; sumsq += ||shard||^2.
+void zero_reduce_scatter(const std::vector<int64_t>& bucket_ptrs, at::Tensor& shard, double scale,
+                         const c10::optional<at::Tensor>& sumsq, const std::vector<int64_t>& flag_ptrs,
+                         const at::Tensor& flags_local, int64_t rank, int64_t world, int64_t seq) {
+  check_contig(shard, "shard");
+  MINT_CHECK(shard.scalar_type() == at::kFloat && shard.numel() % 4 == 0, "shard must be fp32 with numel % 4 == 0");
+  MINT_CHECK(static_cast<int64_t>(bucket_ptrs.size()) == world && static_cast<int64_t>(flag_ptrs.size()) == world,
+             "one bucket / flag pointer per rank");
+  c10::cuda::CUDAGuard guard(shard.device());
+  const int dev = shard.get_device();
+  zc::Peers pe = make_peers(bucket_ptrs, {}, flag_ptrs, world);
+  const long long n = shard.numel();
+  zc::zero_reduce_scatter_kernel<<<grid_for(n / 4, dev), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      pe, shard.data_ptr<float>(), rank * n, n, static_cast<float>(scale),
+      sumsq.has_value() && sumsq->defined() ? sumsq->data_ptr<float>() : nullptr, flags_local.data_ptr<int>(),
+      static_cast<int>(rank), static_cast<int>(world), static_cast<int>(seq), status_ptr(dev));
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+// Copy this rank's shard into every peer's bucket at offset rank * shard_len (bucket_ptrs[p] = rank p's
+// bucket). Completion is published by zero_barrier, once after the pushes of every bucket.
+void zero_all_gather(const at::Tensor& shard, const std::vector<int64_t>& bucket_ptrs, int64_t rank, int64_t world) {
+  check_contig(shard, "shard");
+  MINT_CHECK(shard.scalar_type() == at::kFloat && shard.numel() % 4 == 0, "shard must be fp32 with numel % 4 == 0");
+  MINT_CHECK(static_cast<int64_t>(bucket_ptrs.size()) == world, "one bucket pointer per rank");
+  c10::cuda::CUDAGuard guard(shard.device());
+  const int dev = shard.get_device();
+  std::vector<int64_t> no_flags(world, 0);
+  zc::Peers pe = make_peers({}, bucket_ptrs, no_flags, world);
+  const long long n = shard.numel();
+  zc::zero_push_kernel<<<grid_for(n / 4, dev), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      pe, shard.data_ptr<float>(), rank * n, n, static_cast<int>(rank), static_cast<int>(world));
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+// Stream-ordered barrier over the group: everything this rank's stream did before it (peer stores
+// included) is visible to every peer when the peer's barrier returns.
+void zero_barrier(const std::vector<int64_t>& flag_ptrs, const at::Tensor& flags_local, int64_t rank, int64_t world,
+                  int64_t seq) {
+  MINT_CHECK(static_cast<int64_t>(flag_ptrs.size()) == world, "one flag pointer per rank");
+  c10::cuda::CUDAGuard guard(flags_local.device());
+  const int dev = flags_local.get_device();
+  zc::Peers pe = make_peers({}, {}, flag_ptrs, world);
+  zc::zero_signal_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      pe, flags_local.data_ptr<int>(), static_cast<int>(rank), static_cast<int>(world), static_cast<int>(seq),
+      status_ptr(dev));
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace mint

@@ -101,6 +101,12 @@ class _BackwardGather(torch.autograd.Function):
         return g, None, None
 
 
+def _ext_mod():  # noqa: ANN202
+    from mint_b200.ops import _ext  # noqa: PLC0415
+
+    return _ext.require()
+
+
 class GradEngine:
     def __init__(self, model: nn.Module, parallel: ParallelContext, bucket_cap_mb: float = 256.0) -> None:
         self.model = model
@@ -114,6 +120,10 @@ class GradEngine:
         self.sync_grads = True
         self.epoch = 0  # bumped whenever parameter values change (optimizer step, load)
         self._in_backward: set[str] = set()
+        # ZeRO-2 on CUDA: gradient reduce-scatter and parameter all-gather as NVLink peer-memory kernels
+        # (csrc/zero_comm.cu) over symmetric bucket buffers instead of NCCL; MINT_FUSED_ZERO=0 disables
+        self.fused = self._fused_possible(model)
+        self._zc = None
         self.buckets: list[Bucket] = []
         self.by_param: dict[int, tuple[Bucket, Slot]] = {}
         self.groups: dict[str, list[Bucket]] = defaultdict(list)
@@ -181,7 +191,12 @@ class GradEngine:
             shard = size // dp
         b = Bucket(len(self.buckets), grp, kind, pk, dtype, slots, size, shard)
         dev = items[0][1].device
-        data = torch.zeros(size, dtype=dtype, device=dev)
+        if self.fused and dtype == torch.float32 and shard % 4 == 0:
+            b.extra["symm_data"] = self._symm(size * 4, dev)
+            b.extra["symm_grad"] = self._symm(size * 4, dev)
+            data = b.extra["symm_data"].view((size,), torch.float32)
+        else:
+            data = torch.zeros(size, dtype=dtype, device=dev)
         for s in slots:
             data[s.start : s.start + s.numel].copy_(s.param.detach().reshape(-1))
             self.by_param[id(s.param)] = (b, s)
@@ -198,12 +213,57 @@ class GradEngine:
             b.shard_data = data[lo : lo + shard]
             for s in slots:
                 s.param.data = data[s.start : s.start + s.numel].view(s.shape)
-            b.grad = torch.zeros(size, dtype=dtype, device=dev)
+            b.grad = (b.extra["symm_grad"].view((size,), torch.float32) if "symm_grad" in b.extra
+                      else torch.zeros(size, dtype=dtype, device=dev))
         if self.level >= 2 and self.dp > 1:
             b.grad_shard = torch.zeros(shard, dtype=dtype, device=dev)
         self.buckets.append(b)
         for s in slots:
             s.param._grad_engine = self  # lets the optimizer find the engine
+
+    # ------------------------------------------------------------------ fused ZeRO-2 transport
+    def _fused_possible(self, model: nn.Module) -> bool:
+        import os  # noqa: PLC0415
+
+        if os.environ.get("MINT_FUSED_ZERO", "1") == "0" or self.level != 2 or not self.distributed:
+            return False
+        if self.dp > 8 or not torch.cuda.is_available():
+            return False
+        dev = next((p.device for p in model.parameters()), torch.device("cpu"))
+        if dev.type != "cuda":
+            return False
+        from mint_b200.ops import _ext  # noqa: PLC0415
+
+        return _ext.kernels_enabled() and hasattr(_ext.require(), "zero_reduce_scatter")
+
+    def _symm(self, nbytes: int, dev: torch.device):  # noqa: ANN202
+        from mint_b200.parallel.fused import _Symm  # noqa: PLC0415
+
+        if self._zc is None:
+            # control: flags [dp] int32 (one slot per peer), one sequence counter for both collectives
+            ctrl = _Symm(256, self.group, dev)
+            self._zc = {"ctrl": ctrl, "flags": ctrl.view((self.dp,), torch.int32), "seq": 0,
+                        "stream": torch.cuda.Stream(device=dev)}
+        return _Symm(nbytes, self.group, dev)
+
+    def _next_seq(self) -> int:
+        self._zc["seq"] += 1
+        return self._zc["seq"]
+
+    def _fused_reduce_scatter(self, b: Bucket) -> torch.Tensor:
+        """This rank's shard of sum over ranks of the bucket's gradient, / dp, on the comm stream."""
+        zc = self._zc
+        out = torch.empty_like(b.grad_shard)
+        stream = zc["stream"]
+        stream.wait_stream(torch.cuda.current_stream())  # every gradient of the bucket has landed
+        with torch.cuda.stream(stream):
+            _ext_mod().zero_reduce_scatter(b.extra["symm_grad"].ptrs, out, 1.0 / self.dp, None,
+                                               zc["ctrl"].ptrs, zc["flags"], self.rank, self.dp, self._next_seq())
+        out.record_stream(stream)
+        return out
+
+    def _fused_all_gather(self, b: Bucket) -> None:
+        _ext_mod().zero_all_gather(b.shard_data, b.extra["symm_data"].ptrs, self.rank, self.dp)
 
     # ------------------------------------------------------------------ grads
     def _install_grad_views(self, b: Bucket) -> None:
@@ -256,6 +316,10 @@ class GradEngine:
         else:
             if not self.sync_grads and self.level == 2:
                 return
+            if "symm_grad" in b.extra:
+                b.handle = ("fused", self._fused_reduce_scatter(b))
+                b.pending_scale = False
+                return
             out = torch.empty_like(b.grad_shard)
             h = dist.reduce_scatter_tensor(out, b.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
             b.handle = (h, out)
@@ -266,7 +330,11 @@ class GradEngine:
     def _finish_bucket(self, b: Bucket) -> None:
         if b.handle is None:
             return
-        if isinstance(b.handle, tuple):
+        if isinstance(b.handle, tuple) and b.handle[0] == "fused":
+            zc = self._zc
+            torch.cuda.current_stream().wait_stream(zc["stream"])
+            b.grad_shard.add_(b.handle[1])  # already scaled by 1/dp in the kernel
+        elif isinstance(b.handle, tuple):
             h, out = b.handle
             h.wait()
             b.grad_shard.add_(out)
@@ -290,7 +358,7 @@ class GradEngine:
             if self.level in (0, 1):
                 if b.grad is not None:
                     b.grad.mul_(inv)
-            elif b.grad_shard is not None:
+            elif b.grad_shard is not None and "symm_grad" not in b.extra:
                 b.grad_shard.mul_(inv)
             b.pending_scale = False
 
@@ -355,11 +423,21 @@ class GradEngine:
             self._in_backward.clear()
             return
         handles = []
+        pushed = False
         for b in self.buckets:
+            if "symm_data" in b.extra:
+                self._fused_all_gather(b)
+                pushed = True
+                continue
             src = b.shard_data.clone()
             handles.append(dist.all_gather_into_tensor(b.data, src, group=self.group, async_op=True))
         for h in handles:
             h.wait()
+        if pushed:
+            # one barrier for every bucket's push: peers' shards have landed here, and no peer still
+            # reads this rank's gradient buckets, so the next zero_grad and forward may proceed
+            zc = self._zc
+            _ext_mod().zero_barrier(zc["ctrl"].ptrs, zc["flags"], self.rank, self.dp, self._next_seq())
 
     # ------------------------------------------------------------------ grad norm
     def _reduced_grad(self, b: Bucket) -> torch.Tensor | None:

@@ -1,0 +1,143 @@
+"""Worker for test_fused_zero.py, launched by torchrun with one rank per GPU.
+
+Checks the ZeRO peer-memory collectives (csrc/zero_comm.cu) against NCCL:
+  1. reduce-scatter of a symmetric fp32 bucket with the 1/dp scale and squared-norm fused, three
+     calls in a row (flags are sequence numbers, never reset);
+  2. all-gather (push of every rank's shard + one barrier) into a symmetric bucket;
+  3. ZeRO-2 training (dp = world, NorMuon + AdamW, global-norm clipping) for three steps: the
+     consolidated parameters with the fused transport against the NCCL transport.
+Prints one line per check and exits non-zero on a mismatch.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+
+
+def rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+def train(fused: str, dev: torch.device) -> dict[str, torch.Tensor]:
+    from mint_b200.models.gemma import Gemma, GemmaConfig, configure_optimizer
+    from mint_b200.optim.muon_adamw import MuonAdamWConfig
+    from mint_b200.parallel.api import setup_parallel
+    from mint_b200.parallel.context import ParallelContext
+    from mint_b200.parallel.zero import get_engine
+    from mint_b200.trainer.scheduler import SchedulerConfig
+    from mint_b200.utils.checkpointer import consolidated_state_dict
+
+    os.environ["MINT_FUSED_ZERO"] = fused
+    cfg = GemmaConfig(embed_dim=256, hidden_dim=512, seq_length=256, vocab_size=1024, n_layers=2, n_heads=2,
+                      n_kv_heads=1, head_dim=128, rope_base_theta=10000)
+    pctx = ParallelContext.build(tp_size=1, ddp_level=2, device_type="cuda")
+    torch.manual_seed(1337)
+    model = Gemma(cfg).to(dev)
+    model = setup_parallel(model, pctx, bucket_cap_mb=0.5)
+    eng = get_engine(model)
+    assert eng.fused == (fused == "1"), (eng.fused, fused)
+    opt = configure_optimizer(model, cfg, SchedulerConfig(), MuonAdamWConfig(), dp_group=pctx.dp_group)
+    g = torch.Generator(device="cpu").manual_seed(7)
+    for _ in range(3):
+        x = torch.randint(0, cfg.vocab_size, (2 * pctx.dp_size, cfg.seq_length), generator=g)
+        y = torch.randint(0, cfg.vocab_size, (2 * pctx.dp_size, cfg.seq_length), generator=g)
+        xs = x.chunk(pctx.dp_size)[pctx.dp_rank].to(dev)
+        ys = y.chunk(pctx.dp_size)[pctx.dp_rank].to(dev)
+        opt.zero_grad()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model.loss(xs, ys, torch.ones_like(xs, dtype=torch.float32))
+        loss.backward()
+        eng.finish_grad_sync()
+        eng.sync_tp_partial_grads()
+        eng._synced = True
+        eng.clip_grad_norm(0.5)
+        opt.step()
+    torch.cuda.synchronize()
+    return {k: v.detach().float().cpu() for k, v in consolidated_state_dict(model).items()}
+
+
+def main() -> None:
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", local)
+    from mint_b200.ops import _ext
+    from mint_b200.parallel.fused import _Symm
+
+    C = _ext.require()
+    failures = 0
+    shard = 3 * 1024 * 1024 + 16
+    size = shard * world
+    grad = _Symm(size * 4, dist.group.WORLD, dev)
+    ctrl = _Symm(256, dist.group.WORLD, dev)
+    flags = ctrl.view((world,), torch.int32)
+    seq = 0
+    for it in range(3):
+        torch.manual_seed(100 * it + rank)
+        gv = grad.view((size,), torch.float32)
+        gv.copy_(torch.randn(size, device=dev))
+        want = torch.empty(shard, device=dev)
+        dist.reduce_scatter_tensor(want, gv.clone())
+        want /= world
+        out = torch.empty(shard, device=dev)
+        sumsq = torch.zeros(1, device=dev)
+        dist.barrier()
+        seq += 1
+        C.zero_reduce_scatter(grad.ptrs, out, 1.0 / world, sumsq, ctrl.ptrs, flags, rank, world, seq)
+        # the buffer may be rewritten only after every peer has read it
+        seq += 1
+        C.zero_barrier(ctrl.ptrs, flags, rank, world, seq)
+        torch.cuda.synchronize()
+        e = rel(out, want)
+        en = abs(sumsq.item() - want.square().sum().item()) / want.square().sum().item()
+        ok = e < 1e-6 and en < 1e-4
+        failures += not ok
+        print(f"[rank {rank}] reduce-scatter call {it}: rel err {e:.2e} norm err {en:.2e} {'OK' if ok else 'FAIL'}",
+              flush=True)
+    data = _Symm(size * 4, dist.group.WORLD, dev)
+    for it in range(3):
+        dv = data.view((size,), torch.float32)
+        dv.fill_(-1.0)
+        dist.barrier()
+        torch.manual_seed(7 + it + 10 * rank)
+        mine = torch.randn(shard, device=dev)
+        dv[rank * shard : (rank + 1) * shard].copy_(mine)
+        # peers must not push into this rank's copy before the fill above: one barrier first
+        seq += 1
+        C.zero_barrier(ctrl.ptrs, flags, rank, world, seq)
+        C.zero_all_gather(mine, data.ptrs, rank, world)
+        seq += 1
+        C.zero_barrier(ctrl.ptrs, flags, rank, world, seq)
+        torch.cuda.synchronize()
+        want = torch.empty(size, device=dev)
+        dist.all_gather_into_tensor(want, mine)
+        ok = torch.equal(dv, want)
+        failures += not ok
+        print(f"[rank {rank}] all-gather call {it}: {'OK' if ok else 'FAIL'}", flush=True)
+    _ext.check_device_status()
+
+    ref = train("0", dev)
+    got = train("1", dev)
+    worst = max(rel(got[k], ref[k]) for k in ref)
+    ok = set(ref) == set(got) and worst < 1e-3
+    failures += not ok
+    print(f"[rank {rank}] ZeRO-2 3 steps fused vs NCCL: worst param rel diff {worst:.2e} over {len(ref)} "
+          f"{'OK' if ok else 'FAIL'}", flush=True)
+    torch.cuda.synchronize()
+    _ext.check_device_status()
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(1 if failures else 0)
+
+
+if __name__ == "__main__":
+    main()
