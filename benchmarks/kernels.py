@@ -7,6 +7,7 @@
     python benchmarks/kernels.py gemm --M 65536 --N 2304 --K 768              # y = x W^T
     python benchmarks/kernels.py gemm --M 768 --N 2304 --K 65536 --layout wgrad
     python benchmarks/kernels.py gemm --M 768 --N 3072 --K 768 --batch 24     # batched (Polar Express)
+    python benchmarks/kernels.py norm --M 65536 --D 768                       # QK-norm+RoPE, add+RMSNorm
     python benchmarks/kernels.py attn ... --once       # one untimed call per kernel (for ncu captures)
     python benchmarks/kernels.py gemm ... --once-lib   # the same for the library path
 
@@ -168,6 +169,61 @@ def run_gemm(a: argparse.Namespace) -> dict:
             "ours_tflops": flop / t_o / 1e9, "cublas_tflops": flop / t_l / 1e9}
 
 
+def hbm_peak_gbs() -> tuple[float, str]:
+    p = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def run_norm(a: argparse.Namespace) -> dict:
+    """QK-norm + RoPE and residual-add + RMSNorm, forward and backward, on the d12 shapes."""
+    C = _ext.require()
+    torch.manual_seed(0)
+    M, D, hq, hkv, dh = a.M, a.D, a.hq, a.hkv, 128
+    H = hq + 2 * hkv
+    T = a.T
+    qkv = torch.randn(M // T, T, H * dh, device="cuda", dtype=torch.bfloat16)
+    qs, ks = torch.zeros(dh, device="cuda"), torch.zeros(dh, device="cuda")
+    pos = torch.arange(T, device="cuda", dtype=torch.float32)[:, None]
+    inv = 1.0 / (10000.0 ** (torch.arange(0, dh, 2, device="cuda", dtype=torch.float32) / dh))
+    cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
+    q, k, v, rq, rk = C.qk_norm_rope_fwd(qkv, hq, hkv, dh, qs, ks, cos, sin, 0, 1e-6, True)
+    dq, dk, dv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
+    res = torch.randn(M, D, device="cuda", dtype=torch.float32)
+    x = torch.randn(M, D, device="cuda", dtype=torch.bfloat16)
+    post, pre = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+    h, y, ra, rh = C.add_rmsnorm_fwd(res, x, post, pre, 1e-6, 1)
+    dh_, dy = torch.randn_like(h), torch.randn_like(y)
+    if a.once:
+        C.qk_norm_rope_bwd(dq, dk, dv, qkv, rq, rk, qs, ks, cos, sin, hq, hkv, dh, 0, True)
+        C.add_rmsnorm_bwd(dh_, dy, x, h, ra, rh, post, pre)
+        torch.cuda.synchronize()
+        return {"once": True}
+    peak, kind = hbm_peak_gbs()
+    e2, e4 = 2, 4
+    rows_qk = M * (hq + hkv)
+    cases = {
+        "qk_norm_rope_fwd": (lambda: C.qk_norm_rope_fwd(qkv, hq, hkv, dh, qs, ks, cos, sin, 0, 1e-6, True),
+                             2 * M * H * dh * e2 + rows_qk * e4),
+        "qk_norm_rope_bwd": (lambda: C.qk_norm_rope_bwd(dq, dk, dv, qkv, rq, rk, qs, ks, cos, sin, hq, hkv, dh, 0, True),
+                             2 * M * H * dh * e2 + rows_qk * dh * e2 + rows_qk * e4),
+        "add_rmsnorm_fwd": (lambda: C.add_rmsnorm_fwd(res, x, post, pre, 1e-6, 1),
+                            M * D * (e4 + e2) + M * D * (e4 + e2) + 2 * M * e4),
+        "add_rmsnorm_bwd": (lambda: C.add_rmsnorm_bwd(dh_, dy, x, h, ra, rh, post, pre),
+                            M * D * (e4 + e2 + e2 + e4) + M * D * (e4 + e2) + 2 * M * e4),
+    }
+    out = {"M": M, "D": D, "hq": hq, "hkv": hkv, "peak_gbs": peak, "peak": kind}
+    for name, (fn, nbytes) in cases.items():
+        t = time_fn(fn, a.iters)
+        out[f"{name}_ms"] = t
+        out[f"{name}_frac"] = nbytes / (t * 1e-3) / 1e9 / peak
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -185,12 +241,18 @@ def main() -> None:
     gm.add_argument("--K", type=int, default=768)
     gm.add_argument("--batch", type=int, default=1)
     gm.add_argument("--layout", choices=["fwd", "dgrad", "wgrad"], default="fwd")
-    for p in (at, gm):
+    nm = sub.add_parser("norm")
+    nm.add_argument("--M", type=int, default=65536)
+    nm.add_argument("--T", type=int, default=2048)
+    nm.add_argument("--D", type=int, default=768)
+    nm.add_argument("--hq", type=int, default=6)
+    nm.add_argument("--hkv", type=int, default=6)
+    for p in (at, gm, nm):
         p.add_argument("--iters", type=int, default=10)
         p.add_argument("--once", action="store_true")
         p.add_argument("--once-lib", action="store_true", help="run the library (cuBLAS / SDPA) path once")
     a = ap.parse_args()
-    res = run_attn(a) if a.cmd == "attn" else run_gemm(a)
+    res = {"attn": run_attn, "gemm": run_gemm, "norm": run_norm}[a.cmd](a)
     _ext.check_device_status()
     print(json.dumps(res), flush=True)
 

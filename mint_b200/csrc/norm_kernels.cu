@@ -4,6 +4,9 @@
 //   qk_norm_rope      per-head RMSNorm of q and k + half-split rotary embedding, splitting the fused QKV output
 // Backward kernels reduce the scale gradients per CTA in shared memory, then one atomicAdd per
 // column per CTA into an fp32 accumulator.
+#include <cstdlib>
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -101,6 +104,109 @@ __global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const float* __res
   }
 }
 
+__device__ __forceinline__ float half_warp_sum(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack_bf16x8(const uint4& raw, float (&x)[8]) {
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(h2[e]);
+    x[2 * e] = f.x;
+    x[2 * e + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&x)[8]) {
+  return make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                    pack_bf16x2(x[6], x[7]));
+}
+
+__device__ __forceinline__ void load_f32x8(const float* p, float (&x)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+}
+
+// Register-resident add + RMSNorm forward for D = 32 * VPT (VPT a multiple of 8): one warp per
+// row, lane l owns columns {l * 8 + 256 * c + e}; the row's a (bf16) and res (fp32) are loaded with
+// 16-byte accesses before any math (144 B in flight per lane at D = 768), h and y written once.
+template <int VPT, typename Ty>
+__global__ void __launch_bounds__(256) add_rmsnorm_fwd_reg_kernel(
+    const float* __restrict__ res, const __nv_bfloat16* __restrict__ a, const float* __restrict__ post,
+    const float* __restrict__ pre, float* __restrict__ h, Ty* __restrict__ y, float* __restrict__ rstd_a,
+    float* __restrict__ rstd_h, int rows, float eps) {
+  constexpr int D = VPT * 32;
+  constexpr int NC = VPT / 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerBlock + warp;
+  if (row >= rows) return;
+  const long long off = static_cast<long long>(row) * D;
+  uint4 araw[NC];
+  float4 r0[NC], r1[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int j = lane * 8 + c * 256;
+    araw[c] = *reinterpret_cast<const uint4*>(a + off + j);
+    r0[c] = *reinterpret_cast<const float4*>(res + off + j);
+    r1[c] = *reinterpret_cast<const float4*>(res + off + j + 4);
+  }
+  float av[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&araw[c]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(b2[e]);
+      av[c * 8 + 2 * e] = f.x;
+      av[c * 8 + 2 * e + 1] = f.y;
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  const float ra = rsqrtf(warp_sum(ss) * (1.f / D) + eps);
+  float sh = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int j = lane * 8 + c * 256;
+    const float rv[8] = {r0[c].x, r0[c].y, r0[c].z, r0[c].w, r1[c].x, r1[c].y, r1[c].z, r1[c].w};
+    float pw[8];
+    load_f32x8(post + j, pw);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      // the normalized branch is rounded to bf16 as the unfused module's output would be
+      const float n = __bfloat162float(__float2bfloat16_rn(av[c * 8 + e] * ra * (1.f + pw[e])));
+      av[c * 8 + e] = rv[e] + n;  // av now holds h
+      sh += av[c * 8 + e] * av[c * 8 + e];
+    }
+    *reinterpret_cast<float4*>(h + off + j) = make_float4(av[c * 8], av[c * 8 + 1], av[c * 8 + 2], av[c * 8 + 3]);
+    *reinterpret_cast<float4*>(h + off + j + 4) =
+        make_float4(av[c * 8 + 4], av[c * 8 + 5], av[c * 8 + 6], av[c * 8 + 7]);
+  }
+  if (lane == 0) rstd_a[row] = ra;
+  if (pre == nullptr) return;
+  const float rh = rsqrtf(warp_sum(sh) * (1.f / D) + eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int j = lane * 8 + c * 256;
+    float pw[8], o[8];
+    load_f32x8(pre + j, pw);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = av[c * 8 + e] * rh * (1.f + pw[e]);
+    if constexpr (std::is_same<Ty, float>::value) {
+      *reinterpret_cast<float4*>(y + off + j) = make_float4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<float4*>(y + off + j + 4) = make_float4(o[4], o[5], o[6], o[7]);
+    } else {
+      *reinterpret_cast<uint4*>(y + off + j) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                          pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+    }
+  }
+  if (lane == 0) rstd_h[row] = rh;
+}
+
 // dres = dh + rmsnorm_bwd(dy; h, pre);  da = rmsnorm_bwd(dres; a, post)
 template <typename Ty>
 __global__ void __launch_bounds__(256) add_rmsnorm_bwd_kernel(
@@ -155,130 +261,135 @@ __global__ void __launch_bounds__(256) add_rmsnorm_bwd_kernel(
   }
 }
 
-// Register-resident variant of add_rmsnorm_bwd_kernel for D = 32 * VPT <= 768 (VPT a multiple of 8): one
-// warp per row, lane l owns columns {l * 8 + 256 * c + e : c < VPT / 8, e < 8}, so every operand is
-// read once with 16-byte vector loads and the scale gradients accumulate in registers across rows.
+// Register-resident add + RMSNorm backward for D = 32 * VPT (VPT a multiple of 8), 4 warps per
+// block, one warp per row: every operand of the row (dy, h, dh, a and both rstd values) is loaded
+// with 16-byte accesses before the first reduction, so ~290 B per lane are in flight at D = 768.
+// The (1 + scale) weights and the per-warp scale-gradient accumulators live in shared memory, which
+// keeps the kernel near 100 registers (5 blocks per SM).
+constexpr int kArnBwdWarps = 4;
 template <int VPT>
-__global__ void __launch_bounds__(256) add_rmsnorm_bwd_reg_kernel(
+__global__ void __launch_bounds__(kArnBwdWarps * 32) add_rmsnorm_bwd_reg_kernel(
     const float* __restrict__ dh, const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ a,
     const float* __restrict__ h, const float* __restrict__ rstd_a, const float* __restrict__ rstd_h,
     const float* __restrict__ post, const float* __restrict__ pre, float* __restrict__ dres,
     __nv_bfloat16* __restrict__ da, float* __restrict__ dpost, float* __restrict__ dpre, int rows) {
   constexpr int D = VPT * 32;
-  constexpr int NC = VPT / 8;  // 8-element chunks per lane
-  __shared__ float s_red[8][2 * D];
+  constexpr int NC = VPT / 8;
+  // shared arrays are indexed [i][lane] (i = c * 8 + e, the lane's i-th column) so that a warp's
+  // 32 accesses hit 32 different banks
+  __shared__ float s_w[2][VPT][32];                  // 1 + post, 1 + pre
+  __shared__ float s_acc[kArnBwdWarps][2][VPT][32];  // per-warp dpost, dpre column sums
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float post1[VPT], pre1[VPT], acc_post[VPT], acc_pre[VPT];
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int j = lane * 8 + c * 256 + e;
-      post1[c * 8 + e] = 1.f + post[j];
-      pre1[c * 8 + e] = pre != nullptr ? 1.f + pre[j] : 1.f;
-      acc_post[c * 8 + e] = 0.f;
-      acc_pre[c * 8 + e] = 0.f;
-    }
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    const int i = (j >> 8) * 8 + (j & 7), l = (j & 255) >> 3;
+    s_w[0][i][l] = 1.f + post[j];
+    s_w[1][i][l] = pre != nullptr ? 1.f + pre[j] : 1.f;
   }
-  const int nwarps = blockDim.x >> 5;
-  for (int row = blockIdx.x * nwarps + warp; row < rows; row += gridDim.x * nwarps) {
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    s_acc[warp][0][i][lane] = 0.f;
+    s_acc[warp][1][i][lane] = 0.f;
+  }
+  __syncthreads();
+  for (int row = blockIdx.x * kArnBwdWarps + warp; row < rows; row += gridDim.x * kArnBwdWarps) {
     const long long off = static_cast<long long>(row) * D;
-    float g[VPT];  // gradient into h (then the post-norm output gradient)
+    uint4 yraw[NC], araw[NC];
+    float4 h0[NC], h1[NC], d0[NC], d1[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int j = lane * 8 + c * 256;
+      if (dy != nullptr) {
+        yraw[c] = *reinterpret_cast<const uint4*>(dy + off + j);
+        h0[c] = *reinterpret_cast<const float4*>(h + off + j);
+        h1[c] = *reinterpret_cast<const float4*>(h + off + j + 4);
+      }
+      if (dh != nullptr) {
+        d0[c] = *reinterpret_cast<const float4*>(dh + off + j);
+        d1[c] = *reinterpret_cast<const float4*>(dh + off + j + 4);
+      } else {
+        d0[c] = d1[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      araw[c] = *reinterpret_cast<const uint4*>(a + off + j);
+    }
+    const float ra = rstd_a[row];
+    const float rh = dy != nullptr ? rstd_h[row] : 0.f;
+    float g[VPT];  // gradient into h = dres
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const float dv[8] = {d0[c].x, d0[c].y, d0[c].z, d0[c].w, d1[c].x, d1[c].y, d1[c].z, d1[c].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g[c * 8 + e] = dv[e];
+    }
     if (dy != nullptr) {
-      float y[VPT], hv[VPT];
+      float yv[VPT], hv[VPT];
+      float dot = 0.f;
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
         const int j = lane * 8 + c * 256;
-        const uint4 u = *reinterpret_cast<const uint4*>(dy + off + j);
-        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&yraw[c]);
+        const float hh[8] = {h0[c].x, h0[c].y, h0[c].z, h0[c].w, h1[c].x, h1[c].y, h1[c].z, h1[c].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __bfloat1622float2(b2[e]);
-          y[c * 8 + 2 * e] = f.x;
-          y[c * 8 + 2 * e + 1] = f.y;
+          yv[c * 8 + 2 * e] = f.x;
+          yv[c * 8 + 2 * e + 1] = f.y;
         }
-        const float4 h0 = *reinterpret_cast<const float4*>(h + off + j);
-        const float4 h1 = *reinterpret_cast<const float4*>(h + off + j + 4);
-        hv[c * 8 + 0] = h0.x; hv[c * 8 + 1] = h0.y; hv[c * 8 + 2] = h0.z; hv[c * 8 + 3] = h0.w;
-        hv[c * 8 + 4] = h1.x; hv[c * 8 + 5] = h1.y; hv[c * 8 + 6] = h1.z; hv[c * 8 + 7] = h1.w;
-      }
-      const float rh = rstd_h[row];
-      float dot = 0.f;
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) dot += y[i] * pre1[i] * hv[i];
+        for (int e = 0; e < 8; ++e) {
+          hv[c * 8 + e] = hh[e];
+          dot += yv[c * 8 + e] * s_w[1][c * 8 + e][lane] * hh[e];
+        }
+      }
       dot = warp_sum(dot) * (1.f / D);
       const float k3 = rh * rh * rh * dot;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
-        g[i] = rh * pre1[i] * y[i] - hv[i] * k3;
-        acc_pre[i] += y[i] * hv[i] * rh;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < VPT; ++i) g[i] = 0.f;
-    }
-    if (dh != nullptr) {
-#pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        const int j = lane * 8 + c * 256;
-        const float4 d0 = *reinterpret_cast<const float4*>(dh + off + j);
-        const float4 d1 = *reinterpret_cast<const float4*>(dh + off + j + 4);
-        g[c * 8 + 0] += d0.x; g[c * 8 + 1] += d0.y; g[c * 8 + 2] += d0.z; g[c * 8 + 3] += d0.w;
-        g[c * 8 + 4] += d1.x; g[c * 8 + 5] += d1.y; g[c * 8 + 6] += d1.z; g[c * 8 + 7] += d1.w;
+        g[i] += rh * s_w[1][i][lane] * yv[i] - hv[i] * k3;
+        s_acc[warp][1][i][lane] += yv[i] * hv[i] * rh;
       }
     }
     float av[VPT];
+    float dot = 0.f;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int j = lane * 8 + c * 256;
       *reinterpret_cast<float4*>(dres + off + j) = make_float4(g[c * 8], g[c * 8 + 1], g[c * 8 + 2], g[c * 8 + 3]);
       *reinterpret_cast<float4*>(dres + off + j + 4) =
           make_float4(g[c * 8 + 4], g[c * 8 + 5], g[c * 8 + 6], g[c * 8 + 7]);
-      const uint4 u = *reinterpret_cast<const uint4*>(a + off + j);
-      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&araw[c]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f = __bfloat1622float2(b2[e]);
         av[c * 8 + 2 * e] = f.x;
         av[c * 8 + 2 * e + 1] = f.y;
       }
-    }
-    const float ra = rstd_a[row];
-    float dot = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) dot += g[i] * post1[i] * av[i];
+      for (int e = 0; e < 8; ++e) dot += g[c * 8 + e] * s_w[0][c * 8 + e][lane] * av[c * 8 + e];
+    }
     dot = warp_sum(dot) * (1.f / D);
     const float k3 = ra * ra * ra * dot;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      uint4 o;
-      uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+      const int j = lane * 8 + c * 256;
+      float o[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i0 = c * 8 + 2 * e, i1 = i0 + 1;
-        w[e] = pack_bf16x2(ra * post1[i0] * g[i0] - av[i0] * k3, ra * post1[i1] * g[i1] - av[i1] * k3);
-        acc_post[i0] += g[i0] * av[i0] * ra;
-        acc_post[i1] += g[i1] * av[i1] * ra;
+      for (int e = 0; e < 8; ++e) {
+        const int i = c * 8 + e;
+        o[e] = ra * s_w[0][i][lane] * g[i] - av[i] * k3;
+        s_acc[warp][0][i][lane] += g[i] * av[i] * ra;
       }
-      *reinterpret_cast<uint4*>(da + off + lane * 8 + c * 256) = o;
-    }
-  }
-  // column sums over this block's warps, then one atomic per column
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int j = lane * 8 + c * 256 + e;
-      s_red[warp][j] = acc_post[c * 8 + e];
-      s_red[warp][D + j] = acc_pre[c * 8 + e];
+      *reinterpret_cast<uint4*>(da + off + j) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                           pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
     }
   }
   __syncthreads();
   for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    const int i = (j >> 8) * 8 + (j & 7), l = (j & 255) >> 3;
     float tp = 0.f, tq = 0.f;
-    for (int w = 0; w < nwarps; ++w) {
-      tp += s_red[w][j];
-      tq += s_red[w][D + j];
+#pragma unroll
+    for (int w = 0; w < kArnBwdWarps; ++w) {
+      tp += s_acc[w][0][i][l];
+      tq += s_acc[w][1][i][l];
     }
     atomicAdd(&dpost[j], tp);
     if (dpre != nullptr) atomicAdd(&dpre[j], tq);
@@ -408,128 +519,178 @@ __global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
   if (lane == 0) (is_q ? rq : rk)[static_cast<long long>(m) * (is_q ? Hq : Hkv) + (is_q ? hh : hh - Hq)] = r;
 }
 
-// head_dim 128 specialization: lane l owns elements 4l..4l+3 (8-byte accesses); the rotation
-// partner (j +- 64) lives in lane l ^ 16.
+// head_dim 128 specializations. A half-warp owns one 256-byte row: lane l (0..15 within the
+// half-warp) holds elements 8l..8l+7 (16-byte accesses) and its rotation partner (j +- 64) is lane
+// l ^ 8 of the same half-warp; reductions stay inside the half-warp (xor 8, 4, 2, 1). Each thread
+// issues the loads of all its rows before any math, so an SM keeps 64-128 KB of reads in flight,
+// which is what HBM3e needs to stream at full rate (one 8-byte load per thread reached ~40 %).
+constexpr int kQkFwdRows = 4;  // rows per half-warp, forward
+
+// Block (x, hh) handles head slot hh (q, k or v) of rows m = x*16*R + i*16 + hw (i < R): each row
+// is 256 contiguous bytes, so fixing the head per block costs no coalescing and needs no division.
 __global__ void __launch_bounds__(256) qk_norm_rope_fwd128_kernel(
     const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ qs, const float* __restrict__ ks,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ q,
     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v, float* __restrict__ rq, float* __restrict__ rk,
     int M, int T, int Hq, int Hkv, int start, int use_rope, float eps) {
   constexpr int Dh = 128;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
+  const int hh = blockIdx.y;
   const int H = Hq + 2 * Hkv;
-  const long long item = static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp;
-  if (item >= static_cast<long long>(M) * H) return;
-  const int m = static_cast<int>(item / H);
-  const int hh = static_cast<int>(item % H);
-  const uint2 raw = *reinterpret_cast<const uint2*>(qkv + item * Dh + lane * 4);
-  if (hh >= Hq + Hkv) {
-    *reinterpret_cast<uint2*>(v + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh + lane * 4) = raw;
+  const long long rstride = static_cast<long long>(H) * Dh;
+  const int m0 = blockIdx.x * 16 * kQkFwdRows + hw;
+  const __nv_bfloat16* src = qkv + static_cast<long long>(hh) * Dh + hl * 8;
+  uint4 raw[kQkFwdRows];
+#pragma unroll
+  for (int i = 0; i < kQkFwdRows; ++i) {
+    const int m = m0 + i * 16;
+    raw[i] = m < M ? *reinterpret_cast<const uint4*>(src + m * rstride) : make_uint4(0, 0, 0, 0);
+  }
+  if (hh >= Hq + Hkv) {  // v head: copied through
+    __nv_bfloat16* dst = v + static_cast<long long>(hh - Hq - Hkv) * Dh + hl * 8;
+#pragma unroll
+    for (int i = 0; i < kQkFwdRows; ++i) {
+      const int m = m0 + i * 16;
+      if (m < M) *reinterpret_cast<uint4*>(dst + static_cast<long long>(m) * Hkv * Dh) = raw[i];
+    }
     return;
   }
   const bool is_q = hh < Hq;
-  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  const float2 x01 = __bfloat1622float2(h2[0]), x23 = __bfloat1622float2(h2[1]);
-  float x[4] = {x01.x, x01.y, x23.x, x23.y};
-  const float r = rsqrtf(warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]) / Dh + eps);
-  const float4 sc = *reinterpret_cast<const float4*>((is_q ? qs : ks) + lane * 4);
-  x[0] *= r * (1.f + sc.x);
-  x[1] *= r * (1.f + sc.y);
-  x[2] *= r * (1.f + sc.z);
-  x[3] *= r * (1.f + sc.w);
-  float o[4] = {x[0], x[1], x[2], x[3]};
-  if (use_rope) {
-    const int pos = start + (m % T);
-    const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-    const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+  const int hsub = is_q ? hh : hh - Hq;
+  const int nh = is_q ? Hq : Hkv;
+  __nv_bfloat16* dst = (is_q ? q : k) + static_cast<long long>(hsub) * Dh + hl * 8;
+  float* rdst = (is_q ? rq : rk) + hsub;
+  float w[8];
+  load_f32x8((is_q ? qs : ks) + hl * 8, w);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
-      o[e] = lane < 16 ? x[e] * cc[e] - partner * ss[e] : partner * ss[e] + x[e] * cc[e];
+  for (int e = 0; e < 8; ++e) w[e] += 1.f;
+#pragma unroll
+  for (int i = 0; i < kQkFwdRows; ++i) {
+    const int m = m0 + i * 16;
+    float x[8];
+    unpack_bf16x8(raw[i], x);
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+    const float r = rsqrtf(half_warp_sum(ss) / Dh + eps);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] *= r * w[e];
+    if (use_rope) {
+      const int pos = start + ((m < M ? m : 0) % T);
+      float c[8], sn[8];
+      load_f32x8(cos_t + static_cast<long long>(pos) * 64 + (hl & 7) * 8, c);
+      load_f32x8(sin_t + static_cast<long long>(pos) * 64 + (hl & 7) * 8, sn);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, x[e], 8);
+        x[e] = hl < 8 ? x[e] * c[e] - partner * sn[e] : partner * sn[e] + x[e] * c[e];
+      }
+    }
+    if (m < M) {
+      *reinterpret_cast<uint4*>(dst + static_cast<long long>(m) * nh * Dh) = pack_bf16x8(x);
+      if (hl == 0) rdst[static_cast<long long>(m) * nh] = r;
     }
   }
-  uint2 out;
-  out.x = pack_bf16x2(o[0], o[1]);
-  out.y = pack_bf16x2(o[2], o[3]);
-  __nv_bfloat16* dst = is_q ? q + (static_cast<long long>(m) * Hq + hh) * Dh : k + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh;
-  *reinterpret_cast<uint2*>(dst + lane * 4) = out;
-  if (lane == 0) (is_q ? rq : rk)[static_cast<long long>(m) * (is_q ? Hq : Hkv) + (is_q ? hh : hh - Hq)] = r;
 }
 
-__global__ void __launch_bounds__(256) qk_norm_rope_bwd128_kernel(
+// Block (x, hh) handles head slot hh (a q, k or v head) of rows m = x*16*R + i*16 + hw, striding
+// over m; every row is 256 contiguous bytes, so a fixed head per block costs no coalescing and
+// gives each thread one kind of row: one set of scale weights and scale-gradient accumulators
+// (its 8 columns), reduced once per block at the end.
+template <int kQkBwdRows>
+__global__ void __launch_bounds__(256, kQkBwdRows >= 4 ? 3 : 4) qk_norm_rope_bwd128_kernel(
     const __nv_bfloat16* __restrict__ dq, const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv,
     const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ rq, const float* __restrict__ rk,
     const float* __restrict__ qs, const float* __restrict__ ks, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dqs,
     float* __restrict__ dks, int M, int T, int Hq, int Hkv, int start, int use_rope) {
   constexpr int Dh = 128;
-  __shared__ float s_acc[kRowsPerBlock][2][Dh];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    s_acc[warp][0][lane * 4 + e] = 0.f;
-    s_acc[warp][1][lane * 4 + e] = 0.f;
-  }
+  __shared__ float s_acc[16][Dh];
+  const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
+  const int hh = blockIdx.y;
   const int H = Hq + 2 * Hkv;
-  const long long total = static_cast<long long>(M) * H;
-  const float4 scq = *reinterpret_cast<const float4*>(qs + lane * 4);
-  const float4 sck = *reinterpret_cast<const float4*>(ks + lane * 4);
-  for (long long item = static_cast<long long>(blockIdx.x) * kRowsPerBlock + warp; item < total;
-       item += static_cast<long long>(gridDim.x) * kRowsPerBlock) {
-    const int m = static_cast<int>(item / H);
-    const int hh = static_cast<int>(item % H);
-    __nv_bfloat16* out = dqkv + item * Dh + lane * 4;
-    if (hh >= Hq + Hkv) {
-      *reinterpret_cast<uint2*>(out) =
-          *reinterpret_cast<const uint2*>(dv + (static_cast<long long>(m) * Hkv + (hh - Hq - Hkv)) * Dh + lane * 4);
-      continue;
-    }
-    const bool is_q = hh < Hq;
-    const __nv_bfloat16* gsrc = is_q ? dq + (static_cast<long long>(m) * Hq + hh) * Dh
-                                     : dk + (static_cast<long long>(m) * Hkv + (hh - Hq)) * Dh;
-    const uint2 graw = *reinterpret_cast<const uint2*>(gsrc + lane * 4);
-    const uint2 xraw = *reinterpret_cast<const uint2*>(qkv + item * Dh + lane * 4);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&graw);
-    const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xraw);
-    const float2 g01 = __bfloat1622float2(g2[0]), g23 = __bfloat1622float2(g2[1]);
-    const float2 x01 = __bfloat1622float2(x2[0]), x23 = __bfloat1622float2(x2[1]);
-    float g[4] = {g01.x, g01.y, g23.x, g23.y};
-    const float x[4] = {x01.x, x01.y, x23.x, x23.y};
-    if (use_rope) {
-      const int pos = start + (m % T);
-      const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-      const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(pos) * 64 + (lane & 15) * 4);
-      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
-      float gn[4];
+  const long long rstride = static_cast<long long>(H) * Dh;
+  const int step = gridDim.x * 16 * kQkBwdRows;
+  if (hh >= Hq + Hkv) {  // v head: the gradient passes through
+    const __nv_bfloat16* src = dv + static_cast<long long>(hh - Hq - Hkv) * Dh + hl * 8;
+    for (int m0 = blockIdx.x * 16 * kQkBwdRows; m0 < M; m0 += step) {
+      uint4 g[kQkBwdRows];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float partner = __shfl_xor_sync(0xffffffffu, g[e], 16);
-        gn[e] = lane < 16 ? g[e] * cc[e] + partner * ss[e] : -partner * ss[e] + g[e] * cc[e];
+      for (int i = 0; i < kQkBwdRows; ++i) {
+        const int m = m0 + i * 16 + hw;
+        g[i] = m < M ? *reinterpret_cast<const uint4*>(src + static_cast<long long>(m) * Hkv * Dh) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) g[e] = gn[e];
+      for (int i = 0; i < kQkBwdRows; ++i) {
+        const int m = m0 + i * 16 + hw;
+        if (m < M) *reinterpret_cast<uint4*>(dqkv + m * rstride + static_cast<long long>(hh) * Dh + hl * 8) = g[i];
+      }
     }
-    const float4 sc = is_q ? scq : sck;
-    const float w[4] = {1.f + sc.x, 1.f + sc.y, 1.f + sc.z, 1.f + sc.w};
-    const float r = is_q ? rq[static_cast<long long>(m) * Hq + hh] : rk[static_cast<long long>(m) * Hkv + (hh - Hq)];
-    const float dot = warp_sum(g[0] * w[0] * x[0] + g[1] * w[1] * x[1] + g[2] * w[2] * x[2] + g[3] * w[3] * x[3]) / Dh;
-    float d[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      d[e] = r * w[e] * g[e] - x[e] * r * r * r * dot;
-      s_acc[warp][is_q ? 0 : 1][lane * 4 + e] += g[e] * x[e] * r;
-    }
-    uint2 o;
-    o.x = pack_bf16x2(d[0], d[1]);
-    o.y = pack_bf16x2(d[2], d[3]);
-    *reinterpret_cast<uint2*>(out) = o;
+    return;
   }
+  const bool is_q = hh < Hq;
+  const int hsub = is_q ? hh : hh - Hq;
+  const int nh = is_q ? Hq : Hkv;
+  const __nv_bfloat16* gbase = (is_q ? dq : dk) + static_cast<long long>(hsub) * Dh + hl * 8;
+  const float* rbase = (is_q ? rq : rk) + hsub;
+  float w[8], acc[8];
+  load_f32x8((is_q ? qs : ks) + hl * 8, w);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    w[e] += 1.f;
+    acc[e] = 0.f;
+  }
+  for (int m0 = blockIdx.x * 16 * kQkBwdRows; m0 < M; m0 += step) {
+    uint4 graw[kQkBwdRows], xraw[kQkBwdRows];
+    float rr[kQkBwdRows];
+#pragma unroll
+    for (int i = 0; i < kQkBwdRows; ++i) {
+      const int m = m0 + i * 16 + hw;
+      const bool live = m < M;
+      graw[i] = live ? *reinterpret_cast<const uint4*>(gbase + static_cast<long long>(m) * nh * Dh) : make_uint4(0, 0, 0, 0);
+      xraw[i] = live ? *reinterpret_cast<const uint4*>(qkv + m * rstride + static_cast<long long>(hh) * Dh + hl * 8)
+                     : make_uint4(0, 0, 0, 0);
+      rr[i] = live ? rbase[static_cast<long long>(m) * nh] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < kQkBwdRows; ++i) {
+      const int m = m0 + i * 16 + hw;
+      float g[8], x[8];
+      unpack_bf16x8(graw[i], g);
+      unpack_bf16x8(xraw[i], x);
+      if (use_rope) {
+        const int pos = start + ((m < M ? m : 0) % T);
+        float c[8], sn[8];
+        load_f32x8(cos_t + static_cast<long long>(pos) * 64 + (hl & 7) * 8, c);
+        load_f32x8(sin_t + static_cast<long long>(pos) * 64 + (hl & 7) * 8, sn);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float partner = __shfl_xor_sync(0xffffffffu, g[e], 8);
+          g[e] = hl < 8 ? g[e] * c[e] + partner * sn[e] : -partner * sn[e] + g[e] * c[e];
+        }
+      }
+      const float r = rr[i];
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dot += g[e] * w[e] * x[e];
+      dot = half_warp_sum(dot) / Dh;
+      float d[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        d[e] = r * w[e] * g[e] - x[e] * r * r * r * dot;
+        acc[e] += g[e] * x[e] * r;  // rows past M have g = 0
+      }
+      if (m < M) *reinterpret_cast<uint4*>(dqkv + m * rstride + static_cast<long long>(hh) * Dh + hl * 8) = pack_bf16x8(d);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s_acc[hw][hl * 8 + e] = acc[e];
   __syncthreads();
-  for (int j = threadIdx.x; j < 2 * Dh; j += blockDim.x) {
+  if (threadIdx.x < Dh) {
     float t = 0.f;
-    for (int w = 0; w < kRowsPerBlock; ++w) t += s_acc[w][j / Dh][j % Dh];
-    atomicAdd(j < Dh ? &dqs[j] : &dks[j - Dh], t);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) t += s_acc[r][threadIdx.x];
+    atomicAdd((is_q ? dqs : dks) + threadIdx.x, t);
   }
 }
 
@@ -731,7 +892,28 @@ std::vector<at::Tensor> add_rmsnorm_fwd(const at::Tensor& res, const at::Tensor&
   auto st = at::cuda::getCurrentCUDAStream();
   const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
   const float* pre_p = has_pre ? pre->data_ptr<float>() : nullptr;
-  if (y_dt == at::kFloat) {
+  if (D % 256 == 0 && D <= 1024) {
+    const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+#define MINT_ARN_FWD_REG(VPT)                                                                                    \
+  if (y_dt == at::kFloat) {                                                                                      \
+    add_rmsnorm_fwd_reg_kernel<VPT, float><<<grid, 256, 0, st>>>(                                               \
+        res.data_ptr<float>(), ap, post.data_ptr<float>(), pre_p, h.data_ptr<float>(),                           \
+        has_pre ? y.data_ptr<float>() : nullptr, ra.data_ptr<float>(), has_pre ? rh.data_ptr<float>() : nullptr, \
+        rows, static_cast<float>(eps));                                                                          \
+  } else {                                                                                                       \
+    add_rmsnorm_fwd_reg_kernel<VPT, __nv_bfloat16><<<grid, 256, 0, st>>>(                                       \
+        res.data_ptr<float>(), ap, post.data_ptr<float>(), pre_p, h.data_ptr<float>(),                           \
+        has_pre ? reinterpret_cast<__nv_bfloat16*>(y.data_ptr()) : nullptr, ra.data_ptr<float>(),                \
+        has_pre ? rh.data_ptr<float>() : nullptr, rows, static_cast<float>(eps));                                \
+  }
+    switch (D / 32) {
+      case 8: MINT_ARN_FWD_REG(8); break;
+      case 16: MINT_ARN_FWD_REG(16); break;
+      case 24: MINT_ARN_FWD_REG(24); break;
+      default: MINT_ARN_FWD_REG(32); break;
+    }
+#undef MINT_ARN_FWD_REG
+  } else if (y_dt == at::kFloat) {
     add_rmsnorm_fwd_kernel<float><<<grid, 256, 0, st>>>(
         res.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()), post.data_ptr<float>(), pre_p,
         h.data_ptr<float>(), has_pre ? y.data_ptr<float>() : nullptr, ra.data_ptr<float>(),
@@ -776,10 +958,10 @@ std::vector<at::Tensor> add_rmsnorm_bwd(const c10::optional<at::Tensor>& dh, con
   const float* dh_p = (dh.has_value() && dh->defined()) ? dh->data_ptr<float>() : nullptr;
   const bool has_dy = dy.has_value() && dy->defined() && has_pre;
   if ((!has_dy || dy->scalar_type() == at::kBFloat16) && D % 256 == 0 && D <= 768) {
-    // register-resident kernel: 8 warps per block, ~2 blocks per SM
-    const int grid_r = std::min<int>((rows + 7) / 8, num_sms(h.get_device()) * 2);
+    // register-resident kernel: 4 warps per block, ~5 blocks per SM
+    const int grid_r = std::min<int>((rows + kArnBwdWarps - 1) / kArnBwdWarps, num_sms(h.get_device()) * 5);
 #define MINT_ARN_BWD_REG(VPT)                                                                                   \
-  add_rmsnorm_bwd_reg_kernel<VPT><<<grid_r, 256, 0, st>>>(                                                     \
+  add_rmsnorm_bwd_reg_kernel<VPT><<<grid_r, kArnBwdWarps * 32, 0, st>>>(                                                     \
       dh_p, has_dy ? reinterpret_cast<const __nv_bfloat16*>(dy->data_ptr()) : nullptr,                          \
       reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()), h.data_ptr<float>(), rstd_a.data_ptr<float>(),      \
       has_pre ? rstd_h.data_ptr<float>() : nullptr, post.data_ptr<float>(), has_pre ? pre->data_ptr<float>() : nullptr, \
@@ -836,7 +1018,9 @@ std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, int64_t n_q, int
   auto st = at::cuda::getCurrentCUDAStream();
   const int grid = static_cast<int>((items + kRowsPerBlock - 1) / kRowsPerBlock);
   if (Dh == 128) {
-    qk_norm_rope_fwd128_kernel<<<grid, 256, 0, st>>>(
+    const dim3 grid128(static_cast<unsigned>((M + 16 * kQkFwdRows - 1) / (16 * kQkFwdRows)),
+                       static_cast<unsigned>(n_q + 2 * n_kv));
+    qk_norm_rope_fwd128_kernel<<<grid128, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qs.data_ptr<float>(), ks.data_ptr<float>(),
         cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q.data_ptr()),
         reinterpret_cast<__nv_bfloat16*>(k.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v.data_ptr()),
@@ -880,7 +1064,16 @@ std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor&
   const long long cap = static_cast<long long>(num_sms(qkv.get_device())) * 8;
   const int grid = static_cast<int>(want < cap ? want : cap);
   if (Dh == 128) {
-    qk_norm_rope_bwd128_kernel<<<grid, 256, 0, st>>>(
+    const int H = static_cast<int>(n_q + 2 * n_kv);
+    static const int rows_env = [] {
+      const char* e = std::getenv("MINT_QK_BWD_ROWS");
+      return e != nullptr && std::atoi(e) == 2 ? 2 : 4;
+    }();
+    const long long gx_want = (M + 16 * rows_env - 1) / (16 * rows_env);
+    const long long gx_cap = std::max<long long>(1, (static_cast<long long>(num_sms(qkv.get_device())) * 8 + H - 1) / H);
+    const dim3 grid128(static_cast<unsigned>(std::min(gx_want, gx_cap)), static_cast<unsigned>(H));
+    auto kern = rows_env == 2 ? qk_norm_rope_bwd128_kernel<2> : qk_norm_rope_bwd128_kernel<4>;
+    kern<<<grid128, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(dq.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dk.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
         rq.data_ptr<float>(), rk.data_ptr<float>(), qs.data_ptr<float>(), ks.data_ptr<float>(),
