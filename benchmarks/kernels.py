@@ -216,7 +216,14 @@ def run_norm(a: argparse.Namespace) -> dict:
         "add_rmsnorm_bwd": (lambda: C.add_rmsnorm_bwd(dh_, dy, x, h, ra, rh, post, pre),
                             M * D * (e4 + e2 + e2 + e4) + M * D * (e4 + e2) + 2 * M * e4),
     }
-    out = {"M": M, "D": D, "hq": hq, "hkv": hkv, "peak_gbs": peak, "peak": kind}
+    V = a.V
+    logits = torch.randn(M, V, device="cuda", dtype=torch.bfloat16)
+    tgt = torch.randint(0, V, (M,), device="cuda")
+    cmask = torch.ones(M, device="cuda")
+    denom = torch.full((1,), float(M), device="cuda")
+    # in place: every timed call rewrites the logits with gradients (same traffic, values irrelevant)
+    cases["ce_fused_fwd_bwd"] = (lambda: C.ce_fused_fwd_bwd(logits, tgt, cmask, denom, V, 0), 2 * M * V * e2)
+    out = {"M": M, "D": D, "hq": hq, "hkv": hkv, "V": V, "peak_gbs": peak, "peak": kind}
     for name, (fn, nbytes) in cases.items():
         t = time_fn(fn, a.iters)
         out[f"{name}_ms"] = t
@@ -247,6 +254,7 @@ def main() -> None:
     nm.add_argument("--D", type=int, default=768)
     nm.add_argument("--hq", type=int, default=6)
     nm.add_argument("--hkv", type=int, default=6)
+    nm.add_argument("--V", type=int, default=65536)
     for p in (at, gm, nm):
         p.add_argument("--iters", type=int, default=10)
         p.add_argument("--once", action="store_true")

@@ -270,24 +270,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int doc_k = (p.doc != nullptr && kj < p.T) ? p.doc[static_cast<long long>(b) * p.T + kj] : 0;
     const int2 dk = (doc_sorted && kj < p.T) ? db[kj] : make_int2(0, p.T);
     bool ok = n > 0;
+    // this thread's LSE (threads 0..127, log2 units) or delta (128..255) value of query tile `it`,
+    // loaded one iteration ahead so the global-memory latency overlaps the previous tile's work
+    auto stage_value = [&](int it) -> float {
+      const int h = hk * G + it / nq;
+      const int qi = (i0 + it % nq) * kB + (mt & (kB - 1));
+      const long long rowbase = (static_cast<long long>(b) * p.Hq + h) * p.T;
+      if (mt < kB) return qi < p.T ? p.lse[rowbase + qi] * 1.4426950408889634f : INFINITY;
+      return qi < p.T ? p.delta[rowbase + qi] : 0.f;
+    };
+    float staged = n > 0 ? stage_value(0) : 0.f;
     for (int it = 0; it < n && ok; ++it) {
       const uint32_t ph = it & 1;
       const int h = hk * G + it / nq;
       const int q0 = (i0 + it % nq) * kB;
       const int q_last = min(p.T, q0 + kB) - 1;
-      // stage this query tile's LSE (log2 units) and delta once every math warp is done with the
-      // previous tile's values
+      // stage this query tile's LSE and delta once every math warp is done with the previous tile's
       if (it > 0 && !(ok = mbar_wait_warp(&s.stg_free, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag))) break;
-      {
-        const int c = mt & (kB - 1);
-        const int qi = q0 + c;
-        const long long rowbase = (static_cast<long long>(b) * p.Hq + h) * p.T;
-        if (mt < kB) {
-          s.lse2[c] = qi < p.T ? p.lse[rowbase + qi] * 1.4426950408889634f : INFINITY;
-        } else {
-          s.dlt[c] = qi < p.T ? p.delta[rowbase + qi] : 0.f;
-        }
+      if (mt < kB) {
+        s.lse2[mt] = staged;
+      } else {
+        s.dlt[mt - kB] = staged;
       }
+      if (it + 1 < n) staged = stage_value(it + 1);
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.stg_full);
       if (!(ok = mbar_wait_warp(&s.stg_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;

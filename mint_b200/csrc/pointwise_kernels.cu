@@ -182,33 +182,46 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Per-row max and sum-exp over the first `valid` columns of a bf16 row (8 elements per vector load).
+__device__ __forceinline__ void max_sumexp8(const uint4& u, int j, int valid, float& mx, float& se) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+  float x[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(p[e]);
+    x[2 * e] = f.x;
+    x[2 * e + 1] = f.y;
+  }
+  float lm = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    if (j + e < valid) lm = fmaxf(lm, x[e]);
+  if (lm > mx) {
+    se *= exp2f((mx - lm) * kLog2e);
+    mx = lm;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    if (j + e < valid) se += exp2f((x[e] - mx) * kLog2e);
+}
+
+// Row max and sum of exp(x - max) over the first `valid` columns. The vector path issues four
+// 16-byte loads per thread before using any (64 KB in flight per 512-thread block), which keeps
+// HBM streaming where one load at a time left it latency-bound.
 __device__ __forceinline__ void row_max_sumexp(const __nv_bfloat16* __restrict__ row, int V, int valid, float* red,
                                                float& mx_out, float& se_out) {
   float mx = -INFINITY, se = 0.f;
   const bool vec = (V & 7) == 0;
   if (vec) {
-    for (int j = threadIdx.x * 8; j < V; j += blockDim.x * 8) {
-      const uint4 u = *reinterpret_cast<const uint4*>(row + j);
-      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
-      float x[8];
+    const int step = blockDim.x * 8;
+    int j = threadIdx.x * 8;
+    for (; j + 3 * step < V; j += 4 * step) {
+      uint4 u[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(p[e]);
-        x[2 * e] = f.x;
-        x[2 * e + 1] = f.y;
-      }
-      float lm = -INFINITY;
+      for (int k = 0; k < 4; ++k) u[k] = *reinterpret_cast<const uint4*>(row + j + k * step);
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (j + e < valid) lm = fmaxf(lm, x[e]);
-      if (lm > mx) {
-        se *= exp2f((mx - lm) * kLog2e);
-        mx = lm;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (j + e < valid) se += exp2f((x[e] - mx) * kLog2e);
+      for (int k = 0; k < 4; ++k) max_sumexp8(u[k], j + k * step, valid, mx, se);
     }
+    for (; j < V; j += step) max_sumexp8(*reinterpret_cast<const uint4*>(row + j), j, valid, mx, se);
   } else {
     for (int j = threadIdx.x; j < valid; j += blockDim.x) {
       const float x = __bfloat162float(row[j]);
@@ -226,24 +239,39 @@ __device__ __forceinline__ void row_max_sumexp(const __nv_bfloat16* __restrict__
 }
 
 // grad[j] = (softmax_j - [j == t]) * scale for j < valid, 0 for padded columns; written in place.
+__device__ __forceinline__ uint4 grad8(uint4 u, int j, int valid, float lse, long long t_local, float scale) {
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(p[e]);
+    const int c0 = j + 2 * e, c1 = c0 + 1;
+    float g0 = c0 < valid ? exp2f((f.x - lse) * kLog2e) : 0.f;
+    float g1 = c1 < valid ? exp2f((f.y - lse) * kLog2e) : 0.f;
+    if (c0 == t_local) g0 -= 1.f;
+    if (c1 == t_local) g1 -= 1.f;
+    p[e] = __floats2bfloat162_rn(g0 * scale, g1 * scale);
+  }
+  return u;
+}
+
+// softmax(x) - onehot(target), times `scale`, written over the row (four loads in flight per thread)
 __device__ __forceinline__ void row_write_grad(__nv_bfloat16* __restrict__ row, int V, int valid, float lse,
                                                long long t_local, float scale) {
   const bool vec = (V & 7) == 0;
   if (vec) {
-    for (int j = threadIdx.x * 8; j < V; j += blockDim.x * 8) {
-      uint4 u = *reinterpret_cast<const uint4*>(row + j);
-      __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&u);
+    const int step = blockDim.x * 8;
+    int j = threadIdx.x * 8;
+    for (; j + 3 * step < V; j += 4 * step) {
+      uint4 u[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(p[e]);
-        const int c0 = j + 2 * e, c1 = c0 + 1;
-        float g0 = c0 < valid ? exp2f((f.x - lse) * kLog2e) : 0.f;
-        float g1 = c1 < valid ? exp2f((f.y - lse) * kLog2e) : 0.f;
-        if (c0 == t_local) g0 -= 1.f;
-        if (c1 == t_local) g1 -= 1.f;
-        p[e] = __floats2bfloat162_rn(g0 * scale, g1 * scale);
-      }
-      *reinterpret_cast<uint4*>(row + j) = u;
+      for (int k = 0; k < 4; ++k) u[k] = *reinterpret_cast<const uint4*>(row + j + k * step);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        *reinterpret_cast<uint4*>(row + j + k * step) = grad8(u[k], j + k * step, valid, lse, t_local, scale);
+    }
+    for (; j < V; j += step) {
+      *reinterpret_cast<uint4*>(row + j) =
+          grad8(*reinterpret_cast<const uint4*>(row + j), j, valid, lse, t_local, scale);
     }
   } else {
     for (int j = threadIdx.x; j < V; j += blockDim.x) {
@@ -256,7 +284,7 @@ __device__ __forceinline__ void row_write_grad(__nv_bfloat16* __restrict__ row, 
 
 // Single-GPU fused CE: per row loss = lse - logit[target]; gradient logits written in place,
 // scaled by mask[row] / denom. The second pass re-reads the row, which is still in L2.
-__global__ void __launch_bounds__(512) ce_fused_kernel(__nv_bfloat16* __restrict__ logits,
+__global__ void __launch_bounds__(512, 3) ce_fused_kernel(__nv_bfloat16* __restrict__ logits,
                                                        const int64_t* __restrict__ targets,
                                                        const float* __restrict__ mask, const float* __restrict__ denom,
                                                        float* __restrict__ row_loss, int M, int V, int valid,
@@ -278,7 +306,7 @@ __global__ void __launch_bounds__(512) ce_fused_kernel(__nv_bfloat16* __restrict
 }
 
 // TP pass 1: local max, local sum-exp relative to it, and the target logit if this shard owns it
-__global__ void __launch_bounds__(512) ce_stats_kernel(const __nv_bfloat16* __restrict__ logits,
+__global__ void __launch_bounds__(512, 3) ce_stats_kernel(const __nv_bfloat16* __restrict__ logits,
                                                        const int64_t* __restrict__ targets, float* __restrict__ out_mx,
                                                        float* __restrict__ out_se, float* __restrict__ out_tl, int M,
                                                        int V, int valid, long long vstart) {
@@ -297,7 +325,7 @@ __global__ void __launch_bounds__(512) ce_stats_kernel(const __nv_bfloat16* __re
 }
 
 // TP pass 2: gradient logits in place given the global lse
-__global__ void __launch_bounds__(512) ce_grad_kernel(__nv_bfloat16* __restrict__ logits,
+__global__ void __launch_bounds__(512, 3) ce_grad_kernel(__nv_bfloat16* __restrict__ logits,
                                                       const int64_t* __restrict__ targets,
                                                       const float* __restrict__ mask, const float* __restrict__ lse,
                                                       const float* __restrict__ denom, int M, int V, int valid,
