@@ -14,6 +14,8 @@
 //               P (bf16) in the 128B-swizzled K-major layout the PV MMA reads, and finally
 //               normalizes its half of O and stores O and the log-sum-exp.
 // Tiles outside the causal / window band are never visited. All waits are bounded.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -36,6 +38,8 @@ struct FwdParams {
   int B, T, Hq, Hkv;
   int causal, window;     // window < 0: none
   float scale_log2;       // softmax scale * log2(e)
+  int diag;               // timing diagnostics (MINT_FA_DIAG bits): 1 exp2 replaced by a multiply-add,
+                          // 2 MMAs not issued (results meaningless; for isolating pipeline stages)
   uint32_t* status;
 };
 
@@ -175,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(&s.q_full, 0, p.status, kStatusTimeoutAttention, abort_flag);
       if (ok && (ok = mbar_wait(&s.k_full[0], 0, p.status, kStatusTimeoutAttention, abort_flag))) {
         tc_fence_after();
-        issue_qk(tmem, q_addr, smem_u32(s.k[0]));
+        if (!(p.diag & 2)) issue_qk(tmem, q_addr, smem_u32(s.k[0]));
         umma_commit(&s.s_full[0]);
         umma_commit(&s.k_empty[0]);
       }
@@ -184,14 +188,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st = (t + 1) & 1;
           if (!mbar_wait(&s.k_full[st], ((t + 1) >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
           tc_fence_after();
-          issue_qk(tmem + st * 128, q_addr, smem_u32(s.k[st]));
+          if (!(p.diag & 2)) issue_qk(tmem + st * 128, q_addr, smem_u32(s.k[st]));
           umma_commit(&s.s_full[st]);
           umma_commit(&s.k_empty[st]);
         }
         if (!mbar_wait(&s.p_full, t & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
         if (!mbar_wait(&s.v_full[t & 1], (t >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
         tc_fence_after();
-        issue_pv(tmem_o, p_addr, smem_u32(s.v[t & 1]), t > 0);
+        if (!(p.diag & 2)) issue_pv(tmem_o, p_addr, smem_u32(s.v[t & 1]), t > 0);
         umma_commit(&s.pv_done);
         umma_commit(&s.v_empty[t & 1]);
       }
@@ -307,8 +311,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       float rs = 0.f;
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float a = (m == -INFINITY) ? 0.f : exp2f(x[2 * c] - m);
-        const float bb = (m == -INFINITY) ? 0.f : exp2f(x[2 * c + 1] - m);
+        float a, bb;
+        if (p.diag & 1) {
+          a = (m == -INFINITY) ? 0.f : fmaf(x[2 * c] - m, 0.01f, 1.f);
+          bb = (m == -INFINITY) ? 0.f : fmaf(x[2 * c + 1] - m, 0.01f, 1.f);
+        } else {
+          a = (m == -INFINITY) ? 0.f : exp2f(x[2 * c] - m);
+          bb = (m == -INFINITY) ? 0.f : exp2f(x[2 * c + 1] - m);
+        }
         rs += a + bb;
         pk[c] = pack_bf16x2(a, bb);
       }
@@ -480,6 +490,11 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k,
   p.window = static_cast<int>(window);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.status = status_ptr(q.get_device());
+  static const int diag = [] {
+    const char* e = std::getenv("MINT_FA_DIAG");
+    return e == nullptr ? 0 : std::atoi(e);
+  }();
+  p.diag = diag;
   const CUtensorMap tq = make_tmap_3d_bf16(q.data_ptr(), fa::kD, Hq, static_cast<uint64_t>(B) * T, fa::kD,
                                            static_cast<uint64_t>(Hq) * fa::kD, 64, 1, 128, true);
   const CUtensorMap tk = make_tmap_3d_bf16(k.data_ptr(), fa::kD, Hkv, static_cast<uint64_t>(B) * T, fa::kD,
