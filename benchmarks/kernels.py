@@ -45,8 +45,12 @@ def flush_l2() -> None:
     _FLUSH.fill_(1.0)
 
 
+REPEAT = 1  # calls per timed sample (--repeat): > 1 hides the host-side launch cost of one call
+
+
 def time_fn(fn, iters: int, warmup: int = 3) -> float:  # noqa: ANN001
-    """Median milliseconds of ``fn()`` over ``iters`` runs, L2 flushed before each."""
+    """Median milliseconds per call of ``fn()`` over ``iters`` samples of REPEAT back-to-back calls,
+    L2 flushed before each sample."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -55,10 +59,11 @@ def time_fn(fn, iters: int, warmup: int = 3) -> float:  # noqa: ANN001
         flush_l2()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        fn()
+        for _ in range(REPEAT):
+            fn()
         e.record()
         torch.cuda.synchronize()
-        times.append(s.elapsed_time(e))
+        times.append(s.elapsed_time(e) / REPEAT)
     return statistics.median(times)
 
 
@@ -257,9 +262,13 @@ def main() -> None:
     nm.add_argument("--V", type=int, default=65536)
     for p in (at, gm, nm):
         p.add_argument("--iters", type=int, default=10)
+        p.add_argument("--repeat", type=int, default=1,
+                       help="back-to-back calls per timed sample (the first reads a flushed L2, the rest a warm one)")
         p.add_argument("--once", action="store_true")
         p.add_argument("--once-lib", action="store_true", help="run the library (cuBLAS / SDPA) path once")
     a = ap.parse_args()
+    global REPEAT
+    REPEAT = max(1, a.repeat)
     res = {"attn": run_attn, "gemm": run_gemm, "norm": run_norm}[a.cmd](a)
     _ext.check_device_status()
     print(json.dumps(res), flush=True)

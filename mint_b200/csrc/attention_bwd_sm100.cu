@@ -314,11 +314,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.causal) keep = keep && kj <= qi;
           if (p.window >= 0) keep = keep && qi - kj <= p.window;
           if (p.doc != nullptr && !doc_sorted && keep) keep = p.doc[static_cast<long long>(b) * p.T + qi] == doc_k;
-          x[c] = keep ? exp2f(x[c] * p.scale_log2 - lse2[c]) : 0.f;
+          const float t = fmaf(x[c], p.scale_log2, -lse2[c]);
+          x[c] = keep ? ((c & 1) ? exp2_poly(t) : exp2f(t)) : 0.f;
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = exp2f(x[c] * p.scale_log2 - lse2[c]);
+        for (int c = 0; c < 64; ++c) {
+          // half of the exponentials on the MUFU unit, half as a polynomial on the FMA pipe
+          const float t = fmaf(x[c], p.scale_log2, -lse2[c]);
+          x[c] = (c & 1) ? exp2_poly(t) : exp2f(t);
+        }
       }
       // the shared P/dS tile is free: dK_{i-1} / dQ_{i-1} (dq_full_{i-1}) finished reading dS_{i-1}, and
       // this warp's dQ_{i-1} reduce-adds (staged in the same bytes it now writes) read their source
@@ -382,7 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.dq_free);
     }
-    if (lane == 0) bulk_wait_all();  // dQ reductions done before the shared memory is released
+    // the dQ reductions have read their shared-memory sources before it is released (their global
+    // writes complete with the grid, before any later kernel on the stream reads dQ)
+    if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
     // dK / dV rows: TMEM lane = key index (tcgen05.ld is warp-collective: every lane loads)
     ok = __all_sync(0xffffffffu, ok);

@@ -107,7 +107,7 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_addr, uint3
 
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                  const __grid_constant__ CUtensorMap tv, FwdParams p) {
+                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -358,6 +358,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = qi < p.T;
+      // rows of warps whose 32 rows all lie inside the sequence leave through shared memory (the Q
+      // tile is free: every MMA reading it completed) and one TMA store per warp; the others (the
+      // sequence's ragged last tile) store directly, so no row of the next sequence is touched
+      const bool via_tma = q0 + q * 32 + 32 <= p.T;
       __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + (row_ok ? qi : 0)) * p.Hq + h) * kD + cb;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -372,8 +376,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           v4.y = pack_bf16x2(__uint_as_float(u[e + 2]) * inv, __uint_as_float(u[e + 3]) * inv);
           v4.z = pack_bf16x2(__uint_as_float(u[e + 4]) * inv, __uint_as_float(u[e + 5]) * inv);
           v4.w = pack_bf16x2(__uint_as_float(u[e + 6]) * inv, __uint_as_float(u[e + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + c * 32 + e) = v4;
+          if (via_tma) {
+            const int chunk = c * 4 + (e >> 3);  // 16-byte chunk of this half row, 128B swizzle
+            *reinterpret_cast<uint4*>(s.q + half * kAtomBytes + r * 128 + ((chunk ^ (r & 7)) << 4)) = v4;
+          } else {
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v4;
+          }
         }
+      }
+      if (via_tma) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&to, s.q + half * kAtomBytes + q * 32 * 128, cb, h, b * p.T + q0 + q * 32);
+          bulk_commit();
+          bulk_wait_read<0>();  // the shared memory must stay valid until the store has read it
+        }
+        __syncwarp();
       }
       // natural-log LSE of the scaled scores: (m + log2 l) * ln 2
       if (row_ok && half == 0) {
@@ -510,7 +529,10 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k,
     configured[dev & 63] = true;
   }
   dim3 grid((T + fa::kBM - 1) / fa::kBM, Hq, B);
-  fa::fa_fwd_kernel<<<grid, fa::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  // O leaves in 32-row x 64-dim boxes, one TMA store per softmax warp
+  const CUtensorMap to = make_tmap_3d_bf16(o.data_ptr(), fa::kD, Hq, static_cast<uint64_t>(B) * T, fa::kD,
+                                           static_cast<uint64_t>(Hq) * fa::kD, 64, 1, 32, true);
+  fa::fa_fwd_kernel<<<grid, fa::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, to, p);
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
   return {o, lse};

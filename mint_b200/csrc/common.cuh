@@ -417,6 +417,25 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// 2^t for t <= 0 on the FMA pipe, for kernels whose exponentials would otherwise saturate the
+// MUFU unit (attention softmax: one exponential per score). Cody-Waite range reduction: n = round(t)
+// by adding 1.5 * 2^23 (the integer lands in the low mantissa bits), f = t - n in [-0.5, 0.5];
+// 2^f from a degree-3 polynomial whose coefficients are a relative-error least-squares fit on 2000
+// Chebyshev nodes of [-0.5, 0.5] (computed for this file with numpy; max relative error 7.8e-5,
+// far below the bf16 rounding of the probabilities it feeds); 2^n added to the exponent bits.
+// Returns 0 for t < -125 (and for -inf).
+__device__ __forceinline__ float exp2_poly(float t) {
+  const float tc = fmaxf(t, -125.f);
+  const float j = tc + 12582912.f;  // 1.5 * 2^23: round to nearest integer
+  const float n = j - 12582912.f;
+  const float f = tc - n;
+  float p = fmaf(0.05508868396282196f, f, 0.24260404706001282f);
+  p = fmaf(p, f, 0.6932762265205383f);
+  p = fmaf(p, f, 0.9999289512634277f);
+  const int bits = __float_as_int(p) + ((__float_as_int(j) - 0x4B400000) << 23);
+  return t < -125.f ? 0.f : __int_as_float(bits);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
