@@ -246,6 +246,8 @@ def main() -> None:
     ap.add_argument("--micro-batch", type=int, default=0, help="override micro-batch per dp rank")
     ap.add_argument("--matrix-optimizer", choices=["muon", "adamw"], default="muon")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-same-optimizer", action="store_true",
+                    help="skip the extra all-AdamW measurement (the reference arm's optimizer)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -352,6 +354,35 @@ def main() -> None:
 
         _ext.check_device_status()
 
+    same_opt = None
+    if args.impl == "ours" and args.matrix_optimizer == "muon" and not args.no_same_optimizer:
+        # the same step with the reference arm's optimizer (AdamW on every group), so that a ratio
+        # against the reference compares identical work; the NorMuon number above stays the headline
+        del step
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        args_a = argparse.Namespace(**{**vars(args), "matrix_optimizer": "adamw"})
+        _dev2, step_a, _ = build_ours(args_a, cfg, lay)
+        for i in range(args.warmup):
+            x, y = dev_batches[i % 2]
+            step_a(x, y, mask, doc)
+        torch.cuda.synchronize()
+        barrier()
+        sa, ea = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sa.record()
+        for i in range(args.steps):
+            x, y = dev_batches[i % 2]
+            loss_a = step_a(x, y, mask, doc)
+        ea.record()
+        torch.cuda.synchronize()
+        ms_a = max_over_ranks(sa.elapsed_time(ea) / args.steps)
+        same_opt = {"matrix_optimizer": "adamw", "value": mb * T * dp / (ms_a / 1e3), "unit": "tokens/s",
+                    "ms_per_step": ms_a, "final_loss": float(loss_a.detach()),
+                    "how": "same model, data and timing; AdamW on every parameter group as the reference's "
+                           "configure_optimizer (device-timed, max over ranks)"}
+        if ext is not None:
+            _ext.check_device_status()
+
     tok_s = mb * T * dp / (ms / 1e3)
     pk = peaks()
     fpt = flops_per_token(cfg)
@@ -368,6 +399,8 @@ def main() -> None:
         })
         if e2e is not None:
             line["e2e"] = e2e
+        if same_opt is not None:
+            line["same_optimizer_as_reference"] = same_opt
         print(json.dumps(line), flush=True)
     if _dist.is_available() and _dist.is_initialized():
         barrier()

@@ -35,7 +35,18 @@ std::vector<at::Tensor> ce_row_stats(const at::Tensor& logits, const at::Tensor&
 void ce_grad_inplace(at::Tensor& logits, const at::Tensor& targets, const at::Tensor& mask, const at::Tensor& lse,
                      const at::Tensor& denom, int64_t valid, int64_t vstart);
 void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1, double b2,
-                double eps, double wd, int64_t step);
+                double eps, double wd, int64_t step, const c10::optional<at::Tensor>& gscale);
+void normuon_prep(const at::Tensor& gptrs, at::Tensor& mb, at::Tensor& sumsq, int64_t per, double mu,
+                  const c10::optional<at::Tensor>& gscale);
+void normuon_cast(const at::Tensor& gptrs, const at::Tensor& sumsq, at::Tensor& X);
+at::Tensor normuon_stats(const at::Tensor& X, bool tall);
+void normuon_scale(const at::Tensor& partial, at::Tensor& v2, at::Tensor& scale, int64_t red, double beta2);
+void normuon_apply(const at::Tensor& X, const at::Tensor& scale, const at::Tensor& pptrs, int64_t r0, int64_t c0,
+                   int64_t rs, int64_t cs, bool tall, double lr, double wd);
+void sumsq_multi(const at::Tensor& ptrs, const at::Tensor& sizes, at::Tensor& out, int64_t max_len);
+void clip_coef(const at::Tensor& sumsq, double max_norm, at::Tensor& coef, at::Tensor& norm);
+void cast_multi(const at::Tensor& src, const at::Tensor& dst, const at::Tensor& sizes, int64_t max_len);
+at::Tensor exp2_poly_eval(const at::Tensor& x);
 std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
                                        double scale, const c10::optional<at::Tensor>& dbounds);
@@ -65,10 +76,34 @@ static int64_t read_status(bool reset) {
   return static_cast<int64_t>(mint::read_status_word(dev, reset));
 }
 
+static void set_wait_limit(int64_t ns) {
+  int dev = 0;
+  MINT_CUDA_CHECK(cudaGetDevice(&dev));
+  mint::set_wait_limit_ns(dev, static_cast<uint64_t>(ns));
+}
+
+static int64_t get_wait_limit() {
+  int dev = 0;
+  MINT_CUDA_CHECK(cudaGetDevice(&dev));
+  return static_cast<int64_t>(mint::wait_limit_ns(dev));
+}
+
+// The current device's status word as a 1-element int32 CUDA tensor (no copy; the block lives
+// until the process exits), so the host can snapshot it with an asynchronous copy each step.
+static at::Tensor status_tensor() {
+  int dev = 0;
+  MINT_CUDA_CHECK(cudaGetDevice(&dev));
+  uint32_t* p = mint::status_ptr(dev);
+  return at::from_blob(p, {1}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, dev));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mint_b200 sm_100a kernels";
   m.def("read_status", &read_status, "read (and optionally clear) this device's kernel status word",
         py::arg("reset") = false);
+  m.def("set_wait_limit_ns", &set_wait_limit, "bound (ns) of every spin-wait in this device's kernels");
+  m.def("wait_limit_ns", &get_wait_limit, "current spin-wait bound (ns) of this device's kernels");
+  m.def("status_tensor", &status_tensor, "this device's kernel status word as a 1-element int32 tensor");
   m.def("gemm", &mint::gemm_bf16, "C = alpha * op(A) @ op(B) + beta * D (tcgen05)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("D"), py::arg("a_kmajor"), py::arg("b_kmajor"), py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("alpha_t") = py::none(), py::arg("accumulate") = false);
@@ -86,7 +121,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fused_fwd_bwd", &mint::ce_fused_fwd_bwd);
   m.def("ce_row_stats", &mint::ce_row_stats);
   m.def("ce_grad_inplace", &mint::ce_grad_inplace);
-  m.def("adamw_step", &mint::adamw_step);
+  m.def("adamw_step", &mint::adamw_step, "fused AdamW over a flat fp32 shard", py::arg("p"), py::arg("g"),
+        py::arg("m"), py::arg("v"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"),
+        py::arg("step"), py::arg("gscale") = py::none());
+  m.def("normuon_prep", &mint::normuon_prep, "NorMuon momentum + Nesterov + per-matrix squared norm (in place)");
+  m.def("normuon_cast", &mint::normuon_cast, "NorMuon Frobenius normalization to the bf16 Polar-Express input");
+  m.def("normuon_stats", &mint::normuon_stats, "row (tall) or column sums of squares of the orthogonalized stack");
+  m.def("normuon_scale", &mint::normuon_scale, "NorMuon second moment update and per-row/column step scale");
+  m.def("normuon_apply", &mint::normuon_apply, "NorMuon update with cautious weight decay through a pointer table");
+  m.def("sumsq_multi", &mint::sumsq_multi, "sum of squares over a table of fp32 segments (accumulated)");
+  m.def("clip_coef", &mint::clip_coef, "gradient-norm clip coefficient on the device");
+  m.def("cast_multi", &mint::cast_multi, "fp32 -> bf16 copies of a table of segments in one launch");
+  m.def("exp2_poly_eval", &mint::exp2_poly_eval, "elementwise 2^x with attention's FMA-pipe polynomial (tests)");
   m.def("flash_attn_fwd", &mint::flash_attn_fwd, "tcgen05 FlashAttention forward -> (o, lse)", py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("doc"), py::arg("causal"), py::arg("window"), py::arg("scale"),
         py::arg("dbounds") = py::none());

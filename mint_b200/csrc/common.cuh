@@ -26,13 +26,31 @@ enum StatusCode : uint32_t {
   kStatusTimeoutAttention = 1u << 5,
 };
 
-// Wait limit for any spin in device code: 4 s of %globaltimer.
-constexpr uint64_t kWaitLimitNs = 4000000000ull;
+// Per-device status block (256 bytes, allocated by host_common.cpp): word 0 is the status word
+// (OR of StatusCode bits), bytes 8..15 the wait limit in nanoseconds that bounds every spin in
+// device code. The host sets the limit at run time (mint_b200.ops._ext.set_wait_limit), so a test
+// can make a wait give up after a fraction of a second; kDefaultWaitLimitNs applies when a kernel
+// runs without a status block or the stored limit is zero.
+constexpr uint64_t kDefaultWaitLimitNs = 4000000000ull;
+constexpr int kStatusLimitWord = 2;  // uint32 index of the 64-bit limit inside the block
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+__device__ __forceinline__ uint64_t wait_limit_ns(const uint32_t* status) {
+  if (status == nullptr) return kDefaultWaitLimitNs;
+  const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(status + kStatusLimitWord);
+  return v != 0 ? v : kDefaultWaitLimitNs;
+}
+
+// True when any kernel has recorded an error on this device: update kernels (AdamW, NorMuon) then
+// leave the parameters untouched, so a step whose gradients came through a timed-out collective
+// cannot corrupt the model before the host reads the word and raises.
+__device__ __forceinline__ bool status_failed(const uint32_t* status) {
+  return status != nullptr && *reinterpret_cast<const volatile uint32_t*>(status) != 0u;
 }
 
 __device__ __forceinline__ void record_status(uint32_t* status, uint32_t code) {
@@ -86,17 +104,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Wait for phase `parity` of `bar` to complete. Returns false (and records `code`) when the
-// wait exceeds kWaitLimitNs or `abort_flag` (shared) becomes non-zero.
+// wait exceeds the device's wait limit or `abort_flag` (shared) becomes non-zero.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code,
                                           volatile int* abort_flag) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer();
+  const uint64_t limit = wait_limit_ns(status);
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(addr, parity)) return true;
     if ((it & 255u) == 0u) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit) {
         record_status(status, code);
         if (abort_flag != nullptr) *abort_flag = 1;
         return false;
@@ -338,17 +357,18 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Spin (bounded by kWaitLimitNs) until *flag >= target. `sys` selects system scope (a flag written
-// by another GPU) or GPU scope. Returns false and records `code` on timeout or abort.
+// Spin (bounded by the device's wait limit) until *flag >= target. `sys` selects system scope (a
+// flag written by another GPU) or GPU scope. Returns false and records `code` on timeout or abort.
 __device__ __forceinline__ bool wait_flag(const int* flag, int target, bool sys, uint32_t* status, uint32_t code,
                                           volatile int* abort_flag) {
   if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
   const uint64_t t0 = globaltimer();
+  const uint64_t limit = wait_limit_ns(status);
   for (uint32_t it = 1;; ++it) {
     if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
     if ((it & 63u) == 0u) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit) {
         record_status(status, code);
         if (abort_flag != nullptr) *abort_flag = 1;
         return false;
@@ -423,7 +443,7 @@ __device__ __forceinline__ float warp_max(float v) {
 // 2^f from a degree-3 polynomial whose coefficients are a relative-error least-squares fit on 2000
 // Chebyshev nodes of [-0.5, 0.5] (computed for this file with numpy; max relative error 7.8e-5,
 // far below the bf16 rounding of the probabilities it feeds); 2^n added to the exponent bits.
-// Returns 0 for t < -125 (and for -inf).
+// Returns 0 for t < -125 (and for -inf); a NaN argument comes back as NaN.
 __device__ __forceinline__ float exp2_poly(float t) {
   const float tc = fmaxf(t, -125.f);
   const float j = tc + 12582912.f;  // 1.5 * 2^23: round to nearest integer
@@ -433,7 +453,8 @@ __device__ __forceinline__ float exp2_poly(float t) {
   p = fmaf(p, f, 0.6932762265205383f);
   p = fmaf(p, f, 0.9999289512634277f);
   const int bits = __float_as_int(p) + ((__float_as_int(j) - 0x4B400000) << 23);
-  return t < -125.f ? 0.f : __int_as_float(bits);
+  // t >= -125 is false for NaN: such a t falls through to the last select and is returned as is
+  return t >= -125.f ? __int_as_float(bits) : (t < -125.f ? 0.f : t);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

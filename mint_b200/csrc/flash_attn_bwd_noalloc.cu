@@ -1,13 +1,16 @@
 // Allocation-free FlashAttention backward entry point (declared in flash_attn_bwd_noalloc.h; no
-// counterpart in the reference framework). The fp32 dQ accumulator, the delta rows and a spare
-// status word live in one file-scope device array instead of per-call allocations; the kernels
-// are the ones of attention_bwd_sm100.cu, launched through flash_attn_bwd_launch_raw.
+// counterpart in the reference framework). The fp32 dQ accumulator, the delta rows and a status
+// block (status word + wait limit, the layout common.cuh defines) live in one file-scope device
+// array instead of per-call allocations; the kernels are the ones of attention_bwd_sm100.cu,
+// launched through flash_attn_bwd_launch_raw, and always report into that internal block. A small
+// kernel then moves any error bits into the caller's status word when the caller passed one.
 #include <cstdio>
 #include <cstdint>
 #include <exception>
 #include <mutex>
 
 #include "attention_bwd_raw.h"
+#include "common.cuh"
 #include "flash_attn_bwd_noalloc.h"
 
 namespace {
@@ -16,7 +19,7 @@ constexpr long long kMaxRows = MINT_FLASH_ATTN_BWD_NOALLOC_MAX_ROWS;  // B * T *
 constexpr long long kHeadDim = 128;
 constexpr long long kDqFloats = kMaxRows * kHeadDim;  // 16 MiB
 constexpr long long kDeltaFloats = kMaxRows;          // 128 KiB
-constexpr long long kStatusFloats = 64;               // 256 B, first word used
+constexpr long long kStatusFloats = 64;               // 256 B status block: word 0 status, bytes 8..15 wait limit
 constexpr long long kScratchFloats = kDqFloats + kDeltaFloats + kStatusFloats;
 constexpr int kMaxDevices = 64;
 
@@ -57,10 +60,30 @@ int scratch_for_current_device(float** out, char* err, size_t len) {
       return 3;
     }
     mint::flash_attn_bwd_configure_current_device();  // throws on error (caught by the caller)
+    // the status block's wait limit (a plain copy into the array; nothing is allocated)
+    const uint64_t limit = mint::kDefaultWaitLimitNs;
+    const size_t limit_off = static_cast<size_t>(kDqFloats + kDeltaFloats) * sizeof(float) + 8;
+    e = cudaMemcpyToSymbol(g_fa_bwd_scratch, &limit, sizeof(limit), limit_off, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      char msg[256];
+      std::snprintf(msg, sizeof(msg), "mint_flash_attn_bwd_noalloc: setting the wait limit failed: %s",
+                    cudaGetErrorString(e));
+      set_error(err, len, msg);
+      return 3;
+    }
     g_scratch_addr[dev] = static_cast<float*>(ptr);
   }
   *out = g_scratch_addr[dev];
   return 0;
+}
+
+// Moves the error bits of the internal status word into the caller's word and clears the former.
+__global__ void forward_status_kernel(uint32_t* internal, uint32_t* user) {
+  const uint32_t bits = *reinterpret_cast<volatile uint32_t*>(internal);
+  if (bits != 0u) {
+    atomicOr(user, bits);
+    *internal = 0u;
+  }
 }
 
 }  // namespace
@@ -112,8 +135,10 @@ extern "C" int mint_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
     a.dv = dv;
     a.dq_acc = base;
     a.delta = base + kDqFloats;
-    a.status = status != nullptr ? reinterpret_cast<uint32_t*>(status)
-                                 : reinterpret_cast<uint32_t*>(base + kDqFloats + kDeltaFloats);
+    // the kernels read their wait limit next to the status word, so they always get the internal
+    // 256-byte block; a caller's 4-byte word receives the bits afterwards
+    uint32_t* internal_status = reinterpret_cast<uint32_t*>(base + kDqFloats + kDeltaFloats);
+    a.status = internal_status;
     a.B = B;
     a.T = T;
     a.Hq = Hq;
@@ -131,6 +156,17 @@ extern "C" int mint_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
       return 3;
     }
     mint::flash_attn_bwd_launch_raw(a, stream);
+    if (status != nullptr) {
+      forward_status_kernel<<<1, 1, 0, stream>>>(internal_status, reinterpret_cast<uint32_t*>(status));
+      e = cudaGetLastError();
+      if (e != cudaSuccess) {
+        char msg[256];
+        std::snprintf(msg, sizeof(msg), "mint_flash_attn_bwd_noalloc: status launch failed: %s",
+                      cudaGetErrorString(e));
+        set_error(err, err_len, msg);
+        return 3;
+      }
+    }
     return 0;
   } catch (const std::exception& ex) {
     char msg[512];
@@ -141,4 +177,23 @@ extern "C" int mint_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
     set_error(err, err_len, "mint_flash_attn_bwd_noalloc: unknown error");
     return 3;
   }
+}
+
+extern "C" int mint_flash_attn_bwd_noalloc_status(int reset, unsigned int* out) {
+  if (out == nullptr) return 1;
+  float* base = nullptr;
+  if (scratch_for_current_device(&base, nullptr, 0) != 0) return 3;
+  const size_t off = static_cast<size_t>(kDqFloats + kDeltaFloats) * sizeof(float);
+  // synchronous copies: the value reflects every call enqueued before this one has finished
+  if (cudaDeviceSynchronize() != cudaSuccess) return 3;
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fa_bwd_scratch, sizeof(v), off, cudaMemcpyDeviceToHost) != cudaSuccess) return 3;
+  if (reset != 0 && v != 0) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_fa_bwd_scratch, &zero, sizeof(zero), off, cudaMemcpyHostToDevice) != cudaSuccess) {
+      return 3;
+    }
+  }
+  *out = v;
+  return 0;
 }

@@ -38,8 +38,13 @@ extern "C" {
 //   lse            : [B, Hq, T] fp32 natural-log softmax normalizer saved by the forward pass
 //   doc            : [B, T] int32 document ids (attention stays inside a document), or NULL
 // causal != 0 keeps keys j <= i; window >= 0 also drops keys with i - j > window (< 0: no window).
-// `status` is an optional device pointer to a 32-bit word that receives error bits when a kernel
-// gives up on a bounded wait; with NULL a word inside the library's array is used instead.
+// `status` is an optional device pointer to a 32-bit word: when a kernel gives up on a bounded wait
+// (4 s) the call ORs an error bit into it (a one-thread kernel after the backward kernels moves the
+// bits there), and the gradients of that call must not be used. With NULL the bits stay in a word
+// inside the library's array; read and clear them with mint_flash_attn_bwd_noalloc_status.
+// `doc`: with document ids the kernels compare ids element by element and skip no key tiles (the
+// regular binding also passes precomputed document bounds and skips whole tiles outside a query's
+// document), so packed documents are correct here but slower than through the binding.
 // All work is enqueued on `stream`; the call returns before the GPU finishes.
 // Returns 0 on success, 1 for a bad argument, 2 for a size above the scratch limit, 3 for a CUDA
 // error during set-up or launch. On failure a message is written to `err` (if non-NULL,
@@ -48,6 +53,11 @@ int mint_flash_attn_bwd_noalloc(const void* dout, const void* q, const void* k, 
                                 const float* lse, const int* doc, void* dq, void* dk, void* dv, int B, int T,
                                 int Hq, int Hkv, int causal, int window, float scale, unsigned int* status,
                                 cudaStream_t stream, char* err, size_t err_len);
+
+// Reads (and with reset != 0 clears) the internal status word of the current device: the error
+// bits of every call made with status == NULL. Synchronizes the device first, so it is a host-side
+// check between steps, not something to call inside a stream capture. Returns 0 on success.
+int mint_flash_attn_bwd_noalloc_status(int reset, unsigned int* out);
 
 // Largest B * T * Hq that mint_flash_attn_bwd_noalloc accepts.
 #define MINT_FLASH_ATTN_BWD_NOALLOC_MAX_ROWS 32768

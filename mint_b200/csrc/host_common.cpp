@@ -41,9 +41,27 @@ uint32_t* status_ptr(int device) {
     void* p = nullptr;
     MINT_CUDA_CHECK(cudaMalloc(&p, 256));
     MINT_CUDA_CHECK(cudaMemset(p, 0, 256));
+    // bytes 8..15: the wait limit (ns) of every bounded spin in device code (see common.cuh)
+    const uint64_t limit = kDefaultWaitLimitNsHost;
+    MINT_CUDA_CHECK(cudaMemcpy(static_cast<char*>(p) + 8, &limit, sizeof(limit), cudaMemcpyHostToDevice));
     g_status[device] = static_cast<uint32_t*>(p);
   }
   return g_status[device];
+}
+
+void set_wait_limit_ns(int device, uint64_t ns) {
+  uint32_t* p = status_ptr(device);
+  MINT_CHECK(ns > 0, "the wait limit must be positive");
+  // synchronous copy: kernels launched after this call see the new limit
+  MINT_CUDA_CHECK(cudaDeviceSynchronize());
+  MINT_CUDA_CHECK(cudaMemcpy(reinterpret_cast<char*>(p) + 8, &ns, sizeof(ns), cudaMemcpyHostToDevice));
+}
+
+uint64_t wait_limit_ns(int device) {
+  uint32_t* p = status_ptr(device);
+  uint64_t ns = 0;
+  MINT_CUDA_CHECK(cudaMemcpy(&ns, reinterpret_cast<char*>(p) + 8, sizeof(ns), cudaMemcpyDeviceToHost));
+  return ns;
 }
 
 uint32_t read_status_word(int device, bool reset) {

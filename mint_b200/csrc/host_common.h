@@ -21,9 +21,13 @@ namespace mint {
                 __FILE__, ":", __LINE__);                                                           \
   } while (0)
 
-// Device pointer to this device's status word (allocated once per device, zero-initialized).
+// Device pointer to this device's status block (allocated once per device): word 0 is the status
+// word (zero = no kernel reported an error), bytes 8..15 the wait limit in ns of every bounded spin.
+constexpr uint64_t kDefaultWaitLimitNsHost = 4000000000ull;
 uint32_t* status_ptr(int device);
 uint32_t read_status_word(int device, bool reset);
+void set_wait_limit_ns(int device, uint64_t ns);
+uint64_t wait_limit_ns(int device);
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride `ld` elements,
 // box = [box_rows, box_cols], 128-byte swizzle. Requires cols*2 and ld*2 to be multiples of 16.

@@ -337,9 +337,14 @@ __global__ void __launch_bounds__(512, 3) ce_grad_kernel(__nv_bfloat16* __restri
 
 // p <- p (1 - lr wd); m <- lerp(m, g, 1 - b1); v <- lerp(v, g^2, 1 - b2);
 // p <- p - (lr / bc1) * m / (sqrt(v / bc2) + eps)
+// Skipped entirely (parameters and moments unchanged) once any kernel recorded an error status.
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, long long n, float lr, float b1, float b2, float eps, float wd,
-                             float bc1, float bc2) {
+                             float bc1, float bc2, const float* __restrict__ gscale,
+                             const uint32_t* __restrict__ status) {
+  if (status_failed(status)) return;
+  // gradient-clipping coefficient computed on the device (1 when the caller passes none)
+  const float gs = gscale != nullptr ? *gscale : 1.f;
   const float step = lr / bc1;
   const float decay = 1.f - lr * wd;
   const float inv_bc2 = 1.f / bc2;
@@ -351,6 +356,10 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float4 pp = p4[i], gg = g4[i], mm = m4[i], vv = v4[i];
+    gg.x *= gs;
+    gg.y *= gs;
+    gg.z *= gs;
+    gg.w *= gs;
     float* pa = &pp.x;
     const float* ga = &gg.x;
     float* ma = &mm.x;
@@ -367,10 +376,19 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
   for (long long i = n4 * 4 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    m[i] = m[i] + (1.f - b1) * (g[i] - m[i]);
-    v[i] = v[i] + (1.f - b2) * (g[i] * g[i] - v[i]);
+    const float gi = g[i] * gs;
+    m[i] = m[i] + (1.f - b1) * (gi - m[i]);
+    v[i] = v[i] + (1.f - b2) * (gi * gi - v[i]);
     p[i] = p[i] * decay - step * m[i] / (sqrtf(v[i] * inv_bc2) + eps);
   }
+}
+
+// Elementwise exp2_poly (common.cuh), exposed so its error bound and NaN handling can be tested
+// against exp2f directly rather than only through attention's tolerances.
+__global__ void exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    y[i] = exp2_poly(x[i]);
 }
 
 int ew_grid(long long n, int dev) {
@@ -514,7 +532,7 @@ void ce_grad_inplace(at::Tensor& logits, const at::Tensor& targets, const at::Te
 }
 
 void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1, double b2,
-                double eps, double wd, int64_t step) {
+                double eps, double wd, int64_t step, const c10::optional<at::Tensor>& gscale) {
   const at::Tensor* all[4] = {&p, &g, &m, &v};
   for (const at::Tensor* t : all) {
     check_cuda(*t, "adamw tensor");
@@ -530,9 +548,24 @@ void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v
   adamw_kernel<<<ew_grid((n + 3) / 4, p.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), n, static_cast<float>(lr),
       static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
-      static_cast<float>(bc1), static_cast<float>(bc2));
+      static_cast<float>(bc1), static_cast<float>(bc2),
+      gscale.has_value() ? gscale->data_ptr<float>() : nullptr, status_ptr(p.get_device()));
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
+}
+
+at::Tensor exp2_poly_eval(const at::Tensor& x) {
+  check_contig(x, "x");
+  MINT_CHECK(x.scalar_type() == at::kFloat, "x must be fp32");
+  auto y = at::empty_like(x);
+  const long long n = x.numel();
+  if (n == 0) return y;
+  c10::cuda::CUDAGuard g(x.device());
+  exp2_poly_kernel<<<ew_grid(n, x.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      x.data_ptr<float>(), y.data_ptr<float>(), n);
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+  return y;
 }
 
 }  // namespace mint

@@ -58,12 +58,90 @@ def use_cuda_kernels(t) -> bool:  # noqa: ANN001
     return True
 
 
+STATUS_BITS = {
+    1 << 0: "timed-out wait in a GEMM producer",
+    1 << 1: "timed-out wait in a GEMM MMA issuer",
+    1 << 2: "timed-out wait in a GEMM epilogue",
+    1 << 3: "bad kernel argument",
+    1 << 4: "timed-out wait for a peer GPU (fused collective)",
+    1 << 5: "timed-out wait in attention",
+}
+
+
+class DeviceStatusError(RuntimeError):
+    """A kernel recorded an error in the device status word: its outputs (and every parameter
+    update that would have used them) are not to be trusted."""
+
+
+def _describe(code: int) -> str:
+    names = [txt for bit, txt in STATUS_BITS.items() if code & bit]
+    return f"0x{code:x} ({'; '.join(names) or 'unknown bits'})"
+
+
 def check_device_status() -> None:
-    """Raise if any kernel recorded an error (timed-out wait, bad shape) in the device status word."""
+    """Raise if any kernel recorded an error (timed-out wait, bad shape) in the device status word.
+
+    Synchronizes with the device (a 4-byte device-to-host copy)."""
     mod = _try_load()
     if mod is None:
         return
     code = int(mod.read_status(False))
     if code != 0:
         mod.read_status(True)
-        raise RuntimeError(f"mint_b200 kernel reported device status 0x{code:x} (see kernel error codes)")
+        raise DeviceStatusError(f"mint_b200 kernel reported device status {_describe(code)}")
+
+
+def set_wait_limit(seconds: float) -> None:
+    """Bound every spin-wait of this device's kernels (default 4 s). On expiry a kernel records a
+    status bit, drains its in-flight work and returns; the parameter-update kernels then skip
+    their updates until the host has read the word."""
+    require().set_wait_limit_ns(max(1, int(seconds * 1e9)))
+
+
+def wait_limit() -> float:
+    return require().wait_limit_ns() / 1e9
+
+
+class StatusWatch:
+    """Per-step check of the device status word without stalling the host.
+
+    ``poll()`` raises :class:`DeviceStatusError` if the snapshot taken by the previous ``poll()``
+    (an asynchronous copy into pinned memory, enqueued after that step's work) shows an error,
+    then enqueues a new snapshot. A failed step is therefore reported one step later at most; the
+    update kernels (AdamW, NorMuon) already skipped their updates on the device, so no parameter
+    was changed with data from a timed-out collective. ``flush()`` checks synchronously."""
+
+    def __init__(self) -> None:
+        import torch  # noqa: PLC0415
+
+        self._torch = torch
+        self._host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._event = None
+
+    def poll(self) -> None:
+        torch = self._torch
+        if self._event is not None:
+            self._event.synchronize()
+            code = int(self._host[0])
+            if code != 0:
+                self._event = None
+                check_device_status()  # clears the word and raises with the decoded bits
+                raise DeviceStatusError(f"mint_b200 kernel reported device status {_describe(code)}")
+        self._host.copy_(require().status_tensor(), non_blocking=True)
+        self._event = torch.cuda.Event()
+        self._event.record()
+
+    def flush(self) -> None:
+        self._event = None
+        check_device_status()
+
+
+_WATCHES: dict[int, StatusWatch] = {}
+
+
+def status_watch(device_index: int) -> StatusWatch:
+    w = _WATCHES.get(device_index)
+    if w is None:
+        w = StatusWatch()
+        _WATCHES[device_index] = w
+    return w

@@ -26,7 +26,9 @@ def _main_grad(w: torch.Tensor) -> torch.Tensor | None:
     return g
 
 
-_CAST_CACHE: dict[tuple, tuple[tuple, torch.Tensor]] = {}
+# bf16 compute copies of (concatenated) fp32 master weights: key -> [stamp, copy, weights]
+_CAST_CACHE: dict[tuple, list] = {}
+_REFRESH_TABLES: dict[tuple, tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]] = {}
 
 
 def _stamp(weights: tuple[torch.Tensor, ...]) -> tuple | None:
@@ -53,8 +55,56 @@ def _cast_weight(weights: tuple[torch.Tensor, ...], dtype: torch.dtype) -> torch
     else:
         out = torch.cat([w.detach().to(dtype) for w in weights], dim=0)
     if stamp is not None:
-        _CAST_CACHE[key] = (stamp, out)
+        _CAST_CACHE[key] = [stamp, out, weights]
     return out
+
+
+def refresh_weight_shadows() -> None:
+    """Re-cast every cached bf16 weight copy whose fp32 master changed, in ONE kernel launch.
+
+    Called by the optimizers after each step (the step bumps the engine epoch, so every copy is
+    stale): the next forward then finds its copies current instead of casting and concatenating
+    each weight group separately. Copies whose weights were re-allocated are dropped."""
+    stale = []
+    for key, ent in list(_CAST_CACHE.items()):
+        stamp, out, weights = ent
+        now = _stamp(weights)
+        if now is None or now == stamp:
+            continue
+        if now[1] != stamp[1] or not out.is_cuda or out.dtype != torch.bfloat16:
+            del _CAST_CACHE[key]  # storage moved or not a CUDA bf16 copy: rebuilt on next use
+            continue
+        stale.append((key, ent, now))
+    if not stale or not _ext.kernels_enabled():
+        return
+    segs = []
+    for _key, ent, _now in stale:
+        out, weights = ent[1], ent[2]
+        off = 0
+        for w in weights:
+            if w.dtype != torch.float32 or not w.is_contiguous():
+                segs = None
+                break
+            segs.append((w.data_ptr(), out.data_ptr() + off * 2, w.numel()))
+            off += w.numel()
+        if segs is None:
+            break
+    if segs is None:  # an unusual weight: leave those copies to the lazy per-call cast
+        return
+    tkey = tuple(segs)
+    table = _REFRESH_TABLES.get(tkey)
+    dev = stale[0][1][1].device
+    if table is None:
+        if len(_REFRESH_TABLES) > 8:
+            _REFRESH_TABLES.clear()
+        table = (torch.tensor([a for a, _b, _n in segs], dtype=torch.int64, device=dev),
+                 torch.tensor([b for _a, b, _n in segs], dtype=torch.int64, device=dev),
+                 torch.tensor([n for _a, _b, n in segs], dtype=torch.int64, device=dev),
+                 max(n for _a, _b, n in segs))
+        _REFRESH_TABLES[tkey] = table
+    _ext.require().cast_multi(table[0], table[1], table[2], table[3])
+    for _key, ent, now in stale:
+        ent[0] = now
 
 
 def weight_grads(weights: tuple[torch.Tensor, ...], want: list[bool], dy2: torch.Tensor,

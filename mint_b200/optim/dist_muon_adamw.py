@@ -23,7 +23,7 @@ import torch
 import torch.distributed as dist
 from torch.optim import Optimizer
 
-from mint_b200.optim.functional import POLAR_EXPRESS_COEFFS, adamw_update, normuon_update_batched
+from mint_b200.optim.functional import POLAR_EXPRESS_COEFFS, NorMuonStack, adamw_update, normuon_update_batched
 from mint_b200.optim.muon_adamw import AdamConfig, MuonAdamWConfig, MuonConfig
 
 
@@ -46,6 +46,13 @@ class DistMuonAdamW(Optimizer):
         self._shard_state: dict[int, dict[str, Any]] = {}
         # stacked NorMuon state per (group, shape, dtype, tp split) of the matrices this rank updates
         self._muon_stacks: dict[tuple, dict[str, Any]] = {}
+        if self._engine is not None:
+            # the update kernels read the clip coefficient on the device: no separate scaling pass
+            self._engine.defer_clip = self._engine.clip_on_device()
+
+    def _grad_scale(self):  # noqa: ANN202
+        eng = self._engine
+        return None if eng is None else eng.grad_scale
 
     @property
     def engine(self):  # noqa: ANN201
@@ -108,7 +115,7 @@ class DistMuonAdamW(Optimizer):
                 st = self._ensure_bucket_state(b)
                 st["step"] += 1
                 adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
-                             group["eps"], group["weight_decay"])
+                             group["eps"], group["weight_decay"], grad_scale=self._grad_scale())
                 for sub in st["views"]:
                     sub["step"] = st["step"]
         for p in group["params"]:
@@ -127,6 +134,7 @@ class DistMuonAdamW(Optimizer):
                         st[key] = {"step": 0, "exp_avg": torch.zeros_like(pv), "exp_avg_sq": torch.zeros_like(pv),
                                    "offset": off, "numel": n}
                     units.append((pv, gv, st[key]))
+            in_engine = eng is not None and id(p) in eng.by_param
             for pv, gv, st in units:
                 if "step" not in st:
                     st["step"] = 0
@@ -134,7 +142,8 @@ class DistMuonAdamW(Optimizer):
                     st["exp_avg_sq"] = torch.zeros_like(pv)
                 st["step"] += 1
                 adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
-                             group["eps"], group["weight_decay"])
+                             group["eps"], group["weight_decay"],
+                             grad_scale=self._grad_scale() if in_engine else None)
 
     def _muon_units(self, group: dict) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
         """(param, this rank's whole matrix view, its gradient view) for every matrix this rank updates."""
@@ -189,8 +198,23 @@ class DistMuonAdamW(Optimizer):
             members = [u[0] for u in units]
             shape = units[0][1].shape
             st = self._muon_stack_state(key, members, shape, units[0][1].device)
-            grads = torch.stack([u[2].float() for u in units])
             tp_group, tp_dim = self._tp_of(members[0])
+            pviews, gviews = [u[1] for u in units], [u[2] for u in units]
+            if tp_group is None and NorMuonStack.supported(pviews, gviews):
+                dev = st.get("device_stack")
+                if dev is None:
+                    n = len(units)
+                    dev = NorMuonStack(pviews, gviews, st["mb"], st["smb"].view(n, -1))
+                    st["device_stack"] = dev
+                dev.bind(pviews, gviews)
+                dev.step(lr=group["lr"], momentum=group["momentum"],
+                         beta2=group["beta2"] if group.get("beta2") is not None else 0.0,
+                         wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5), grad_scale=self._grad_scale())
+                continue
+            grads = torch.stack([u[2].float() for u in units])
+            gs = self._grad_scale()
+            if gs is not None:
+                grads.mul_(gs)
             normuon_update_batched(
                 [u[1] for u in units], grads, st["mb"], st["smb"],
                 lr=group["lr"], momentum=group["momentum"],
@@ -243,6 +267,9 @@ class DistMuonAdamW(Optimizer):
         if eng is not None:
             eng.after_step()
             eng._synced = False
+        from mint_b200.ops.linear import refresh_weight_shadows  # noqa: PLC0415
+
+        refresh_weight_shadows()  # bf16 compute copies of the updated weights, one launch
         return loss
 
     # ------------------------------------------------------------------ (de)serialization

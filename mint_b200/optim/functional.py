@@ -39,11 +39,15 @@ def adamw_update(
     beta2: float,
     eps: float,
     wd: float,
+    grad_scale: torch.Tensor | None = None,
 ) -> None:
+    """``grad_scale``: optional 1-element device tensor multiplied into ``g`` (gradient clipping)."""
     if p.is_cuda and _ext.kernels_enabled():
         _ext.require().adamw_step(p, g, exp_avg, exp_avg_sq, float(lr), float(beta1), float(beta2),
-                                  float(eps), float(wd), int(step))
+                                  float(eps), float(wd), int(step), grad_scale)
         return
+    if grad_scale is not None:
+        g = g * grad_scale
     p.mul_(1 - lr * wd)
     exp_avg.lerp_(g, 1 - beta1)
     exp_avg_sq.lerp_(g.square(), 1 - beta2)
@@ -85,6 +89,24 @@ def polar_express(g: torch.Tensor, ns_steps: int) -> torch.Tensor:
 
 
 @torch.no_grad()
+def polar_express_chain_bf16(x: torch.Tensor, ns_steps: int) -> torch.Tensor:
+    """The Polar-Express iterations on an already normalized bf16 stack ``[n, rows, cols]`` (or one
+    matrix): three tcgen05 GEMM launches per iteration for the whole stack, the ``b*A + c*A@A`` and
+    ``a*X + B@X`` combinations folded into the GEMM epilogues."""
+    tall = x.shape[-2] > x.shape[-1]
+    for a, b, c in POLAR_EXPRESS_COEFFS[:ns_steps]:
+        if tall:
+            A = matmul(x, x, trans_a=True)  # X^T X per matrix
+            B = matmul(A, A, alpha=c, beta=b, d=A)
+            x = matmul(x, B, alpha=1.0, beta=a, d=x)  # a X + X B
+        else:
+            A = matmul(x, x, trans_b=True)  # X X^T per matrix
+            B = matmul(A, A, alpha=c, beta=b, d=A)
+            x = matmul(B, x, alpha=1.0, beta=a, d=x)  # a X + B X
+    return x
+
+
+@torch.no_grad()
 def polar_express_batched(g: torch.Tensor, ns_steps: int) -> torch.Tensor:
     """``polar_express`` on a stack ``[n, rows, cols]`` of equally shaped matrices at once.
 
@@ -96,17 +118,7 @@ def polar_express_batched(g: torch.Tensor, ns_steps: int) -> torch.Tensor:
     norms = x.flatten(1).norm(dim=1).view(n, 1, 1)
     x = x / (norms * 1.01 + 1e-6)
     if g.is_cuda and _ext.kernels_enabled():
-        x = x.to(torch.bfloat16)
-        for a, b, c in POLAR_EXPRESS_COEFFS[:ns_steps]:
-            if tall:
-                A = matmul(x, x, trans_a=True)  # X^T X per matrix
-                B = matmul(A, A, alpha=c, beta=b, d=A)
-                x = matmul(x, B, alpha=1.0, beta=a, d=x)  # a X + X B
-            else:
-                A = matmul(x, x, trans_b=True)  # X X^T per matrix
-                B = matmul(A, A, alpha=c, beta=b, d=A)
-                x = matmul(B, x, alpha=1.0, beta=a, d=x)  # a X + B X
-        return x.float()
+        return polar_express_chain_bf16(x.to(torch.bfloat16), ns_steps).float()
     for a, b, c in POLAR_EXPRESS_COEFFS[:ns_steps]:
         if tall:
             A = x.mT @ x
@@ -225,3 +237,64 @@ def normuon_update_batched(
     mask = (g * pf) >= 0
     new = pf - (lr * g + lr * wd * pf * mask)
     torch._foreach_copy_(params, list(new.to(params[0].dtype).unbind(0)))
+
+
+class NorMuonStack:
+    """Device-side NorMuon for ``n`` equally shaped whole matrices whose gradients and parameters
+    live anywhere in device memory (gradient-engine bucket views), with no stacking copies.
+
+    One step is: ``normuon_prep`` (momentum, Nesterov, the clip coefficient read on the device,
+    per-matrix squared norm; the Nesterov gradient overwrites the gradient), ``normuon_cast``
+    (Frobenius normalization into a bf16 stack), the Polar-Express GEMM chain, ``normuon_stats`` /
+    ``normuon_scale`` (row or column second moments, the NorMuon rescale back to the pre-norm
+    Frobenius norm) and ``normuon_apply`` (update with cautious weight decay). Same math as
+    ``normuon_update_batched``; the pointer tables are rebuilt only when a view moves."""
+
+    def __init__(self, params: list[torch.Tensor], grads: list[torch.Tensor], mb: torch.Tensor, smb: torch.Tensor) -> None:
+        self.n = len(params)
+        self.rows, self.cols = params[0].shape
+        dev = params[0].device
+        self.key = None
+        self.mb = mb
+        self.smb = smb
+        self.sumsq = torch.zeros(self.n, dtype=torch.float32, device=dev)
+        self.x = torch.empty(self.n, self.rows, self.cols, dtype=torch.bfloat16, device=dev)
+        j = self.rows if self.rows >= self.cols else self.cols
+        self.scale = torch.empty(self.n, j, dtype=torch.float32, device=dev)
+        self.bind(params, grads)
+
+    @staticmethod
+    def supported(params: list[torch.Tensor], grads: list[torch.Tensor]) -> bool:
+        if not params or not params[0].is_cuda or not _ext.kernels_enabled():
+            return False
+        rows, cols = params[0].shape
+        if cols % 8 or (rows * cols) % 8:
+            return False
+        for t in list(params) + list(grads):
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.data_ptr() % 16 or tuple(t.shape) != (rows, cols):
+                return False
+        return True
+
+    def bind(self, params: list[torch.Tensor], grads: list[torch.Tensor]) -> None:
+        key = (tuple(p.data_ptr() for p in params), tuple(g.data_ptr() for g in grads))
+        if key == self.key:
+            return
+        dev = params[0].device
+        self.pptrs = torch.tensor([p.data_ptr() for p in params], dtype=torch.int64, device=dev)
+        self.gptrs = torch.tensor([g.data_ptr() for g in grads], dtype=torch.int64, device=dev)
+        self.key = key
+
+    @torch.no_grad()
+    def step(self, *, lr: float, momentum: float, beta2: float, wd: float, ns_steps: int,
+             grad_scale: torch.Tensor | None = None) -> None:
+        C = _ext.require()
+        rows, cols = self.rows, self.cols
+        C.normuon_prep(self.gptrs, self.mb, self.sumsq, rows * cols, float(momentum), grad_scale)
+        C.normuon_cast(self.gptrs, self.sumsq, self.x)
+        x = polar_express_chain_bf16(self.x, ns_steps)
+        tall = rows >= cols
+        partial = C.normuon_stats(x, tall)
+        red = cols if tall else rows
+        C.normuon_scale(partial, self.smb, self.scale, red, float(beta2))
+        lr = lr * max(1.0, rows / cols) ** 0.5
+        C.normuon_apply(x, self.scale, self.pptrs, 0, 0, rows, cols, tall, float(lr), float(wd))

@@ -18,11 +18,17 @@ Sequence-parallel activations are ``[B, T / tp, d]`` (a shard of every sequence)
 layout is ``[B, T, d]`` (rows of rank p's shard of sequence b at rows ``b*T + p*T/tp ...``).
 Gradients are those of the NCCL path in ``mint_b200.parallel.tp``; only the transport differs.
 
-Buffers: symmetric allocations (``torch.distributed._symmetric_memory``) are made collectively the
-first time a call of a given index in the forward pass needs them and reused in later steps. Flags
-carry a call sequence number and are never reset; a call touches a peer's buffers of that call only
-after the peer announced it entered the call, which also keeps the two-slot ring of transient
-buffers safe to reuse.
+Buffers: the gathered input of a column-parallel forward is kept for its weight gradient in a
+symmetric buffer taken from a per-group pool and handed back when that backward has run (at once
+when no backward will follow: no-grad forwards, frozen weights). Every rank runs the same sequence
+of forwards and backwards, so the pool evolves identically on all ranks and a new buffer -- a
+collective ``torch.distributed._symmetric_memory`` allocation -- is made at the same call on every
+rank. Several forwards may be outstanding at once (a frozen reference model, gradient
+accumulation, recomputation); a forward whose backward never runs keeps its buffer until the next
+step boundary (``reset_pools``, called when the gradients are zeroed). Flags carry a call sequence
+number and are never reset; a call touches a peer's buffers of that call only after the peer
+announced it entered the call, which also keeps the two-slot ring of transient buffers safe to
+reuse.
 """
 
 from __future__ import annotations
@@ -41,6 +47,9 @@ class _Symm:
     """One symmetric buffer: the local tensor and every rank's address of it."""
 
     def __init__(self, nbytes: int, group: Any, device: torch.device) -> None:
+        # no kernel here uses NVLink multicast (multimem); keeping the buffers out of multicast
+        # objects also means a rank that dies holds no multicast binding its peers could fault on
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415
 
         self.nbytes = nbytes
@@ -79,27 +88,44 @@ class TPComm:
         self.rs_flags = self.ctrl.view((self.world * self.MAX_FLAG_BLOCKS,), torch.int32, offset=256)
         self.rowflag = torch.zeros(1 << 16, dtype=torch.int32, device=device)
         self.claim = torch.zeros(1, dtype=torch.int64, device=device)
-        self._saved: list[_Symm] = []  # gathered inputs kept for backward, by call index in the pass
-        self._saved_idx = 0
+        self._pool: list[_Symm] = []  # gathered-input buffers, in allocation order
+        self._busy: set[int] = set()  # pool slots held by a forward whose backward has not run
+        self._last_use: list[int] = []  # sequence number of the fused call that last let peers read a slot
         self._ring: list[_Symm | None] = [None, None]
         self._ring_idx = 0
 
     # -------------------------------------------------------------- buffers
-    def begin_forward(self) -> None:
-        """A new forward pass starts: its saved gathered inputs reuse the previous pass's buffers."""
-        self._saved_idx = 0
+    def acquire(self, nbytes: int) -> tuple[int, _Symm]:
+        """A free pooled buffer of at least ``nbytes`` (first fit), or a new one (collective).
 
-    def _saved_buffer(self, nbytes: int) -> _Symm:
-        i = self._saved_idx
-        self._saved_idx += 1
-        if i < len(self._saved) and self._saved[i].nbytes >= nbytes:
-            return self._saved[i]
-        b = _Symm(nbytes, self.group, self.device)  # collective: every rank reaches call i alike
-        if i < len(self._saved):
-            self._saved[i] = b
-        else:
-            self._saved.append(b)
-        return b
+        A peer can still be one fused call behind this rank (each kernel waits for every peer to
+        enter the same call, so no rank is further ahead), and the caller writes its own shard
+        into the buffer before its next kernel starts. A slot whose last peer-read call is the
+        current one or the one before it is therefore skipped even when released."""
+        for i, b in enumerate(self._pool):
+            if i not in self._busy and b.nbytes >= nbytes and self._last_use[i] <= self.seq - 1:
+                self._busy.add(i)
+                return i, b
+        b = _Symm(nbytes, self.group, self.device)  # every rank reaches this call alike
+        self._pool.append(b)
+        self._last_use.append(-(1 << 62))
+        i = len(self._pool) - 1
+        self._busy.add(i)
+        return i, b
+
+    def mark_read_by_peers(self, slot: int) -> None:
+        """The fused call just issued (sequence ``self.seq``) lets peers read ``slot``."""
+        self._last_use[slot] = self.seq
+
+    def release(self, slot: int) -> None:
+        self._busy.discard(slot)
+
+    def reset_pool(self) -> None:
+        """Step boundary: no backward is pending, so every pooled buffer is free again."""
+        self._busy.clear()
+
+    def in_use(self) -> int:
+        return len(self._busy)
 
     def _ring_buffer(self, nbytes: int) -> _Symm:
         i = self._ring_idx
@@ -171,17 +197,20 @@ class _ColumnParallelFn(torch.autograd.Function):
     """``y [B, T, N/tp] = all_gather_T(x [B, T/tp, K]) @ cat(weights)^T``."""
 
     @staticmethod
-    def forward(ctx, x, comm, *weights):  # noqa: ANN001, ANN205
+    def forward(ctx, x, comm, keep, *weights):  # noqa: ANN001, ANN205
         B, seg, K = x.shape
         world, rank = comm.world, comm.rank
         T = seg * world
         rows = B * T
-        gathered = comm._saved_buffer(rows * K * 2)
+        slot, gathered = comm.acquire(rows * K * 2)
         G = gathered.view((B, world, seg, K), torch.bfloat16)
         G[:, rank].copy_(x)  # this rank's shard in place; the kernel pulls the others
         w = _cast_weight(weights, torch.bfloat16)
         y = comm.gemm_ag(gathered, rows, K, w, True, seg)
-        ctx.comm, ctx.weights, ctx.shape, ctx.x_dtype = comm, weights, (B, seg, K), x.dtype
+        comm.mark_read_by_peers(slot)
+        if not keep:
+            comm.release(slot)  # no backward will read the gathered input
+        ctx.comm, ctx.weights, ctx.shape, ctx.x_dtype, ctx.slot = comm, weights, (B, seg, K), x.dtype, slot
         ctx.save_for_backward(gathered.view((rows, K), torch.bfloat16))
         return y.view(B, T, -1)
 
@@ -195,9 +224,10 @@ class _ColumnParallelFn(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             w = _cast_weight(weights, torch.bfloat16)  # [N, K]: op(B) = w read MN-major
             dx = comm.gemm_rs(dy2, w, False, seg).view(B, seg, K).to(ctx.x_dtype)
-        want = [ctx.needs_input_grad[2 + i] for i in range(len(weights))]
+        want = [ctx.needs_input_grad[3 + i] for i in range(len(weights))]
         grads = weight_grads(weights, want, dy2, G)
-        return (dx, None, *grads)
+        comm.release(ctx.slot)  # stream order keeps the weight-gradient GEMM ahead of any reuse
+        return (dx, None, None, *grads)
 
 
 class _RowParallelFn(torch.autograd.Function):
@@ -246,7 +276,8 @@ def enabled(tp: Any, x: torch.Tensor) -> bool:
 
 def column_parallel_linear(x: torch.Tensor, weights: tuple[torch.Tensor, ...], tp: Any) -> torch.Tensor:
     """Sequence-parallel input ``[B, T/tp, K]`` -> ``[B, T, sum N_i / tp]``."""
-    return _ColumnParallelFn.apply(x, get_comm(tp.group, x.device), *weights)
+    keep = torch.is_grad_enabled() and (x.requires_grad or any(w.requires_grad for w in weights))
+    return _ColumnParallelFn.apply(x, get_comm(tp.group, x.device), keep, *weights)
 
 
 def row_parallel_linear(x: torch.Tensor, w: torch.Tensor, tp: Any) -> torch.Tensor:
@@ -254,7 +285,12 @@ def row_parallel_linear(x: torch.Tensor, w: torch.Tensor, tp: Any) -> torch.Tens
     return _RowParallelFn.apply(x, get_comm(tp.group, x.device), w)
 
 
-def begin_forward(tp: Any, device: torch.device) -> None:
-    comm = _COMMS.get((id(tp.group), device.index)) if tp is not None else None
-    if comm is not None:
-        comm.begin_forward()
+def begin_forward(tp: Any, device: torch.device) -> None:  # noqa: ARG001
+    """Kept for callers of the earlier API: buffers are now pooled per forward/backward pair."""
+
+
+def reset_pools() -> None:
+    """Step boundary (gradients zeroed): free every pooled gathered-input buffer. A forward whose
+    backward never ran (an extra forward with gradients enabled) holds its buffer until here."""
+    for comm in _COMMS.values():
+        comm.reset_pool()

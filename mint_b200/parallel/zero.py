@@ -119,6 +119,11 @@ class GradEngine:
         self.distributed = self.dp > 1 and dist.is_available() and dist.is_initialized()
         self.sync_grads = True
         self.epoch = 0  # bumped whenever parameter values change (optimizer step, load)
+        # gradient clipping: with defer_clip the coefficient stays on the device (grad_scale) and the
+        # optimizer's update kernels multiply it in, instead of a separate pass scaling every gradient
+        self.defer_clip = False
+        self.grad_scale: torch.Tensor | None = None
+        self._norm_tables: dict[tuple, tuple[torch.Tensor, torch.Tensor, int]] = {}
         self._in_backward: set[str] = set()
         # ZeRO-2 on CUDA: gradient reduce-scatter and parameter all-gather as NVLink peer-memory kernels
         # (csrc/zero_comm.cu) over symmetric bucket buffers instead of NCCL; MINT_FUSED_ZERO=0 disables
@@ -273,6 +278,10 @@ class GradEngine:
             s.param.grad = b.grad[s.start : s.start + s.numel].view(s.shape)
 
     def zero_grad(self) -> None:
+        from mint_b200.parallel import fused  # noqa: PLC0415
+
+        fused.reset_pools()  # a step boundary: no tensor-parallel backward is pending
+        self.grad_scale = None
         for b in self.buckets:
             if b.grad is not None:
                 b.grad.zero_()
@@ -468,7 +477,9 @@ class GradEngine:
                     continue
             pieces.append(g)
         dev = self.buckets[0].shard_data.device if self.buckets else torch.device("cpu")
-        if pieces:
+        if pieces and self._kernel_norm_ok(pieces):
+            total = self._sumsq_kernel(pieces)
+        elif pieces:
             norms = torch._foreach_norm([t.float() if t.dtype != torch.float32 else t for t in pieces])
             total = torch.stack(norms).square().sum()
         else:
@@ -482,8 +493,43 @@ class GradEngine:
                 dist.all_reduce(total, op=dist.ReduceOp.SUM)
         return total
 
+    @staticmethod
+    def _kernel_norm_ok(pieces: list[torch.Tensor]) -> bool:
+        from mint_b200.ops import _ext  # noqa: PLC0415
+
+        return (pieces[0].is_cuda and _ext.kernels_enabled()
+                and all(t.dtype == torch.float32 and t.is_contiguous() for t in pieces))
+
+    def _sumsq_kernel(self, pieces: list[torch.Tensor]) -> torch.Tensor:
+        """Sum of squares of every piece in one launch (pointer table cached per layout)."""
+        key = tuple((t.data_ptr(), t.numel()) for t in pieces)
+        hit = self._norm_tables.get(key)
+        dev = pieces[0].device
+        if hit is None:
+            ptrs = torch.tensor([k[0] for k in key], dtype=torch.int64, device=dev)
+            sizes = torch.tensor([k[1] for k in key], dtype=torch.int64, device=dev)
+            hit = (ptrs, sizes, max(k[1] for k in key))
+            self._norm_tables[key] = hit
+        out = torch.zeros(1, dtype=torch.float32, device=dev)
+        _ext_mod().sumsq_multi(hit[0], hit[1], out, hit[2])
+        return out.view(())
+
+    def clip_on_device(self) -> bool:
+        """True when the clip coefficient can stay on the device for the update kernels."""
+        from mint_b200.ops import _ext  # noqa: PLC0415
+
+        dev = self.buckets[0].shard_data.device if self.buckets else torch.device("cpu")
+        return dev.type == "cuda" and _ext.kernels_enabled() and _ext.available()
+
     def clip_grad_norm(self, max_norm: float) -> torch.Tensor:
-        norm = self.grad_norm_sq().sqrt()
+        total = self.grad_norm_sq()
+        if self.defer_clip and total.is_cuda:
+            coef = torch.empty(1, dtype=torch.float32, device=total.device)
+            norm = torch.empty(1, dtype=torch.float32, device=total.device)
+            _ext_mod().clip_coef(total.reshape(1).contiguous(), float(max_norm), coef, norm)
+            self.grad_scale = coef
+            return norm.view(())
+        norm = total.sqrt()
         coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
         grads = [g for g in (self._reduced_grad(b) for b in self.buckets) if g is not None]
         if grads:

@@ -96,6 +96,22 @@ def load_consolidated_state_dict(model: nn.Module, state: dict[str, torch.Tensor
             own[key].data.copy_(v.to(own[key].device, own[key].dtype))
 
 
+def _barrier() -> None:
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+def _check_kernel_status(model: nn.Module) -> None:
+    """Synchronous read of the device status word before parameters are consolidated and written."""
+    dev = next((p.device for p in model.parameters() if p.device.type == "cuda"), None)
+    if dev is None:
+        return
+    from mint_b200.ops import _ext  # noqa: PLC0415
+
+    if _ext.available() and _ext.kernels_enabled():
+        _ext.status_watch(dev.index or 0).flush()
+
+
 class Checkpointer:
     def __init__(self, config: CheckpointerConfig, *, is_main_process: bool) -> None:
         self.checkpoint_dir = Path(config.checkpoint_dir)
@@ -132,10 +148,20 @@ class Checkpointer:
             should = step % self.save_every_n_steps == 0
         if not should:
             return None
+        _check_kernel_status(model)  # never write parameters that a failed kernel may have touched
         model_sd = consolidated_state_dict(model)
         optim_sd = optimizer.state_dict()
-        if not self.is_main_process:
+        try:
+            if self.is_main_process:
+                return self._write(step, model_sd, optim_sd, dataloader_state, val_loss, is_best)
             return None
+        finally:
+            # rank 0 writes for seconds while the others would otherwise start the next step and
+            # wait in their fused collectives for it: every rank leaves the save together
+            _barrier()
+
+    def _write(self, step: int, model_sd: dict, optim_sd: dict, dataloader_state: dict[str, Any],
+               val_loss: float | None, is_best: bool) -> Path:
         ckpt = {
             "step": step,
             "model_state_dict": model_sd,

@@ -127,6 +127,26 @@ class Device:
         if eng is not None:
             eng.sync_grads = enabled
 
+    def _poll_kernel_status(self) -> None:
+        """Raise if a kernel of the previous step recorded an error (a timed-out peer wait in a
+        fused collective, a bad argument). The snapshot is asynchronous, so the host never stalls
+        on the current step; the update kernels skip their updates on the device meanwhile."""
+        if not self.is_cuda:
+            return
+        from mint_b200.ops import _ext  # noqa: PLC0415
+
+        if _ext.available() and _ext.kernels_enabled():
+            _ext.status_watch(self.device.index or 0).poll()
+
+    def check_kernel_status(self) -> None:
+        """Synchronous form of the per-step check (checkpointing, end of training)."""
+        if not self.is_cuda:
+            return
+        from mint_b200.ops import _ext  # noqa: PLC0415
+
+        if _ext.available() and _ext.kernels_enabled():
+            _ext.status_watch(self.device.index or 0).flush()
+
     def optimizer_step(self, optimizer: torch.optim.Optimizer, grad_clip: float = 0.0, params=None) -> None:  # noqa: ANN001
         eng = getattr(optimizer, "engine", None)
         if eng is not None:
@@ -138,7 +158,12 @@ class Device:
             if grad_clip > 0:
                 eng.clip_grad_norm(grad_clip)
             optimizer.step()
+            self._poll_kernel_status()
             return
+        self._optimizer_step_plain(optimizer, grad_clip, params)
+        self._poll_kernel_status()
+
+    def _optimizer_step_plain(self, optimizer: torch.optim.Optimizer, grad_clip: float, params) -> None:  # noqa: ANN001
         if grad_clip > 0 and params is None:
             raise ValueError("params required for grad clipping")
         if self.scaler.is_enabled():

@@ -47,11 +47,12 @@ def main() -> None:
         dist.all_gather(parts, x_local)
         full = torch.cat(parts, dim=1)  # [B, T, K]
         for kmajor in (True, False):
-            comm.begin_forward()
-            buf = comm._saved_buffer(B * T * K * 2)
+            slot, buf = comm.acquire(B * T * K * 2)
             buf.view((B, world, seg, K), torch.bfloat16)[:, rank].copy_(x_local)
             wb = w if kmajor else w.t().contiguous()
             y = comm.gemm_ag(buf, B * T, K, wb, kmajor, seg)
+            comm.mark_read_by_peers(slot)
+            comm.release(slot)
             ref = full.reshape(B * T, K).float() @ w.float().t()
             e = rel(y, ref)
             ok = e < 1e-2

@@ -88,3 +88,17 @@ def test_noalloc_rejects_sizes_above_the_limit():
     out = torch.empty_like(q)
     rc, msg = _call(fn, q, q, k, k, q, lse, None, out, out, out, True, -1, 0.1, None)
     assert rc == 2 and "limit" in msg
+
+
+def test_noalloc_internal_status_word_reads_clean():
+    """Calls made with status == NULL report into a word inside the library; the companion C
+    function reads (and can clear) it, so such callers still learn about a timed-out wait."""
+    mod, fn = _lib()
+    _case(mod, fn, 2, 1, 512, 4, 4, True, -1, False)
+    lib = ctypes.CDLL(mod.__file__)
+    read = lib.mint_flash_attn_bwd_noalloc_status
+    read.restype = ctypes.c_int
+    read.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
+    out = ctypes.c_uint(123)
+    assert read(1, ctypes.byref(out)) == 0
+    assert out.value == 0
