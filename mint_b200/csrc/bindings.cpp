@@ -97,6 +97,23 @@ static at::Tensor status_tensor() {
   return at::from_blob(p, {1}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, dev));
 }
 
+// Copy `height` rows of `width` bytes from src (row pitch spitch bytes) to dst (pitch dpitch) on the
+// current stream: the sequence shard of a tensor-parallel rank into its slots of the gathered
+// buffer (one strided 2-D copy instead of an elementwise kernel).
+static void copy_rows_2d(const at::Tensor& dst, int64_t dst_offset_bytes, int64_t dpitch, const at::Tensor& src,
+                         int64_t spitch, int64_t width, int64_t height) {
+  MINT_CHECK(dst.is_cuda() && src.is_cuda(), "copy_rows_2d needs CUDA tensors");
+  MINT_CHECK(width <= dpitch && width <= spitch && height >= 0, "copy_rows_2d: bad geometry");
+  MINT_CHECK(dst_offset_bytes + (height - 1) * dpitch + width <= dst.numel() * dst.element_size(),
+             "copy_rows_2d: destination too small");
+  MINT_CHECK((height - 1) * spitch + width <= src.numel() * src.element_size(), "copy_rows_2d: source too small");
+  if (height == 0 || width == 0) return;
+  c10::cuda::CUDAGuard g(dst.device());
+  char* d = static_cast<char*>(dst.data_ptr()) + dst_offset_bytes;
+  MINT_CUDA_CHECK(cudaMemcpy2DAsync(d, dpitch, src.data_ptr(), spitch, width, height, cudaMemcpyDeviceToDevice,
+                                    at::cuda::getCurrentCUDAStream()));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mint_b200 sm_100a kernels";
   m.def("read_status", &read_status, "read (and optionally clear) this device's kernel status word",
@@ -104,6 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_wait_limit_ns", &set_wait_limit, "bound (ns) of every spin-wait in this device's kernels");
   m.def("wait_limit_ns", &get_wait_limit, "current spin-wait bound (ns) of this device's kernels");
   m.def("status_tensor", &status_tensor, "this device's kernel status word as a 1-element int32 tensor");
+  m.def("copy_rows_2d", &copy_rows_2d, "strided 2-D device copy of rows (cudaMemcpy2DAsync)");
   m.def("gemm", &mint::gemm_bf16, "C = alpha * op(A) @ op(B) + beta * D (tcgen05)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("D"), py::arg("a_kmajor"), py::arg("b_kmajor"), py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("alpha_t") = py::none(), py::arg("accumulate") = false);

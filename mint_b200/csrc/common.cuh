@@ -198,6 +198,11 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// at most N bulk groups of this thread still pending (their writes not yet performed)
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // ------------------------------------------------------------------------------------------
 // tcgen05 (5th-generation tensor cores, accumulators in tensor memory)

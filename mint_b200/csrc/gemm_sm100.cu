@@ -408,14 +408,17 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
 //     in place. Copy warps pull the peers' chunks (128-row blocks, claimed dynamically) over NVLink
 //     into it and publish a per-block flag; the TMA producer waits for a block's flag before
 //     loading it. This rank's own rows are scheduled first, so compute starts at once.
-//   COMM 2, GEMM -> reduce-scatter: tiles of peers' chunks are computed first and pushed from the
-//     epilogue into the owner's receive slot (peer stores) with a per-warp flag; this rank's own
-//     tiles come last and their epilogue adds the received partials before the TMA store of the
-//     reduced rows (C then covers only this rank's chunk, in local row order).
+//   COMM 2, GEMM -> reduce-scatter: tiles of peers' chunks are computed first; the epilogue stages
+//     each 32 x 64 piece in shared memory and a TMA store (one tensor map per peer over that peer's
+//     receive slot for this rank) carries it over NVLink, so the epilogue warps never wait on remote
+//     stores. A warp publishes a tile's flag once the tile's stores are complete, two tiles behind
+//     the newest. This rank's own tiles come last; their epilogue adds the received partials before
+//     the TMA store of the reduced rows (C then covers only this rank's chunk, in local row order).
 // Every call has a sequence number `seq`; flags hold the seq of the call that set them and are
 // never reset. At its start each rank writes seq into every peer's arrive[rank]; no rank reads or
 // writes a peer's buffers of call seq before seeing that peer arrive at seq.
 struct CommParams {
+  CUtensorMap rs_push_map[8];    // RS: peer p's receive slot for this rank as a TMA store map ([Mc, N] bf16)
   int rank, world, seg, seq;
   int* arrive_local;             // [world] (symmetric): arrive_local[p] = latest call rank p entered
   int* arrive_peer[8];           // peers' arrive arrays
@@ -452,19 +455,40 @@ __device__ __forceinline__ int comm_tile_m(const CommParams& c, int o, int tiles
 }
 
 // RS epilogue of one warp's 32 rows x BN columns: push to the owner, or reduce and store.
-constexpr int kRsPend = 16;  // pushed tiles whose flags a warp may hold back before one fence
+constexpr int kRsPend = 16;  // room of the per-warp queue of pushed tiles whose flags are pending
+constexpr int kRsLag = 2;    // a pushed tile's flag is released once two newer tiles were pushed
 
-// Publish the flags of the tiles this warp pushed since its last flush: one system-scope fence
-// orders all their peer stores before the releases.
+// Publish the flags of every tile this warp pushed: wait until all of this lane's TMA stores have
+// been performed, order them (async proxy, then system scope) before the releases.
 __device__ __forceinline__ void rs_flush(const CommParams& c, int* pend, int& npend, int lane) {
   if (npend == 0) return;
-  __threadfence_system();
-  __syncwarp();
   if (lane == 0) {
+    bulk_wait_all();
+    fence_proxy_async_global();
+    __threadfence_system();
     for (int i = 0; i < npend; ++i) st_release_sys(c.rs_flag_peer[pend[2 * i]] + pend[2 * i + 1], c.seq);
   }
   __syncwarp();
   npend = 0;
+}
+
+// After a push of kG bulk groups: release the oldest pending tile once only the kRsLag newest tiles
+// (kRsLag * kG groups, every tile commits exactly kG) may still be in flight.
+template <int kG>
+__device__ __forceinline__ void rs_release_lagged(const CommParams& c, int* pend, int& npend, int lane) {
+  if (npend <= kRsLag) return;
+  if (lane == 0) {
+    bulk_wait<kRsLag * kG>();
+    fence_proxy_async_global();
+    __threadfence_system();
+    st_release_sys(c.rs_flag_peer[pend[0]] + pend[1], c.seq);
+    for (int i = 1; i < npend; ++i) {
+      pend[2 * (i - 1)] = pend[2 * i];
+      pend[2 * (i - 1) + 1] = pend[2 * i + 1];
+    }
+  }
+  __syncwarp();
+  --npend;
 }
 
 template <int BN>
@@ -482,7 +506,7 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
     bool ok = true;
     if (lane == 0) ok = wait_flag(&c.arrive_local[chunk], c.seq, true, p.status, kStatusTimeoutPeer, abort_flag);
     if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
-    __nv_bfloat16* dst = c.rs_push[chunk];
+    const CUtensorMap* pmap = &c.rs_push_map[chunk];
 #pragma unroll 1
     for (int g = 0; g < BN / 64; ++g) {
       uint32_t r0[32], r1[32];
@@ -490,43 +514,39 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
       tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, r1);
       tmem_ld_wait();
       const int col0 = col_base + g * 64;
-      if (col0 >= p.N) continue;
-      uint8_t* buf = bufs + (seq & 1) * 4096;
-      if (lane == 0) bulk_wait_read<1>();
-      __syncwarp();
+      if (col0 < p.N) {
+        uint8_t* buf = bufs + (seq & 1) * 4096;
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 u;
-        u.x = pack_bf16x2(alpha * __uint_as_float(r0[8 * j]), alpha * __uint_as_float(r0[8 * j + 1]));
-        u.y = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 2]), alpha * __uint_as_float(r0[8 * j + 3]));
-        u.z = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 4]), alpha * __uint_as_float(r0[8 * j + 5]));
-        u.w = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 6]), alpha * __uint_as_float(r0[8 * j + 7]));
-        *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
-        u.x = pack_bf16x2(alpha * __uint_as_float(r1[8 * j]), alpha * __uint_as_float(r1[8 * j + 1]));
-        u.y = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 2]), alpha * __uint_as_float(r1[8 * j + 3]));
-        u.z = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 4]), alpha * __uint_as_float(r1[8 * j + 5]));
-        u.w = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 6]), alpha * __uint_as_float(r1[8 * j + 7]));
-        *reinterpret_cast<uint4*>(buf + lane * 128 + (((j + 4) ^ (lane & 7)) << 4)) = u;
+        for (int j = 0; j < 4; ++j) {
+          uint4 u;
+          u.x = pack_bf16x2(alpha * __uint_as_float(r0[8 * j]), alpha * __uint_as_float(r0[8 * j + 1]));
+          u.y = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 2]), alpha * __uint_as_float(r0[8 * j + 3]));
+          u.z = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 4]), alpha * __uint_as_float(r0[8 * j + 5]));
+          u.w = pack_bf16x2(alpha * __uint_as_float(r0[8 * j + 6]), alpha * __uint_as_float(r0[8 * j + 7]));
+          *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+          u.x = pack_bf16x2(alpha * __uint_as_float(r1[8 * j]), alpha * __uint_as_float(r1[8 * j + 1]));
+          u.y = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 2]), alpha * __uint_as_float(r1[8 * j + 3]));
+          u.z = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 4]), alpha * __uint_as_float(r1[8 * j + 5]));
+          u.w = pack_bf16x2(alpha * __uint_as_float(r1[8 * j + 6]), alpha * __uint_as_float(r1[8 * j + 7]));
+          *reinterpret_cast<uint4*>(buf + lane * 128 + (((j + 4) ^ (lane & 7)) << 4)) = u;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        // the owner's receive slot for this rank: rows lrow0.. of chunk-local order, columns col0..
+        if (lane == 0) tma_store_3d(pmap, buf, col0, static_cast<int>(lrow0), 0);
+        ++seq;
       }
-      __syncwarp();
-      // read back row-contiguously: 8 lanes cover one row's 128 bytes, 4 rows per instruction
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int rr = k * 4 + (lane >> 3);
-        const int j = lane & 7;
-        const long long row = lrow0 + rr;
-        const int col = col0 + j * 8;
-        const uint4 u = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((j ^ (rr & 7)) << 4));
-        if (row < c.mc && col < p.N) *reinterpret_cast<uint4*>(dst + row * p.N + col) = u;
-      }
-      ++seq;
+      if (lane == 0) bulk_commit();  // exactly BN / 64 groups per tile (empty past N) for the lag count
     }
     if (lane == 0) {
       pend[2 * npend] = chunk;
       pend[2 * npend + 1] = static_cast<int>(fidx);
     }
     __syncwarp();
-    if (++npend == kRsPend) rs_flush(c, pend, npend, lane);
+    ++npend;
+    rs_release_lagged<BN / 64>(c, pend, npend, lane);
     return true;
   }
   // own rows: publish what this warp pushed (peers may be waiting on it), then wait for every
@@ -1228,14 +1248,19 @@ void gemm_rs(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, bool b_k
   c.rs_flag_stride = flags.size(1);
   MINT_CHECK(static_cast<int64_t>(push_ptrs.size()) == world && static_cast<int64_t>(flag_ptrs.size()) == world,
              "one push / flag pointer per rank");
+  constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
   for (int q = 0; q < world; ++q) {
     c.rs_push[q] = reinterpret_cast<__nv_bfloat16*>(push_ptrs[q]);
     c.rs_flag_peer[q] = reinterpret_cast<int*>(flag_ptrs[q]);
+    // peer q's receive slot for this rank, [Mc, N] bf16 in its symmetric buffer: the epilogue's
+    // 32 x 64 staging boxes leave through TMA stores with this map (plain stores, no multicast)
+    if (q != rank) {
+      c.rs_push_map[q] = make_tmap_3d(c.rs_push[q], BF, 2, N, c.mc, 1, N, c.mc * N, 64, 32, 1, SW128);
+    }
   }
   c.rs_recv = reinterpret_cast<const __nv_bfloat16*>(recv.data_ptr());
   c.rs_flag_local = flags.data_ptr<int>();
-  constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
   const CUtensorMap ta = make_tmap_3d(A.data_ptr(), BF, 2, K, M, 1, A.stride(0), M * A.stride(0), 64, 128, 1, SW128);
   const uint64_t ldb = B.stride(0);
   const CUtensorMap tb = b_kmajor ? make_tmap_3d(B.data_ptr(), BF, 2, K, N, 1, ldb, N * ldb, 64, 128, 1, SW128)

@@ -200,31 +200,27 @@ __global__ void normuon_apply_kernel(const __nv_bfloat16* __restrict__ X, const 
   }
 }
 
-// Sum of squares over a table of fp32 segments (pointers and lengths), accumulated into out[0].
-// grid (chunks, segments).
+// Sum of squares over a table of fp32 pieces (pointers and lengths), accumulated into out[0]. One
+// block per row: callers split long segments into pieces of similar size (kPieceElems), so the
+// work is balanced however unequal the tensors are.
 __global__ void sumsq_multi_kernel(const long long* __restrict__ ptrs, const long long* __restrict__ sizes,
                                    float* __restrict__ out) {
   __shared__ float red[32];
-  const float* x = reinterpret_cast<const float*>(ptrs[blockIdx.y]);
-  const long long n = sizes[blockIdx.y];
+  const float* x = reinterpret_cast<const float*>(ptrs[blockIdx.x]);
+  const long long n = sizes[blockIdx.x];
   const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
   float acc = 0.f;
+  long long start = 0;
   if (vec) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     const long long n4 = n >> 2;
-    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n4;
-         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    for (long long e = threadIdx.x; e < n4; e += blockDim.x) {
       const float4 v = x4[e];
       acc = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, acc))));
     }
-    for (long long e = (n4 << 2) + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n;
-         e += static_cast<long long>(gridDim.x) * blockDim.x)
-      acc = fmaf(x[e], x[e], acc);
-  } else {
-    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n;
-         e += static_cast<long long>(gridDim.x) * blockDim.x)
-      acc = fmaf(x[e], x[e], acc);
+    start = n4 << 2;
   }
+  for (long long e = start + threadIdx.x; e < n; e += blockDim.x) acc = fmaf(x[e], x[e], acc);
   acc = block_sum(acc, red);
   if (threadIdx.x == 0) atomicAdd(out, acc);
 }
@@ -237,29 +233,26 @@ __global__ void clip_coef_kernel(const float* __restrict__ sumsq, float max_norm
   *coef = fminf(1.f, max_norm / (nv + 1e-6f));
 }
 
-// bf16 copies of fp32 segments: dst[k] = bf16(src[k]) for every (src, dst, size) row of the table.
-// grid (chunks, segments); every src / dst is 16 / 8-byte aligned and size % 4 == 0 on the vector path.
+// bf16 copies of fp32 pieces: dst[k] = bf16(src[k]) for every (src, dst, size) row of the table,
+// one block per row (long segments are split into pieces of similar size by the caller).
 __global__ void cast_multi_kernel(const long long* __restrict__ src, const long long* __restrict__ dst,
                                   const long long* __restrict__ sizes) {
-  const float* s = reinterpret_cast<const float*>(src[blockIdx.y]);
-  __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst[blockIdx.y]);
-  const long long n = sizes[blockIdx.y];
+  const float* s = reinterpret_cast<const float*>(src[blockIdx.x]);
+  __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst[blockIdx.x]);
+  const long long n = sizes[blockIdx.x];
   const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15u) == 0) && ((reinterpret_cast<uintptr_t>(d) & 7u) == 0);
   long long start = 0;
   if (vec) {
     const long long n4 = n >> 2;
     const float4* s4 = reinterpret_cast<const float4*>(s);
     uint2* d4 = reinterpret_cast<uint2*>(d);
-    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n4;
-         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    for (long long e = threadIdx.x; e < n4; e += blockDim.x) {
       const float4 v = s4[e];
       d4[e] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
     }
     start = n4 << 2;
   }
-  for (long long e = start + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n;
-       e += static_cast<long long>(gridDim.x) * blockDim.x)
-    d[e] = __float2bfloat16_rn(s[e]);
+  for (long long e = start + threadIdx.x; e < n; e += blockDim.x) d[e] = __float2bfloat16_rn(s[e]);
 }
 
 int chunks_for(long long work, int dev, int ys) {
@@ -385,18 +378,16 @@ void normuon_apply(const at::Tensor& X, const at::Tensor& scale, const at::Tenso
   count_launch();
 }
 
-// out[0] += sum of squares of every segment (out is not cleared here)
+// out[0] += sum of squares of every piece (out is not cleared here); one block per table row
 void sumsq_multi(const at::Tensor& ptrs, const at::Tensor& sizes, at::Tensor& out, int64_t max_len) {
   const int64_t n = ptrs.numel();
   check_ptr_table(ptrs, n, "ptrs");
   check_ptr_table(sizes, n, "sizes");
   check_contig(out, "out");
+  (void)max_len;
   if (n == 0) return;
-  MINT_CHECK(n < 65536, "too many segments");
   c10::cuda::CUDAGuard g(out.device());
-  dim3 grid(chunks_for(std::max<int64_t>(1, max_len / 4), out.get_device(), static_cast<int>(n)),
-            static_cast<unsigned>(n));
-  sumsq_multi_kernel<<<grid, kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  sumsq_multi_kernel<<<static_cast<unsigned>(n), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const long long*>(ptrs.data_ptr<int64_t>()),
       reinterpret_cast<const long long*>(sizes.data_ptr<int64_t>()), out.data_ptr<float>());
   MINT_CUDA_CHECK(cudaGetLastError());
@@ -419,12 +410,10 @@ void cast_multi(const at::Tensor& src, const at::Tensor& dst, const at::Tensor& 
   check_ptr_table(src, n, "src");
   check_ptr_table(dst, n, "dst");
   check_ptr_table(sizes, n, "sizes");
+  (void)max_len;
   if (n == 0) return;
-  MINT_CHECK(n < 65536, "too many segments");
   c10::cuda::CUDAGuard g(src.device());
-  dim3 grid(chunks_for(std::max<int64_t>(1, max_len / 4), src.get_device(), static_cast<int>(n)),
-            static_cast<unsigned>(n));
-  cast_multi_kernel<<<grid, kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  cast_multi_kernel<<<static_cast<unsigned>(n), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const long long*>(src.data_ptr<int64_t>()),
       reinterpret_cast<const long long*>(dst.data_ptr<int64_t>()),
       reinterpret_cast<const long long*>(sizes.data_ptr<int64_t>()));

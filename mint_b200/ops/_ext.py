@@ -145,3 +145,17 @@ def status_watch(device_index: int) -> StatusWatch:
         w = StatusWatch()
         _WATCHES[device_index] = w
     return w
+
+
+PIECE_ELEMS = 1 << 16  # elements per row of the multi-tensor kernels' work tables
+
+
+def piece_table(segments: list[tuple[int, ...]], elem_bytes: tuple[int, ...]) -> list[tuple[int, ...]]:
+    """Split ``(ptr_0, ..., ptr_k, numel)`` segments into rows of at most PIECE_ELEMS elements, each
+    pointer advanced by its own element size, so one block per row gives balanced work."""
+    rows = []
+    for seg in segments:
+        *ptrs, n = seg
+        for off in range(0, n, PIECE_ELEMS):
+            rows.append((*(p + off * eb for p, eb in zip(ptrs, elem_bytes)), min(PIECE_ELEMS, n - off)))
+    return rows

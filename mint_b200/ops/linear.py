@@ -97,10 +97,11 @@ def refresh_weight_shadows() -> None:
     if table is None:
         if len(_REFRESH_TABLES) > 8:
             _REFRESH_TABLES.clear()
-        table = (torch.tensor([a for a, _b, _n in segs], dtype=torch.int64, device=dev),
-                 torch.tensor([b for _a, b, _n in segs], dtype=torch.int64, device=dev),
-                 torch.tensor([n for _a, _b, n in segs], dtype=torch.int64, device=dev),
-                 max(n for _a, _b, n in segs))
+        rows = _ext.piece_table(segs, (4, 2))
+        table = (torch.tensor([a for a, _b, _n in rows], dtype=torch.int64, device=dev),
+                 torch.tensor([b for _a, b, _n in rows], dtype=torch.int64, device=dev),
+                 torch.tensor([n for _a, _b, n in rows], dtype=torch.int64, device=dev),
+                 _ext.PIECE_ELEMS)
         _REFRESH_TABLES[tkey] = table
     _ext.require().cast_multi(table[0], table[1], table[2], table[3])
     for _key, ent, now in stale:

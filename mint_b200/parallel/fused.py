@@ -47,9 +47,6 @@ class _Symm:
     """One symmetric buffer: the local tensor and every rank's address of it."""
 
     def __init__(self, nbytes: int, group: Any, device: torch.device) -> None:
-        # no kernel here uses NVLink multicast (multimem); keeping the buffers out of multicast
-        # objects also means a rank that dies holds no multicast binding its peers could fault on
-        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415
 
         self.nbytes = nbytes
@@ -186,6 +183,15 @@ def get_comm(group: Any, device: torch.device) -> TPComm:
 
 
 # ------------------------------------------------------------------------------------------ autograd
+def _place_shard(gathered: _Symm, x: torch.Tensor, rank: int, world: int) -> None:
+    """Copy this rank's sequence shard ``x [B, seg, K]`` (bf16) into its rows of the gathered
+    layout ``[B, world, seg, K]``: one strided 2-D copy (B rows of seg*K elements)."""
+    B, seg, K = x.shape
+    x = x if (x.dtype == torch.bfloat16 and x.is_contiguous()) else x.to(torch.bfloat16).contiguous()
+    row = seg * K * 2
+    _ext.require().copy_rows_2d(gathered.buf, rank * row, world * row, x, row, row, B)
+
+
 def _bf16_2d(t: torch.Tensor) -> torch.Tensor:
     t2 = t.reshape(-1, t.shape[-1])
     if t2.dtype != torch.bfloat16 or not t2.is_contiguous():
@@ -203,8 +209,7 @@ class _ColumnParallelFn(torch.autograd.Function):
         T = seg * world
         rows = B * T
         slot, gathered = comm.acquire(rows * K * 2)
-        G = gathered.view((B, world, seg, K), torch.bfloat16)
-        G[:, rank].copy_(x)  # this rank's shard in place; the kernel pulls the others
+        _place_shard(gathered, x, rank, world)  # this rank's shard in place; the kernel pulls the others
         w = _cast_weight(weights, torch.bfloat16)
         y = comm.gemm_ag(gathered, rows, K, w, True, seg)
         comm.mark_read_by_peers(slot)
@@ -254,8 +259,7 @@ class _RowParallelFn(torch.autograd.Function):
         n = dy.shape[-1]
         rows = B * T
         gathered = comm._ring_buffer(rows * n * 2)
-        G = gathered.view((B, world, seg, n), torch.bfloat16)
-        G[:, rank].copy_(dy)
+        _place_shard(gathered, dy, rank, world)
         dx = None
         wc = _cast_weight((w,), torch.bfloat16)  # [N, K/tp] = op(B) read MN-major
         dy_full = comm.gemm_ag(gathered, rows, n, wc, False, seg) if ctx.needs_input_grad[0] else None

@@ -506,9 +506,12 @@ class GradEngine:
         hit = self._norm_tables.get(key)
         dev = pieces[0].device
         if hit is None:
-            ptrs = torch.tensor([k[0] for k in key], dtype=torch.int64, device=dev)
-            sizes = torch.tensor([k[1] for k in key], dtype=torch.int64, device=dev)
-            hit = (ptrs, sizes, max(k[1] for k in key))
+            from mint_b200.ops import _ext  # noqa: PLC0415
+
+            rows = _ext.piece_table(list(key), (4,))
+            ptrs = torch.tensor([r[0] for r in rows], dtype=torch.int64, device=dev)
+            sizes = torch.tensor([r[1] for r in rows], dtype=torch.int64, device=dev)
+            hit = (ptrs, sizes, _ext.PIECE_ELEMS)
             self._norm_tables[key] = hit
         out = torch.zeros(1, dtype=torch.float32, device=dev)
         _ext_mod().sumsq_multi(hit[0], hit[1], out, hit[2])

@@ -1,7 +1,9 @@
 """Failure detection on 2 GPUs without a GPU fault: a rank that skips a fused collective makes its
 peer's kernel give up after a short, run-time wait limit and report a status bit that the host
 turns into an exception, while the parameter-update kernels refuse to apply the step. NVLS and
-NVLink multicast are off (plain peer loads and stores only). Skipped with < 2 GPUs."""
+NVLink multicast are off (plain peer loads and stores only; the test's symmetric buffers live on
+the WORLD group, where torch's symmetric memory accepts TORCH_SYMM_MEM_DISABLE_MULTICAST). Skipped
+with < 2 GPUs."""
 
 import os
 import subprocess

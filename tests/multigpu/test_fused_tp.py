@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_fused_tp_two_gpus():
     worker = Path(__file__).with_name("fused_tp_worker.py")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TORCH_SYMM_MEM_DISABLE_MULTICAST="1", MINT_PG_TIMEOUT_S="120")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MINT_PG_TIMEOUT_S="120")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", str(worker)]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True)
