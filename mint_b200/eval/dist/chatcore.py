@@ -1,9 +1,19 @@
-"""ChatCORE: generate a completion per example and grade it with the dataset's ``evaluate``
-(mint/eval/dist/chatcore.py:16-102). ``Gemma.generate`` accepts the HF-style kwargs used here."""
+"""ChatCORE: generative accuracy of a chat model on SFT eval datasets.
+
+Same contract as the reference evaluator (mint/eval/dist/chatcore.py:16-102): each example's last
+(assistant) message is dropped, the rest is rendered with the chat template, the model continues
+greedily after ``<|assistant_start|>`` until ``<|assistant_end|>`` or ``max_new_tokens``, and the
+dataset's ``evaluate(conversation, completion)`` grades the text; examples are dealt to the data-
+parallel ranks round-robin and the result is ``{"tasks": {name: {"accuracy", "num_examples"}},
+"accuracy": mean over tasks, "eval_time_sec"}``.
+
+Organisation: every rank fills one ``[tasks, 2]`` tally (correct, graded) and the tallies of all
+tasks are summed across the dp group in a single all-reduce at the end; prompts are built by
+``prompt_ids`` and decoded by ``complete``, so a caller can grade one example without a dataset.
+"""
 
 from __future__ import annotations
 
-import copy
 import time
 from typing import Any
 
@@ -21,44 +31,50 @@ class ChatCoreEvaluator(Evaluator):
         self.tokenizer = tokenizer
         self.datasets = datasets
 
+    # ------------------------------------------------------------------ one example
+    def prompt_ids(self, conversation: dict[str, Any]) -> list[int]:
+        """Chat-rendered history without the reference answer, ending in ``<|assistant_start|>``."""
+        history = {**conversation, "messages": list(conversation["messages"][:-1])}
+        ids, _mask = self.tokenizer.render_conversation(history, self.config.seq_length - 1)
+        return [*ids, self.tokenizer.encode_special("<|assistant_start|>")]
+
+    @torch.no_grad()
+    def complete(self, conversation: dict[str, Any]) -> str:
+        ids = self.prompt_ids(conversation)
+        prompt = torch.tensor([ids], dtype=torch.long, device=self.device.device)
+        stop = self.tokenizer.encode_special("<|assistant_end|>")
+        with self.device.autocast():
+            out = self.model.generate(prompt, attention_mask=torch.ones_like(prompt),
+                                      pad_token_id=self.tokenizer.pad_token, max_new_tokens=self.config.max_new_tokens,
+                                      eos_token_id=stop, do_sample=False, use_cache=True)
+        return self.tokenizer.decode(out[0, len(ids):].cpu())[0]
+
+    # ------------------------------------------------------------------ datasets
+    def _share(self, dataset: Any, limit: int | None) -> range:  # noqa: ANN401
+        total = len(dataset) if limit is None else min(limit, len(dataset))
+        return range(self.process_info["dp_rank"], total, self.process_info["dp_size"])
+
     def evaluate(self, num_examples: int | None = None) -> dict[str, Any]:
         self.model.eval()
         t0 = time.perf_counter()
-        results = {}
+        names = [type(ds).__name__ for ds in self.datasets]
+        tally = torch.zeros(len(self.datasets), 2, dtype=torch.float64)
         with torch.no_grad():
-            for ds in self.datasets:
-                results[ds.__class__.__name__] = self._evaluate_dataset(ds, num_examples)
+            for k, ds in enumerate(self.datasets):
+                for idx in self._share(ds, num_examples):
+                    conv = ds[idx]
+                    tally[k, 0] += float(bool(ds.evaluate(conv, self.complete(conv))))
+                    tally[k, 1] += 1.0
+        tally = self._sum_over_dp(tally)
         self.device.synchronize()
-        dt = time.perf_counter() - t0
-        if not results:
-            return {"tasks": {}, "accuracy": 0.0, "eval_time_sec": dt}
-        return {"tasks": results, "accuracy": sum(r["accuracy"] for r in results.values()) / len(results),
-                "eval_time_sec": dt}
+        tasks = {name: {"accuracy": float(c / n) if n > 0 else 0.0, "num_examples": int(n)}
+                 for name, (c, n) in zip(names, tally.tolist(), strict=True)}
+        mean = sum(t["accuracy"] for t in tasks.values()) / len(tasks) if tasks else 0.0
+        return {"tasks": tasks, "accuracy": mean, "eval_time_sec": time.perf_counter() - t0}
 
-    def _evaluate_dataset(self, dataset: Any, num_examples: int | None = None) -> dict[str, Any]:  # noqa: ANN401
-        total = len(dataset) if num_examples is None else min(num_examples, len(dataset))
-        rank, world = self.process_info["dp_rank"], self.process_info["dp_size"]
-        correct = count = 0
-        for i in range(rank, total, world):
-            conv = dataset[i]
-            if dataset.evaluate(conv, self._generate_completion(conv)):
-                correct += 1
-            count += 1
-        if world > 1:
-            t = torch.tensor([correct, count], dtype=torch.float32, device=self.device.device)
-            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.device.parallel.dp_group)
-            correct, count = t[0].item(), t[1].item()
-        return {"accuracy": correct / count if count else 0.0, "num_examples": int(count)}
-
-    def _generate_completion(self, conversation: dict) -> str:
-        conversation = copy.deepcopy(conversation)
-        conversation["messages"].pop()
-        ids, _ = self.tokenizer.render_conversation(conversation, self.config.seq_length - 1)
-        ids.append(self.tokenizer.encode_special("<|assistant_start|>"))
-        inp = torch.tensor([ids], dtype=torch.long, device=self.device.device)
-        with self.device.autocast():
-            out = self.model.generate(inp, attention_mask=torch.ones_like(inp), pad_token_id=self.tokenizer.pad_token,
-                                      max_new_tokens=self.config.max_new_tokens,
-                                      eos_token_id=self.tokenizer.encode_special("<|assistant_end|>"),
-                                      do_sample=False, use_cache=True)
-        return self.tokenizer.decode(out[0, inp.shape[1] :].cpu())[0]
+    def _sum_over_dp(self, tally: torch.Tensor) -> torch.Tensor:
+        if self.process_info["dp_size"] <= 1 or tally.numel() == 0:
+            return tally
+        t = tally.to(self.device.device, torch.float32)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.device.parallel.dp_group)
+        return t.double().cpu()

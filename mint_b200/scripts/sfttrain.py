@@ -9,14 +9,8 @@ import torch.distributed as dist
 
 from mint_b200.config.base import Config
 from mint_b200.data.dataloader import DataloaderConfig
-from mint_b200.data.datasets.arc import ARC
 from mint_b200.data.datasets.base import SFTEvalDataset
-from mint_b200.data.datasets.customjsonl import CustomJSON
-from mint_b200.data.datasets.gsm8k import GSM8K
-from mint_b200.data.datasets.humaneval import HumanEval
-from mint_b200.data.datasets.mmlu import MMLU
-from mint_b200.data.datasets.smoltalk import SmolTalk
-from mint_b200.data.datasets.spellingbee import SimpleSpelling, SpellingBee
+from mint_b200.data.datasets.catalog import ARC, GSM8K, MMLU, CustomJSON, HumanEval, SimpleSpelling, SmolTalk, SpellingBee
 from mint_b200.data.dist.sft import DistributedSFTDataloader
 from mint_b200.models.gemma import GemmaConfig, configure_optimizer
 from mint_b200.optim.muon_adamw import MuonAdamWConfig

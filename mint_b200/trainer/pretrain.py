@@ -1,9 +1,13 @@
-"""Pretraining loop (mint/trainer/pretrain.py:27-266): resume (step + per-rank dataloader state),
-gradient accumulation, BPB eval + best checkpoint, CORE eval, profiler stepping, device-timed tok/s."""
+"""Pretraining task on the shared loop (reference behaviour: mint/trainer/pretrain.py:27-266).
+
+Resume restores model, optimizer, step and this rank's dataloader cursor from the checkpoint's
+``{"per_rank": {rank: state}}`` table (gathered to rank 0 when saving); evaluations are the
+bits-per-byte validation loss (which also drives the best checkpoint) and the CORE benchmark; the
+profiler records windows of optimizer steps.
+"""
 
 from __future__ import annotations
 
-import time
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -14,12 +18,10 @@ from torch.optim import Optimizer
 
 from mint_b200.eval.bpb import BPBEvaluator
 from mint_b200.eval.dist.core import CoreEvaluator
-from mint_b200.trainer.base import BasetrainConfig, BaseTrainer
-from mint_b200.trainer.scheduler import Scheduler
-from mint_b200.utils.checkpointer import Checkpointer
+from mint_b200.trainer.base import BasetrainConfig, BaseTrainer, Evaluation
 from mint_b200.utils.device import Device
 from mint_b200.utils.logger import logger
-from mint_b200.utils.profiler import ProfilerConfig, TorchProfiler
+from mint_b200.utils.profiler import ProfilerConfig, StepProfiler
 
 
 @dataclass
@@ -27,129 +29,108 @@ class PretrainConfig(BasetrainConfig):
     profiler: ProfilerConfig = field(default_factory=ProfilerConfig)
 
 
+def flatten_metrics(prefix: str, value: Any, out: dict[str, Any] | None = None) -> dict[str, Any]:  # noqa: ANN401
+    """``{"a": {"b": 1}}`` under ``prefix`` -> ``{"prefix/a/b": 1}``."""
+    out = {} if out is None else out
+    if isinstance(value, dict):
+        for k, v in value.items():
+            flatten_metrics(f"{prefix}/{k}", v, out)
+    else:
+        out[prefix] = value
+    return out
+
+
 class PreTrainer(BaseTrainer):
     def __init__(self, model: nn.Module, optimizer: Optimizer, dataloader: Any, device: Device,  # noqa: ANN401
                  config: PretrainConfig, tokenizer: Any = None, core_bundle_dir: str | None = None) -> None:  # noqa: ANN401
-        super().__init__(model=model, optimizer=optimizer, dataloader=dataloader, device=device, config=config,
-                         tokenizer=tokenizer)
-        self.checkpointer = Checkpointer(config=config.ckpt, is_main_process=self.is_main_process)
-        self.scheduler = Scheduler(num_iterations=config.train_num_steps, config=config.sched)
-        self.core_evaluator = None
-        if tokenizer is not None:
-            try:
-                self.core_evaluator = CoreEvaluator(model=model, config=config.eval, tokenizer=tokenizer,
-                                                    device=device, **({"bundle_dir": core_bundle_dir} if core_bundle_dir else {}))
-            except FileNotFoundError:
-                logger.warning("CORE eval bundle not found; CORE evaluation disabled")
+        super().__init__(model, optimizer, dataloader, device, config, tokenizer)
         self.bpb_evaluator = BPBEvaluator(model=model, config=config.eval, device=device, dataloader=dataloader)
-        self.start_step = 0
-        self.dataloader_state: dict = {}
+        self.core_evaluator = self._make_core(core_bundle_dir)
+        self.profiler = StepProfiler(config.profiler)
+        self.resume_state: dict = {}
         if config.ckpt.resume_from_checkpoint:
-            self._load_pretrained_checkpoint()
-        self.profiler = TorchProfiler(config.profiler)
-        self.last_metrics: dict = {}
+            self.resume()
 
-    def _load_pretrained_checkpoint(self) -> None:
-        path = self.config.ckpt.resume_from_checkpoint
+    def _make_core(self, bundle_dir: str | None) -> CoreEvaluator | None:
+        if self.tokenizer is None:
+            return None
+        kw = {"bundle_dir": bundle_dir} if bundle_dir else {}
+        try:
+            return CoreEvaluator(model=self.model, config=self.config.eval, tokenizer=self.tokenizer,
+                                 device=self.device, **kw)
+        except FileNotFoundError:
+            logger.warning("CORE eval bundle not found; CORE evaluation disabled")
+            return None
+
+    # ------------------------------------------------------------------ resume / dataloader state
+    def resume(self) -> None:
+        src = self.config.ckpt.resume_from_checkpoint
         info = self.checkpointer.load_checkpoint(model=self.model, optimizer=self.optimizer,
-                                                 checkpoint_path=path if isinstance(path, str) else None,
+                                                 checkpoint_path=src if isinstance(src, str) else None,
                                                  load_best=self.config.ckpt.load_best_checkpoint)
         self.start_step = info["step"]
-        self.dataloader_state = self._extract_rank_dataloader_state(info.get("dataloader_state", {}))
-        if self.dataloader_state and hasattr(self.dataloader, "set_state"):
-            self.dataloader.set_state(self.dataloader_state)
+        self.resume_state = self.rank_state(info.get("dataloader_state", {}))
+        if self.resume_state and hasattr(self.dataloader, "set_state"):
+            self.dataloader.set_state(self.resume_state)
         logger.info(f"Resuming training from step {self.start_step}")
 
-    def _local_dataloader_state(self) -> dict:
-        return self.dataloader.get_state() if hasattr(self.dataloader, "get_state") else {}
+    def rank_state(self, saved: dict) -> dict:
+        """This rank's dataloader state from a checkpoint (a single-process state is used as is)."""
+        if not saved:
+            return {}
+        table = saved.get("per_rank")
+        if table is None:
+            return saved
+        rank = self.process_info["rank"] if self.process_info["distributed"] else 0
+        return table.get(rank, table.get(str(rank), {}))
 
-    def _get_dataloader_state(self) -> dict:
-        local = self._local_dataloader_state()
+    def dataloader_state(self) -> dict:
+        """Collective under distribution: every rank's cursor, gathered to rank 0."""
+        local = self.dataloader.get_state() if hasattr(self.dataloader, "get_state") else {}
         if not self.process_info["distributed"]:
             return local
-        if self.is_main_process:
-            gathered: list[dict] = [{} for _ in range(self.process_info["world_size"])]
-            dist.gather_object(local, gathered, dst=0)
-            return {"per_rank": dict(enumerate(gathered))}
-        dist.gather_object(local, None, dst=0)
-        return {}
+        gathered: list[dict] | None = [{} for _ in range(self.process_info["world_size"])] if self.is_main_process else None
+        dist.gather_object(local, gathered, dst=0)
+        return {"per_rank": dict(enumerate(gathered))} if gathered is not None else {}
 
-    def _extract_rank_dataloader_state(self, state: dict) -> dict:
-        if not state:
-            return {}
-        if not self.process_info["distributed"]:
-            return state.get("per_rank", {}).get(0, state) if "per_rank" in state else state
-        per = state.get("per_rank", {})
-        return per.get(self.process_info["rank"], per.get(str(self.process_info["rank"]), {}))
+    # ------------------------------------------------------------------ task
+    def micro_batches(self) -> Any:  # noqa: ANN401
+        return self.dataloader.batch_loader(split="train", resume_state=self.resume_state or None)
 
-    def _run_evaluation(self, evaluator: Any, step: int, metric_prefix: str, *, save_checkpoint: bool = False,  # noqa: ANN401
-                        **eval_kwargs: Any) -> dict[str, Any]:  # noqa: ANN401
+    def evaluations(self) -> list[Evaluation]:
+        evs = [Evaluation("val", self.config.eval_every_n_steps, self._validate)]
+        if self.core_evaluator is not None:
+            evs.append(Evaluation("core", self.config.core_eval_every_n_step, self._core))
+        return evs
+
+    def _evaluate(self, evaluator: Any, prefix: str, step: int, **kw: Any) -> dict[str, Any]:  # noqa: ANN401
         self.model.eval()
         with torch.no_grad():
-            results = evaluator.evaluate(**eval_kwargs)
+            results = evaluator.evaluate(**kw)
         self.model.train()
-        metrics: dict[str, Any] = {}
-
-        def flatten(prefix: str, value: Any) -> None:  # noqa: ANN401
-            if isinstance(value, dict):
-                for k, v in value.items():
-                    flatten(f"{prefix}/{k}", v)
-            else:
-                metrics[prefix] = value
-
-        for k, v in results.items():
-            flatten(f"{metric_prefix}/{k}", v)
+        metrics = flatten_metrics(prefix, results)
         if self.is_main_process:
             logger.info(f"Eval step={step} | " + " | ".join(f"{k}={v:.4f}" for k, v in metrics.items()
                                                             if isinstance(v, (int, float))))
-        self._log_wandb(metrics, step=step)
-        val_loss = results.get("loss") if save_checkpoint else None
-        if val_loss is not None:
-            state = self._get_dataloader_state()
-            is_best = self.checkpointer.should_checkpoint_on_eval(val_loss)
-            self.checkpointer.save_checkpoint(step=step, model=self.model, optimizer=self.optimizer,
-                                              dataloader_state=state, val_loss=val_loss, is_best=is_best)
+        self.sink.log(metrics, step=step)
         return results
 
+    def _validate(self, step: int) -> None:
+        results = self._evaluate(self.bpb_evaluator, "val", step, num_steps=self.config.eval_num_steps)
+        val_loss = results.get("loss")
+        if val_loss is not None:
+            best = self.checkpointer.should_checkpoint_on_eval(val_loss)
+            self.save(step, val_loss=val_loss, is_best=best)
+        if hasattr(self.dataloader, "sample"):
+            self.log_sample_predictions(self.dataloader.sample(num_samples=3))
+
+    def _core(self, step: int) -> None:
+        self._evaluate(self.core_evaluator, "core", step, task_labels=["hellaswag_zeroshot"], limit=1)
+
+    # ------------------------------------------------------------------ profiler around the loop
+    def after_step(self, step: int, metrics: dict) -> None:  # noqa: ARG002
+        self.profiler.step()
+
     def train(self) -> None:
-        self.model.train()
-        t_train0 = time.perf_counter()
-        accum = self.config.gradient_accumulation_steps
-        micro_step = self.start_step * accum
-        acc_loss: Any = 0.0
-        batches = self.dataloader.batch_loader(split="train", resume_state=self.dataloader_state or None)
         with self.profiler:
-            for inputs, targets, loss_mask, doc_ids in batches:
-                step = micro_step // accum
-                if micro_step % accum == 0:
-                    if self._handle_interrupt(step, self.checkpointer) or step >= self.config.train_num_steps:
-                        break
-                    self.timer.start()
-                    self.optimizer.zero_grad()
-                last = (micro_step + 1) % accum == 0
-                self.device.set_grad_sync(last)
-                loss = self._compute_loss(inputs, targets, loss_mask, step, doc_ids)
-                self.device.backward(loss)
-                acc_loss = acc_loss + loss.detach()
-                micro_step += 1
-                if not last:
-                    continue
-                step = micro_step // accum
-                sched = self.scheduler.step(self.optimizer, step)
-                self._perform_optimization_step(micro_step, step, sched)
-                dev_t, wall_t = self.timer.stop()
-                acc_loss = float(acc_loss)
-                tokens = targets.numel() * self.process_info["dp_size"] * accum
-                metrics = self._calculate_step_metrics(acc_loss, wall_t, tokens, sched, t_train0, device_time=dev_t)
-                self.last_metrics = metrics
-                if step % self.config.eval_every_n_steps == 0 and step > 0:
-                    self._run_evaluation(self.bpb_evaluator, step, "val", save_checkpoint=True,
-                                         num_steps=self.config.eval_num_steps)
-                    self._log_sample_predictions(step)
-                if self.core_evaluator is not None and step % self.config.core_eval_every_n_step == 0 and step > 0:
-                    self._run_evaluation(self.core_evaluator, step, "core", task_labels=["hellaswag_zeroshot"], limit=1)
-                self._maybe_save_checkpoint(step, self.checkpointer)
-                self._log_training_progress(step, metrics)
-                self.profiler.step()
-                acc_loss = 0.0
-        self._finalize_training(micro_step // accum, self.checkpointer)
+            super().train()

@@ -1,13 +1,20 @@
-"""Run untrusted snippets with captured stdout/stderr and a SIGALRM time limit (mint/utils/exec.py:9-67)."""
+"""Run a code snippet in a separate Python process with captured output and a wall-clock limit.
+
+Used to grade generated programs (HumanEval). The reference runs the snippet with ``exec`` inside
+the trainer process under a SIGALRM alarm (mint/utils/exec.py:9-67), which only works on the main
+thread and lets the snippet touch the trainer's state. Here every snippet runs in its own
+interpreter (``python -I -c``: isolated mode, no user site, no environment-driven imports) in a
+new session, with stdin closed; on timeout the whole process group is killed, so a snippet that
+forks or loops forever cannot outlive its limit. The result type is the reference's.
+"""
 
 from __future__ import annotations
 
-import io
+import os
 import signal
+import subprocess
 import sys
-from collections.abc import Iterator
-from contextlib import contextmanager
-from typing import NamedTuple, Never
+from typing import NamedTuple
 
 
 class ExecutionResult(NamedTuple):
@@ -16,37 +23,27 @@ class ExecutionResult(NamedTuple):
     error: str = ""
 
 
-class TimeoutHandlerError(Exception):
-    pass
-
-
-def timeout_handler(signum, frame) -> Never:  # noqa: ANN001, ARG001
-    raise TimeoutHandlerError("Code execution timed out")
-
-
-@contextmanager
-def time_limit(seconds: int) -> Iterator[None]:
-    previous = signal.signal(signal.SIGALRM, timeout_handler)
-    signal.alarm(seconds)
+def execute_code(code: str, timeout: int | float = 5) -> ExecutionResult:
+    """Run ``code`` and report ``success`` when it exits 0 and wrote nothing to stderr."""
     try:
-        yield
-    finally:
-        signal.alarm(0)
-        signal.signal(signal.SIGALRM, previous)
-
-
-def execute_code(code: str, timeout: int = 5) -> ExecutionResult:
-    out, err = io.StringIO(), io.StringIO()
-    saved = sys.stdout, sys.stderr
+        proc = subprocess.Popen([sys.executable, "-I", "-c", code], stdin=subprocess.DEVNULL,
+                                stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True, start_new_session=True)
+    except OSError as exc:
+        return ExecutionResult(success=False, error=f"{type(exc).__name__}: {exc}")
     try:
-        sys.stdout, sys.stderr = out, err
-        with time_limit(timeout):
-            exec(code, {"__builtins__": __builtins__})  # noqa: S102
-        error = err.getvalue()
-        return ExecutionResult(success=not error, output=out.getvalue(), error=error)
-    except TimeoutHandlerError as exc:
-        return ExecutionResult(success=False, output=out.getvalue(), error=f"Timeout: {exc!s}")
-    except Exception as exc:  # noqa: BLE001
-        return ExecutionResult(success=False, output=out.getvalue(), error=f"{type(exc).__name__}: {exc!s}")
-    finally:
-        sys.stdout, sys.stderr = saved
+        out, err = proc.communicate(timeout=timeout)
+    except subprocess.TimeoutExpired:
+        _kill_group(proc)
+        out, err = proc.communicate()
+        return ExecutionResult(success=False, output=out or "", error=f"Timeout: code execution exceeded {timeout} s")
+    if proc.returncode != 0:
+        tail = err.strip().splitlines()[-1] if err.strip() else f"exit code {proc.returncode}"
+        return ExecutionResult(success=False, output=out, error=tail)
+    return ExecutionResult(success=not err, output=out, error=err)
+
+
+def _kill_group(proc: subprocess.Popen) -> None:
+    try:
+        os.killpg(proc.pid, signal.SIGKILL)  # the snippet's own process group only (new session)
+    except (ProcessLookupError, PermissionError):
+        proc.kill()
