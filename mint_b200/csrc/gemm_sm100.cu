@@ -12,6 +12,7 @@
 // The fp32 accumulator is double-buffered in tensor memory (2 x BN columns) so the epilogue of
 // tile t overlaps the MMAs of tile t+1. Every mbarrier wait is bounded (common.cuh); on a
 // timeout the kernel records a status code, drains its in-flight MMAs, frees TMEM and exits.
+#include <cstdio>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -973,6 +974,15 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
 void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const c10::optional<at::Tensor>& D_,
                bool a_kmajor, bool b_kmajor, double alpha, double beta, const c10::optional<at::Tensor>& alpha_t,
                bool accumulate) {
+  // MINT_TRACE_GEMM=1: one stderr line per stage of this host function (diagnosing host-side crashes)
+  static const bool trace = std::getenv("MINT_TRACE_GEMM") != nullptr;
+  if (trace) {
+    std::fprintf(stderr, "[gemm] enter A=%p %s B=%p %s C=%p %s dev=%d alpha_t=%d acc=%d\n", A_.data_ptr(),
+                 c10::str(A_.sizes()).c_str(), B_.data_ptr(), c10::str(B_.sizes()).c_str(), C_.data_ptr(),
+                 c10::str(C_.sizes()).c_str(), A_.is_cuda() ? A_.get_device() : -1,
+                 alpha_t.has_value() && alpha_t->defined() ? 1 : 0, accumulate ? 1 : 0);
+    std::fflush(stderr);
+  }
   check_cuda(A_, "A");
   check_cuda(B_, "B");
   check_cuda(C_, "C");
@@ -1108,6 +1118,12 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   const CUtensorMap tcm = make_tmap_3d(C.data_ptr(), f32c ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : BF, f32c ? 4 : 2, N, M,
                                        nb, C.stride(1), bstride(C), f32c ? 32 : 64, 32, 1, SW128);
   const bool a_mn = !a_kmajor, b_mn = !b_kmajor;
+  if (trace) {
+    std::fprintf(stderr, "[gemm] maps ok M=%lld N=%lld K=%lld pair=%d BN=%d splits=%d status=%p\n",
+                 static_cast<long long>(M), static_cast<long long>(N), static_cast<long long>(K), use_pair ? 1 : 0, BN,
+                 p.splits, static_cast<void*>(p.status));
+    std::fflush(stderr);
+  }
 #define MINT_GEMM_DISPATCH(BNV)                                                       \
   if (!a_mn && !b_mn) gemm::launch<BNV, false, false>(ta, tb, tcm, p, sms, stream);   \
   else if (!a_mn && b_mn) gemm::launch<BNV, false, true>(ta, tb, tcm, p, sms, stream); \
@@ -1127,6 +1143,10 @@ void gemm_bf16(const at::Tensor& A_, const at::Tensor& B_, at::Tensor& C_, const
   }
 #undef MINT_GEMM_DISPATCH
 #undef MINT_GEMM_DISPATCH_PAIR
+  if (trace) {
+    std::fprintf(stderr, "[gemm] launched\n");
+    std::fflush(stderr);
+  }
 }
 
 namespace {

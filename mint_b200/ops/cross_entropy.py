@@ -15,6 +15,8 @@ with three [tokens]-sized all-reduces.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 import torch.nn.functional as F  # noqa: N812
@@ -22,6 +24,14 @@ import torch.nn.functional as F  # noqa: N812
 from mint_b200.ops import _ext
 from mint_b200.ops.gemm import matmul
 from mint_b200.ops.linear import _cast_weight
+
+# MINT_CE_CACHED_WEIGHT=0: cast the LM-head weight to the compute dtype on every call instead of
+# using the cached copy that the optimizer refreshes once per step
+_CACHED_WEIGHT = os.environ.get("MINT_CE_CACHED_WEIGHT", "1") != "0"
+
+
+def _head_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    return _cast_weight((weight,), dtype) if _CACHED_WEIGHT else weight.to(dtype).contiguous()
 
 
 def masked_cross_entropy(
@@ -53,7 +63,7 @@ class _LMHeadCEFn(torch.autograd.Function):
         h2 = h.reshape(-1, d)
         if h2.dtype != dtype or not h2.is_contiguous():
             h2 = h2.to(dtype).contiguous()
-        w = _cast_weight((weight,), dtype)  # cached bf16 copy, refreshed once per optimizer step
+        w = _head_weight(weight, dtype)  # cached bf16 copy, refreshed once per optimizer step
         v_rows = w.shape[0]
         if v_rows % 8:
             # pad the (cast) table with zero rows so every logits row is 16-byte aligned; the
@@ -92,7 +102,7 @@ class _LMHeadCEFn(torch.autograd.Function):
         h2, dlogits = ctx.saved_tensors
         weight = ctx.weight
         g32 = g.reshape(1).float().contiguous()  # upstream scalar stays on the device
-        w = _cast_weight((weight,), ctx.dtype)
+        w = _head_weight(weight, ctx.dtype)
         if dlogits.shape[1] != w.shape[0]:
             w = torch.cat([w, w.new_zeros(dlogits.shape[1] - w.shape[0], w.shape[1])])
         dh = matmul(dlogits, w, alpha_tensor=g32, out_dtype=ctx.dtype).view(ctx.h_shape)
