@@ -200,11 +200,11 @@ class DistMuonAdamW(Optimizer):
             st = self._muon_stack_state(key, members, shape, units[0][1].device)
             tp_group, tp_dim = self._tp_of(members[0])
             pviews, gviews = [u[1] for u in units], [u[2] for u in units]
-            if tp_group is None and NorMuonStack.supported(pviews, gviews):
+            if NorMuonStack.supported(pviews, gviews):
                 dev = st.get("device_stack")
                 if dev is None:
                     n = len(units)
-                    dev = NorMuonStack(pviews, gviews, st["mb"], st["smb"].view(n, -1))
+                    dev = NorMuonStack(pviews, gviews, st["mb"], st["smb"].view(n, -1), tp_group=tp_group, tp_dim=tp_dim)
                     st["device_stack"] = dev
                 dev.bind(pviews, gviews)
                 dev.step(lr=group["lr"], momentum=group["momentum"],

@@ -250,21 +250,37 @@ class NorMuonStack:
     Frobenius norm) and ``normuon_apply`` (update with cautious weight decay). Same math as
     ``normuon_update_batched``; the pointer tables are rebuilt only when a view moves."""
 
-    def __init__(self, params: list[torch.Tensor], grads: list[torch.Tensor], mb: torch.Tensor, smb: torch.Tensor) -> None:
+    def __init__(self, params: list[torch.Tensor], grads: list[torch.Tensor], mb: torch.Tensor, smb: torch.Tensor,
+                 tp_group=None, tp_dim: int = 0) -> None:  # noqa: ANN001
+        """``params`` / ``grads``: this rank's matrices (tensor-parallel shards along ``tp_dim`` when
+        ``tp_group`` is given); ``smb``: ``[n, J]`` second moments of the FULL matrices."""
+        import torch.distributed as dist  # noqa: PLC0415
+
         self.n = len(params)
-        self.rows, self.cols = params[0].shape
+        self.shard_rows, self.shard_cols = params[0].shape
+        self.tp_group, self.tp_dim = tp_group, tp_dim
+        self.tp = dist.get_world_size(tp_group) if tp_group is not None else 1
+        self.tp_rank = dist.get_rank(tp_group) if tp_group is not None else 0
+        self.rows = self.shard_rows * (self.tp if tp_dim == 0 else 1)
+        self.cols = self.shard_cols * (self.tp if tp_dim == 1 else 1)
         dev = params[0].device
         self.key = None
         self.mb = mb
         self.smb = smb
         self.sumsq = torch.zeros(self.n, dtype=torch.float32, device=dev)
         self.x = torch.empty(self.n, self.rows, self.cols, dtype=torch.bfloat16, device=dev)
+        if self.tp > 1:  # this rank's normalized shards, all-gathered into x
+            self.x_local = torch.empty(self.n, self.shard_rows, self.shard_cols, dtype=torch.bfloat16, device=dev)
+            self.x_gather = torch.empty(self.tp * self.n * self.shard_rows * self.shard_cols, dtype=torch.bfloat16,
+                                        device=dev)
         j = self.rows if self.rows >= self.cols else self.cols
         self.scale = torch.empty(self.n, j, dtype=torch.float32, device=dev)
         self.bind(params, grads)
 
     @staticmethod
     def supported(params: list[torch.Tensor], grads: list[torch.Tensor]) -> bool:
+        """Device path: CUDA fp32 contiguous 16-byte-aligned matrices whose (shard) columns are a
+        multiple of 8 (16-byte bf16 rows for the Polar-Express GEMMs and the update kernel)."""
         if not params or not params[0].is_cuda or not _ext.kernels_enabled():
             return False
         rows, cols = params[0].shape
@@ -282,6 +298,7 @@ class NorMuonStack:
         dev = params[0].device
         self.pptrs = torch.tensor([p.data_ptr() for p in params], dtype=torch.int64, device=dev)
         self.gptrs = torch.tensor([g.data_ptr() for g in grads], dtype=torch.int64, device=dev)
+        self._keep = (list(params), list(grads))  # the kernels hold raw pointers: keep the memory alive
         self.key = key
 
     @torch.no_grad()
@@ -289,12 +306,34 @@ class NorMuonStack:
              grad_scale: torch.Tensor | None = None) -> None:
         C = _ext.require()
         rows, cols = self.rows, self.cols
-        C.normuon_prep(self.gptrs, self.mb, self.sumsq, rows * cols, float(momentum), grad_scale)
-        C.normuon_cast(self.gptrs, self.sumsq, self.x)
+        rs, cs = self.shard_rows, self.shard_cols
+        C.normuon_prep(self.gptrs, self.mb, self.sumsq, rs * cs, float(momentum), grad_scale)
+        if self.tp == 1:
+            C.normuon_cast(self.gptrs, self.sumsq, self.x)
+        else:
+            self._gather_full()
         x = polar_express_chain_bf16(self.x, ns_steps)
         tall = rows >= cols
         partial = C.normuon_stats(x, tall)
         red = cols if tall else rows
         C.normuon_scale(partial, self.smb, self.scale, red, float(beta2))
         lr = lr * max(1.0, rows / cols) ** 0.5
-        C.normuon_apply(x, self.scale, self.pptrs, 0, 0, rows, cols, tall, float(lr), float(wd))
+        r0 = self.tp_rank * rs if self.tp_dim == 0 and self.tp > 1 else 0
+        c0 = self.tp_rank * cs if self.tp_dim == 1 and self.tp > 1 else 0
+        C.normuon_apply(x, self.scale, self.pptrs, r0, c0, rs, cs, tall, float(lr), float(wd))
+
+    def _gather_full(self) -> None:
+        """Tensor parallelism: the Frobenius norms are summed over the TP group, every rank
+        normalizes its shards to bf16 and the shards are all-gathered into the full matrices (every
+        rank then orthogonalizes the whole stack, so each can update its own slice)."""
+        import torch.distributed as dist  # noqa: PLC0415
+
+        C = _ext.require()
+        dist.all_reduce(self.sumsq, group=self.tp_group)
+        C.normuon_cast(self.gptrs, self.sumsq, self.x_local)
+        dist.all_gather_into_tensor(self.x_gather, self.x_local.view(-1), group=self.tp_group)
+        parts = self.x_gather.view(self.tp, self.n, self.shard_rows, self.shard_cols)
+        if self.tp_dim == 0:
+            self.x.view(self.n, self.tp, self.shard_rows, self.shard_cols).copy_(parts.transpose(0, 1))
+        else:
+            self.x.view(self.n, self.shard_rows, self.tp, self.shard_cols).copy_(parts.permute(1, 2, 0, 3))

@@ -75,6 +75,33 @@ def main() -> None:
     torch.cuda.synchronize()
     _ext.check_device_status()
 
+    # NorMuon on tensor-parallel shards (norms all-reduced, bf16 shards all-gathered, each rank
+    # updating its slice) against the same update of the whole matrices on one rank
+    from mint_b200.optim.functional import NorMuonStack
+
+    for tp_dim, shape in ((0, (512, 256)), (1, (256, 512))):
+        torch.manual_seed(5)
+        full_p = [torch.randn(shape, device=dev) * 0.02 for _ in range(3)]
+        full_g = [torch.randn(shape, device=dev) * 1e-3 for _ in range(3)]
+        rows, cols = shape
+        J = rows if rows >= cols else cols
+        ref_p = [t.clone() for t in full_p]
+        ref = NorMuonStack(ref_p, [t.clone() for t in full_g], torch.zeros(3, rows, cols, device=dev),
+                           torch.zeros(3, J, device=dev))
+        ref.step(lr=0.02, momentum=0.95, beta2=0.9, wd=0.1, ns_steps=5)
+        sh_p = [t.chunk(world, dim=tp_dim)[rank].contiguous() for t in full_p]
+        sh_g = [t.chunk(world, dim=tp_dim)[rank].contiguous() for t in full_g]
+        st = NorMuonStack(sh_p, sh_g, torch.zeros(3, *sh_p[0].shape, device=dev), torch.zeros(3, J, device=dev),
+                          tp_group=dist.group.WORLD, tp_dim=tp_dim)
+        st.step(lr=0.02, momentum=0.95, beta2=0.9, wd=0.1, ns_steps=5)
+        torch.cuda.synchronize()
+        worst = max(rel(got - full_p[i].chunk(world, dim=tp_dim)[rank],
+                        ref_p[i].chunk(world, dim=tp_dim)[rank] - full_p[i].chunk(world, dim=tp_dim)[rank])
+                    for i, got in enumerate(sh_p))
+        ok = worst < 1e-2
+        failures += not ok
+        print(f"[rank {rank}] NorMuon tp_dim={tp_dim}: update rel err {worst:.2e} {'OK' if ok else 'FAIL'}", flush=True)
+
     # model-level: fused vs NCCL path on the same weights and batch
     from mint_b200.models.gemma import GemmaConfig
     from mint_b200.scripts.common import build_model
