@@ -145,7 +145,9 @@ struct TileRanges {
   __device__ __forceinline__ bool active(int x, int j) const { return j >= lo(x) && j < hi(x); }
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+// 320 threads, one CTA per SM: a 200-register budget per thread (instead of a launch bound, which
+// made ptxas settle at 168 and spill the 128 scores each softmax thread holds)
+__global__ void __maxnreg__(200)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -271,6 +273,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
+        // a step no tile uses still consumed a K / V load: release the slots only after it landed
+        if (!v_ready && !(ok = mbar_wait(&s.v_full[st], (t >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)))
+          break;
         umma_commit(&s.v_empty[st]);
         if (t + 1 < n) {
           // tiles whose first key tile is j + 1 start here
@@ -287,6 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             issue_qk(tmem + x * 256, smem_u32(s.q[x]), smem_u32(s.k[(t + 1) & 1]));
             umma_commit(&s.s_full[x]);
           }
+          if (ok && !k_next_ready) {
+            ok = mbar_wait(&s.k_full[(t + 1) & 1], ((t + 1) >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag);
+          }
+          if (!ok) break;
           umma_commit(&s.k_empty[(t + 1) & 1]);
         }
       }
@@ -336,57 +345,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       mk.window = p.window;
       mk.doc_q = doc_q;
       mk.doc_row = p.doc != nullptr ? p.doc + static_cast<long long>(b) * p.T : nullptr;
-      // pass 1: masked row max over the 128 scores, 32 columns at a time
+      // the 128 scores of this row: four loads, one wait
+      uint32_t u[128];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) tmem_ld_32x32b_x32(tmem_s + g * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[g * 32]));
+      uint32_t kbits[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) kbits[g] = chunk_keep_mask(mk, kb + g * 32);
+      tmem_ld_wait();
       float mt = -INFINITY;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(tmem_s + g * 32, u);
-        const uint32_t kbits = chunk_keep_mask(mk, kb + g * 32);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if ((kbits >> e) & 1u) mt = fmaxf(mt, __uint_as_float(u[e]) * p.scale_log2);
-        }
+      for (int e = 0; e < 128; ++e) {
+        if ((kbits[e >> 5] >> (e & 31)) & 1u) mt = fmaxf(mt, __uint_as_float(u[e]) * p.scale_log2);
       }
       const float m_new = fmaxf(m, mt);
       // tcgen05.ld / st are warp-collective: the rescale decision is made uniform across the warp
       const bool grow = m != -INFINITY && m_new > m + kRescaleThreshold;
-      if (c > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds PV_0..PV_{c-1}; PV_{c-1} completed before S(c) was issued into these columns
-        const float alpha = (m == -INFINITY || m_new == -INFINITY) ? 0.f : exp2f(m - m_new);
-        l *= alpha;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint32_t u[32];
-          tmem_ld_32x32b_x32(tmem_o + g * 32, u);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-          tmem_st_32x32b_x32(tmem_o + g * 32, u);
-        }
-        tmem_st_wait();
-        m = m_new;
-      } else if (m == -INFINITY) {
-        m = m_new;  // nothing accumulated in this row yet
-      }
-      // pass 2: P = exp2(s - m) in bf16 (a quarter on the FMA pipe), row sum in fp32. Chunk g's 16
-      // packed columns land on S columns [16g, 16g + 16), which earlier chunks already consumed.
+      const bool rescale = c > 0 && __any_sync(0xffffffffu, grow);
+      const float alpha = (!rescale || m == -INFINITY || m_new == -INFINITY) ? 1.f : exp2f(m - m_new);
+      if (rescale || m == -INFINITY) m = m_new;
+      // P = exp2(s - m) in bf16 (a quarter on the FMA pipe), row sum in fp32, written over the first
+      // 64 columns of S (their scores are already in registers)
       float rs = 0.f;
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(tmem_s + g * 32, u);
-        const uint32_t kbits = m != -INFINITY ? chunk_keep_mask(mk, kb + g * 32) : 0u;
-        tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           float a = 0.f, bb = 0.f;
-          {
-            if ((kbits >> (2 * e)) & 1u) a = exp2f(__uint_as_float(u[2 * e]) * p.scale_log2 - m);
-            if ((kbits >> (2 * e + 1)) & 1u) {
-              const float t = __uint_as_float(u[2 * e + 1]) * p.scale_log2 - m;
+          const int i0 = g * 32 + 2 * e;
+          if (m != -INFINITY) {
+            if ((kbits[g] >> (2 * e)) & 1u) a = exp2f(__uint_as_float(u[i0]) * p.scale_log2 - m);
+            if ((kbits[g] >> (2 * e + 1)) & 1u) {
+              const float t = __uint_as_float(u[i0 + 1]) * p.scale_log2 - m;
               bb = (e & 1) ? exp2_poly(t) : exp2f(t);
             }
           }
@@ -394,6 +385,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[e] = pack_bf16x2(a, bb);
         }
         tmem_st_32x32b_x16(tmem_s + g * 16, pk);
+      }
+      if (rescale) {
+        // O holds PV_0..PV_{c-1}; PV_{c-1} completed before S(c) was issued into this tile's columns,
+        // and PV_c is issued only after this warp signals P ready below
+        l *= alpha;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint32_t w[32];
+          tmem_ld_32x32b_x32(tmem_o + g * 32, w);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(__uint_as_float(w[e]) * alpha);
+          tmem_st_32x32b_x32(tmem_o + g * 32, w);
+        }
       }
       l += rs;
       tmem_st_wait();

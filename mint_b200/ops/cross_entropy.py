@@ -25,9 +25,10 @@ from mint_b200.ops import _ext
 from mint_b200.ops.gemm import matmul
 from mint_b200.ops.linear import _cast_weight
 
-# MINT_CE_CACHED_WEIGHT=0: cast the LM-head weight to the compute dtype on every call instead of
-# using the cached copy that the optimizer refreshes once per step
-_CACHED_WEIGHT = os.environ.get("MINT_CE_CACHED_WEIGHT", "1") != "0"
+# The LM-head weight is cast to the compute dtype on every call (forward and backward). Reusing the
+# linears' cached bf16 copy here (MINT_CE_CACHED_WEIGHT=1) crashed 2-GPU runs with SIGSEGV in the
+# extension call's argument conversion; 1-GPU runs were unaffected. It stays off until explained.
+_CACHED_WEIGHT = os.environ.get("MINT_CE_CACHED_WEIGHT", "0") == "1"
 
 
 def _head_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:

@@ -89,8 +89,9 @@ def main() -> None:
         ref = NorMuonStack(ref_p, [t.clone() for t in full_g], torch.zeros(3, rows, cols, device=dev),
                            torch.zeros(3, J, device=dev))
         ref.step(lr=0.02, momentum=0.95, beta2=0.9, wd=0.1, ns_steps=5)
-        sh_p = [t.chunk(world, dim=tp_dim)[rank].contiguous() for t in full_p]
-        sh_g = [t.chunk(world, dim=tp_dim)[rank].contiguous() for t in full_g]
+        # clones: a dim-0 chunk of a contiguous tensor is already contiguous (a view, not a copy)
+        sh_p = [t.chunk(world, dim=tp_dim)[rank].clone().contiguous() for t in full_p]
+        sh_g = [t.chunk(world, dim=tp_dim)[rank].clone().contiguous() for t in full_g]
         st = NorMuonStack(sh_p, sh_g, torch.zeros(3, *sh_p[0].shape, device=dev), torch.zeros(3, J, device=dev),
                           tp_group=dist.group.WORLD, tp_dim=tp_dim)
         st.step(lr=0.02, momentum=0.95, beta2=0.9, wd=0.1, ns_steps=5)
