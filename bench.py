@@ -309,6 +309,7 @@ def main() -> None:
 
         ext = _ext.require()
         _ext.check_device_status()
+        _ext.reset_fallbacks()
     launches0 = ext.launch_count() if ext is not None else 0
     sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
                            if os.environ.get("CUDA_VISIBLE_DEVICES") else local)
@@ -325,6 +326,11 @@ def main() -> None:
     torch.cuda.synchronize()
     clocks = sampler.stop()
     launches = (ext.launch_count() - launches0) if ext is not None else 0
+    fallbacks = None
+    if ext is not None:
+        from mint_b200.ops import _ext
+
+        fallbacks = sum(_ext.fallback_counts().values())  # PyTorch-fallback calls in the timed steps
     ms = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms)
     last_loss = float(loss.detach())
@@ -397,6 +403,8 @@ def main() -> None:
             "frac_of_measured_bf16_sustained": tflops_per_gpu / pk.get("bf16_tflops_sustained", 1400.0),
             "clocks": clocks, "gpu_launches": launches, "final_loss": last_loss,
         })
+        if fallbacks is not None:
+            line["kernel_fallbacks"] = fallbacks
         if e2e is not None:
             line["e2e"] = e2e
         if same_opt is not None:

@@ -18,6 +18,18 @@ def compute_logps(logits: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
     return (logp * mask).sum(dim=-1)
 
 
+def sequence_logps(model: nn.Module, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+    """``compute_logps(model(input_ids), labels)`` without the [B, T, V] fp32 log-softmax: models
+    with ``token_logps`` (Gemma) give the per-position log-prob of the next label directly."""
+    if not hasattr(model, "token_logps"):
+        return compute_logps(model(input_ids), labels)
+    nxt = torch.full_like(labels, -100)
+    nxt[:, :-1] = labels[:, 1:]
+    mask = nxt != -100
+    logp = model.token_logps(input_ids, nxt.masked_fill(~mask, 0))
+    return (logp * mask).sum(dim=-1)
+
+
 class DPOLoss(nn.Module):
     def __init__(self, beta: float = 0.1) -> None:
         super().__init__()

@@ -26,7 +26,7 @@ from mint_b200.kvcache.base import KVCache
 from mint_b200.nn.base import ModelConfig, compute_dtype
 from mint_b200.nn.blocks import GQAGluBlock
 from mint_b200.nn.norm import RMSNorm
-from mint_b200.ops.cross_entropy import lm_head_cross_entropy
+from mint_b200.ops.cross_entropy import lm_head_cross_entropy, lm_head_token_logps
 from mint_b200.ops.embedding import embedding
 from mint_b200.ops.linear import linear
 from mint_b200.parallel import fused as fused_tp
@@ -220,6 +220,24 @@ class Gemma(nn.Module):
         group = tp.group if tpc.active(tp) else None
         return lm_head_cross_entropy(
             hn, self.output.weight, targets, loss_mask, self.config.vocab_size,
+            vocab_start=self.vocab_start, group=group, compute_dtype=compute_dtype(hn),
+        )
+
+    def token_logps(
+        self,
+        input_ids: torch.Tensor,
+        targets: torch.Tensor,
+        doc_ids: torch.Tensor | None = None,
+        attn_mask: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        """fp32 ``log p(targets[b, t] | input_ids[b, :t+1])`` for every position, without
+        materializing fp32 logits or a log-softmax (fused LM head + row statistics on CUDA).
+        ``targets`` must hold valid token ids; positions to ignore are masked by the caller."""
+        hn = self._trunk(input_ids, None, 0, doc_ids, attn_mask)
+        tp = self.tp
+        group = tp.group if tpc.active(tp) else None
+        return lm_head_token_logps(
+            hn, self.output.weight, targets, self.config.vocab_size,
             vocab_start=self.vocab_start, group=group, compute_dtype=compute_dtype(hn),
         )
 

@@ -29,6 +29,15 @@ class LogitsWrapper(nn.Module):
     def generate(self, *args: Any, **kwargs: Any) -> torch.Tensor:  # noqa: ANN401
         return self._model.generate(*args, **kwargs)
 
+    def __getattr__(self, name: str) -> Any:  # noqa: ANN401
+        # ``token_logps`` (fused DPO log-probs) and other model methods pass through
+        try:
+            return super().__getattr__(name)
+        except AttributeError:
+            if name == "_model":
+                raise
+            return getattr(self._modules["_model"] if "_model" in self._modules else self.__dict__["_model"], name)
+
 
 def compute_dtype(t: torch.Tensor) -> torch.dtype:
     """The dtype GEMMs should run in: the autocast dtype when autocast is on, else ``t.dtype``."""

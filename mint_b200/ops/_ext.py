@@ -48,6 +48,32 @@ def kernels_enabled() -> bool:
     return os.environ.get("MINT_DISABLE_KERNELS", "0") != "1"
 
 
+_FALLBACKS: dict[tuple[str, str], int] = {}
+
+
+def fallback(op: str, reason: str) -> None:
+    """Record that a call of ``op`` on CUDA tensors ran its PyTorch implementation instead of a
+    kernel (an operand the kernel cannot take). The first occurrence of each (op, reason) warns;
+    with ``MINT_STRICT_KERNELS=1`` every occurrence raises, so a hot path cannot silently move onto
+    PyTorch / cuBLAS. ``fallback_counts()`` reports them (``bench.py`` prints the total)."""
+    key = (op, reason)
+    _FALLBACKS[key] = _FALLBACKS.get(key, 0) + 1
+    if os.environ.get("MINT_STRICT_KERNELS", "0") == "1":
+        raise RuntimeError(f"mint_b200: {op} has no kernel path for this call ({reason}); MINT_STRICT_KERNELS=1")
+    if _FALLBACKS[key] == 1:
+        import warnings  # noqa: PLC0415
+
+        warnings.warn(f"mint_b200: {op} ran its PyTorch fallback on CUDA ({reason})", RuntimeWarning, stacklevel=3)
+
+
+def fallback_counts() -> dict[str, int]:
+    return {f"{op}: {reason}": n for (op, reason), n in _FALLBACKS.items()}
+
+
+def reset_fallbacks() -> None:
+    _FALLBACKS.clear()
+
+
 def use_cuda_kernels(t) -> bool:  # noqa: ANN001
     """True when ``t`` lives on a GPU: then the extension is mandatory."""
     if not t.is_cuda:

@@ -146,6 +146,13 @@ def attention(
         d, bounds = _doc_inputs(doc_ids)
         return _FlashAttnFn.apply(q.contiguous(), k.contiguous(), v.contiguous(), causal, window_left, d, scale,
                                   bounds)
+    if q.is_cuda and _ext.kernels_enabled():
+        if attn_mask is not None or bias is not None:
+            _ext.fallback("attention", "explicit mask or bias")
+        elif q.shape[1] != k.shape[1]:
+            _ext.fallback("attention", "query and key lengths differ (decode)")
+        else:
+            _ext.fallback("attention", "dtype / head_dim / head grouping without a kernel")
     return attention_reference(
         q, k, v, causal=causal, window_left=window_left, doc_ids=doc_ids, attn_mask=attn_mask,
         bias=bias, scale=scale,

@@ -137,6 +137,123 @@ def lm_head_cross_entropy(
     return vocab_parallel_cross_entropy(logits, targets, loss_mask, vocab_size, vocab_start, group)
 
 
+class _LMHeadLogpFn(torch.autograd.Function):
+    """Per-token ``log p(target)`` of ``h @ E^T`` (the DPO sequence log-probs).
+
+    Forward: the LM-head GEMM writes bf16 logits, one row-statistics kernel gives max / sum-exp /
+    target logit per row (combined across the TP group for a vocab shard), ``logp = tl - lse``.
+    No fp32 or log-softmax copy of the [tokens, vocab] logits is made. Backward: the same in-place
+    gradient kernel as the CE loss rewrites the saved logits into ``(softmax - onehot) * (-g_t)``
+    with the per-token upstream gradient ``g_t`` as the row weight, then the two GEMMs give
+    ``dh`` and ``dE``. The saved logits are consumed, so the graph supports one backward."""
+
+    @staticmethod
+    def forward(ctx, h, weight, targets, vocab_size, vocab_start, group, dtype):  # noqa: ANN001, ANN205
+        C = _ext.require()
+        d = h.shape[-1]
+        h2 = h.reshape(-1, d)
+        if h2.dtype != dtype or not h2.is_contiguous():
+            h2 = h2.to(dtype).contiguous()
+        w = _head_weight(weight, dtype)
+        v_rows = w.shape[0]
+        if v_rows % 8:
+            w = torch.cat([w, w.new_zeros(8 - v_rows % 8, w.shape[1])])
+        logits = matmul(h2, w, trans_b=True, out_dtype=dtype)
+        t = targets.reshape(-1).to(torch.int64).contiguous()
+        local_valid = max(0, min(weight.shape[0], vocab_size - vocab_start))
+        mx, se, tl = C.ce_row_stats(logits, t, local_valid, vocab_start)
+        if _tp_size(group) > 1:
+            gmx = mx.clone()
+            dist.all_reduce(gmx, op=dist.ReduceOp.MAX, group=group)
+            se = se * torch.exp(mx - gmx)
+            dist.all_reduce(se, op=dist.ReduceOp.SUM, group=group)
+            dist.all_reduce(tl, op=dist.ReduceOp.SUM, group=group)
+            mx = gmx
+        lse = mx + torch.log(se)
+        ctx.save_for_backward(h2, logits, t, lse)
+        ctx.weight, ctx.v_rows, ctx.local_valid, ctx.vocab_start = weight, v_rows, local_valid, vocab_start
+        ctx.h_shape, ctx.h_dtype, ctx.dtype = h.shape, h.dtype, dtype
+        return (tl - lse).view(targets.shape)
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        C = _ext.require()
+        h2, logits, t, lse = ctx.saved_tensors
+        rows = (-g.reshape(-1)).float().contiguous()
+        one = torch.ones(1, dtype=torch.float32, device=logits.device)
+        C.ce_grad_inplace(logits, t, rows, lse, one, ctx.local_valid, ctx.vocab_start)
+        w = _head_weight(ctx.weight, ctx.dtype)
+        if logits.shape[1] != w.shape[0]:
+            w = torch.cat([w, w.new_zeros(logits.shape[1] - w.shape[0], w.shape[1])])
+        dh = matmul(logits, w, out_dtype=ctx.dtype).view(ctx.h_shape)
+        if dh.dtype != ctx.h_dtype:
+            dh = dh.to(ctx.h_dtype)
+        dw = None
+        if ctx.needs_input_grad[1]:
+            gdtype = ctx.weight.dtype if ctx.weight.dtype in (torch.float32, torch.bfloat16) else torch.float32
+            dw = matmul(logits, h2, trans_a=True, out_dtype=gdtype)[: ctx.v_rows]
+        return dh, dw, None, None, None, None, None
+
+
+class _VocabParallelLogp(torch.autograd.Function):
+    """``log p(target)`` per token over a vocab shard, exact across the TP group (PyTorch ops)."""
+
+    @staticmethod
+    def forward(ctx, logits, targets, vocab_size, vocab_start, group):  # noqa: ANN001, ANN205
+        lf = logits.float()
+        v_local = lf.shape[-1]
+        cols = vocab_start + torch.arange(v_local, device=lf.device)
+        lf = lf.masked_fill(cols >= vocab_size, float("-inf"))
+        gmx = lf.max(dim=-1).values
+        dist.all_reduce(gmx, op=dist.ReduceOp.MAX, group=group)
+        ex = torch.exp(lf - gmx.unsqueeze(-1))
+        se = ex.sum(-1)
+        dist.all_reduce(se, op=dist.ReduceOp.SUM, group=group)
+        local_t = targets - vocab_start
+        in_shard = (local_t >= 0) & (local_t < v_local)
+        tl = torch.where(in_shard, lf.gather(-1, local_t.clamp(0, v_local - 1).unsqueeze(-1)).squeeze(-1),
+                         torch.zeros_like(gmx))
+        dist.all_reduce(tl, op=dist.ReduceOp.SUM, group=group)
+        ctx.save_for_backward(ex, se, local_t, in_shard)
+        ctx.ldtype = logits.dtype
+        return tl - (gmx + torch.log(se))
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        ex, se, local_t, in_shard = ctx.saved_tensors
+        p = ex / se.unsqueeze(-1)
+        onehot = torch.zeros_like(p)
+        onehot.scatter_(-1, local_t.clamp(0, p.shape[-1] - 1).unsqueeze(-1), in_shard.unsqueeze(-1).to(p.dtype))
+        return ((onehot - p) * g.unsqueeze(-1)).to(ctx.ldtype), None, None, None, None
+
+
+def lm_head_token_logps(
+    h: torch.Tensor,
+    weight: torch.Tensor,
+    targets: torch.Tensor,
+    vocab_size: int,
+    *,
+    vocab_start: int = 0,
+    group=None,  # noqa: ANN001
+    compute_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """fp32 ``log softmax(h @ weight^T)[target]`` per token, shaped like ``targets`` (ids must be
+    valid vocabulary indices: mask ignored positions after the call). ``weight`` may be a vocab
+    shard; the result is the full-vocabulary log-prob on every TP rank."""
+    dtype = compute_dtype or h.dtype
+    if _ext.use_cuda_kernels(h):
+        return _LMHeadLogpFn.apply(h, weight, targets, vocab_size, vocab_start, group, dtype)
+    logits = F.linear(h.to(dtype), weight.to(dtype))
+    v = logits.shape[-1]
+    if _tp_size(group) == 1:
+        lf = logits.float()
+        if v > vocab_size:
+            lf = lf.masked_fill(torch.arange(v, device=lf.device) >= vocab_size, float("-inf"))
+        return torch.log_softmax(lf, dim=-1).gather(-1, targets.unsqueeze(-1)).squeeze(-1)
+    out = _VocabParallelLogp.apply(logits.reshape(-1, v), targets.reshape(-1), vocab_size, vocab_start, group)
+    return out.view(targets.shape)
+
+
 class _VocabParallelCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logits, targets, mask, vocab_size, vocab_start, group):  # noqa: ANN001, ANN205

@@ -39,6 +39,8 @@ def embedding(
 ) -> torch.Tensor:
     if _ext.use_cuda_kernels(weight) and weight.dtype == torch.float32:
         return _EmbeddingFn.apply(ids, weight, vocab_start)
+    if weight.is_cuda and _ext.kernels_enabled():
+        _ext.fallback("embedding", f"{weight.dtype} weight (the kernel takes fp32)")
     if not vocab_parallel:
         return F.embedding(ids, weight)
     local = ids - vocab_start

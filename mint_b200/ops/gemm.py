@@ -87,6 +87,7 @@ def matmul(
             C.gemm(a, b, out, d, not trans_a, trans_b, float(alpha), float(beta), alpha_tensor, accumulate)
             return out
         # operands whose rows are not 16-byte multiples cannot be described to TMA
+        _ext.fallback("matmul", "operand not TMA-describable (dtype, strides or alignment)")
         res = _ref(a, b, trans_a, trans_b, alpha, beta, d, torch.float32)
         if alpha_tensor is not None:
             res = res * alpha_tensor.float()

@@ -57,6 +57,8 @@ def rmsnorm(
     out_dtype = out_dtype or x.dtype
     if shift is None and _ext.use_cuda_kernels(x):
         return _RMSNormFn.apply(x, scale, eps, out_dtype)
+    if x.is_cuda and _ext.kernels_enabled():
+        _ext.fallback("rmsnorm", "shift (AdaRMSNorm) term")
     return _rms_ref(x, scale, eps, shift).to(out_dtype)
 
 
@@ -109,6 +111,8 @@ def add_rmsnorm(
     y_dtype = y_dtype or a.dtype
     if _ext.use_cuda_kernels(res) and res.dtype == torch.float32:
         return _AddRMSNormFn.apply(res, a, post_scale, pre_scale, eps, y_dtype)
+    if res.is_cuda and _ext.kernels_enabled():
+        _ext.fallback("add_rmsnorm", f"{res.dtype} residual (the kernel takes fp32)")
     n = _rms_ref(a, post_scale, eps, None).to(a.dtype)
     h = res + n
     y = None if pre_scale is None else _rms_ref(h, pre_scale, eps, None).to(y_dtype)

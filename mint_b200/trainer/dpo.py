@@ -15,7 +15,7 @@ from torch import nn
 from torch.optim import Optimizer
 
 from mint_b200.eval.dist.chatcore import ChatCoreEvaluator
-from mint_b200.loss.dpo import DPOLoss, compute_logps
+from mint_b200.loss.dpo import DPOLoss, sequence_logps
 from mint_b200.nn.base import LogitsWrapper
 from mint_b200.trainer.base import BasetrainConfig, BaseTrainer, Evaluation
 from mint_b200.utils.device import Device
@@ -47,8 +47,8 @@ class DPOTrainer(BaseTrainer):
 
     def pair_logps(self, model: nn.Module, ids: torch.Tensor, chosen: torch.Tensor,
                    rejected: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        logits_c, logits_r = model(ids).chunk(2, dim=0)
-        return compute_logps(logits_c, chosen), compute_logps(logits_r, rejected)
+        logps = sequence_logps(model, ids, torch.cat([chosen, rejected], dim=0))
+        return logps.chunk(2, dim=0)
 
     def micro_loss(self, batch: Any, step: int) -> tuple[torch.Tensor, int]:  # noqa: ANN401, ARG002
         ids = torch.cat([batch.chosen_input_ids, batch.rejected_input_ids], dim=0)

@@ -107,6 +107,24 @@ def test_gemm_column_slice_operand():
     assert ((out - exp).norm() / exp.norm()).item() < 2e-3
 
 
+def test_gemm_unaligned_operand_is_a_counted_fallback(monkeypatch):
+    """Rows of 14 bytes cannot be described to TMA: the call still returns the right product, but
+    it is counted and warned about, and raises under MINT_STRICT_KERNELS=1."""
+    from mint_b200.ops import _ext
+
+    _ext.reset_fallbacks()
+    a = torch.randn(64, 7, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(7, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.warns(RuntimeWarning, match="matmul ran its PyTorch fallback"):
+        c = matmul(a, b)
+    torch.testing.assert_close(c.float(), ref(a, b, False, False), rtol=2e-2, atol=2e-2)
+    assert sum(_ext.fallback_counts().values()) == 1
+    monkeypatch.setenv("MINT_STRICT_KERNELS", "1")
+    with pytest.raises(RuntimeError, match="no kernel path"):
+        matmul(a, b)
+    _ext.reset_fallbacks()
+
+
 @pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True)])
 @pytest.mark.parametrize("shape", [(5, 192, 320, 256), (3, 768, 768, 3072), (24, 128, 96, 64)])
 def test_gemm_batched(ta, tb, shape):

@@ -7,7 +7,7 @@ import torch
 import torch.nn.functional as F
 
 from mint_b200.ops import add_rmsnorm, embedding, geglu, qk_norm_rope, rmsnorm, rope_cos_sin
-from mint_b200.ops.cross_entropy import lm_head_cross_entropy, masked_cross_entropy
+from mint_b200.ops.cross_entropy import lm_head_cross_entropy, lm_head_token_logps, masked_cross_entropy
 
 pytestmark = pytest.mark.gpu
 
@@ -140,6 +140,30 @@ def test_lm_head_ce(V, valid):
     l2 = masked_cross_entropy(logits, t, m, valid if V > valid else None)
     (l2 * 0.7).backward()
     assert abs(loss.item() - l2.item()) < 2e-2 * max(1, abs(l2.item()))
+    assert ((h.grad - h2.grad).norm() / h2.grad.norm()) < 3e-2
+    assert ((w.grad - w2.grad).norm() / w2.grad.norm()) < 3e-2
+
+
+@pytest.mark.parametrize("V,valid", [(65536, 65536), (50304, 50267)])
+def test_lm_head_token_logps(V, valid):
+    """Fused DPO log-probs (LM-head GEMM + row statistics, in-place gradient with per-token weights)
+    against fp32 log_softmax + gather, values and both input gradients."""
+    torch.manual_seed(7)
+    B, T, D = 2, 256, 256
+    h = (torch.randn(B, T, D, device="cuda") * 0.5).requires_grad_()
+    w = (torch.randn(V, D, device="cuda") * 0.1).requires_grad_()
+    t = torch.randint(0, valid, (B, T), device="cuda")
+    g = torch.randn(B, T, device="cuda")
+    lp = lm_head_token_logps(h, w, t, valid, compute_dtype=torch.bfloat16)
+    (lp * g).sum().backward()
+    h2, w2 = h.detach().clone().requires_grad_(), w.detach().clone().requires_grad_()
+    logits = h2.bfloat16().float() @ w2.bfloat16().float().t()
+    if V > valid:
+        logits = logits.masked_fill(torch.arange(V, device="cuda") >= valid, float("-inf"))
+    lp2 = torch.log_softmax(logits, dim=-1).gather(-1, t.unsqueeze(-1)).squeeze(-1)
+    (lp2 * g).sum().backward()
+    assert lp.shape == (B, T) and lp.dtype == torch.float32
+    assert (lp - lp2).abs().max().item() < 5e-2
     assert ((h.grad - h2.grad).norm() / h2.grad.norm()) < 3e-2
     assert ((w.grad - w2.grad).norm() / w2.grad.norm()) < 3e-2
 
