@@ -245,6 +245,9 @@ def main() -> None:
     ap.add_argument("--model", choices=list(MODELS), default="d12")
     ap.add_argument("--micro-batch", type=int, default=0, help="override micro-batch per dp rank")
     ap.add_argument("--matrix-optimizer", choices=["muon", "adamw"], default="muon")
+    ap.add_argument("--tp", type=int, default=0, help="override the layout's tensor-parallel size")
+    ap.add_argument("--ddp-level", type=int, default=-1, help="override the layout's ZeRO level (0..3)")
+    ap.add_argument("--sp", choices=["on", "off"], default=None, help="override sequence parallelism")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-same-optimizer", action="store_true",
                     help="skip the extra all-AdamW measurement (the reference arm's optimizer)")
@@ -259,6 +262,14 @@ def main() -> None:
     if args.micro_batch:
         cfg["micro_batch"] = args.micro_batch
     lay = layout_for(args.gpus, args.model)
+    if args.tp:
+        lay["tp"] = args.tp
+    if args.ddp_level >= 0:
+        lay["ddp_level"] = args.ddp_level
+    if args.sp is not None:
+        lay["sp"] = args.sp == "on"
+    if lay["tp"] == 1:
+        lay["sp"] = False
     dp = args.gpus // lay["tp"]
     mb, T, V = cfg["micro_batch"], cfg["seq_length"], cfg["vocab_size"]
     par_name = parallelism_name(args.gpus, lay)

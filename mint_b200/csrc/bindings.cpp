@@ -42,7 +42,11 @@ void normuon_cast(const at::Tensor& gptrs, const at::Tensor& sumsq, at::Tensor& 
 at::Tensor normuon_stats(const at::Tensor& X, bool tall);
 void normuon_scale(const at::Tensor& partial, at::Tensor& v2, at::Tensor& scale, int64_t red, double beta2);
 void normuon_apply(const at::Tensor& X, const at::Tensor& scale, const at::Tensor& pptrs, int64_t r0, int64_t c0,
-                   int64_t rs, int64_t cs, bool tall, double lr, double wd);
+                   int64_t rs, int64_t cs, bool tall, double lr, double wd, const c10::optional<at::Tensor>& peer_ptrs,
+                   int64_t rank, int64_t world);
+void zero_adamw_push(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
+                     double b2, double eps, double wd, int64_t step, const c10::optional<at::Tensor>& gscale,
+                     const std::vector<int64_t>& bucket_ptrs, int64_t rank, int64_t world);
 void sumsq_multi(const at::Tensor& ptrs, const at::Tensor& sizes, at::Tensor& out, int64_t max_len);
 void clip_coef(const at::Tensor& sumsq, double max_norm, at::Tensor& coef, at::Tensor& norm);
 void cast_multi(const at::Tensor& src, const at::Tensor& dst, const at::Tensor& sizes, int64_t max_len);
@@ -146,7 +150,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("normuon_cast", &mint::normuon_cast, "NorMuon Frobenius normalization to the bf16 Polar-Express input");
   m.def("normuon_stats", &mint::normuon_stats, "row (tall) or column sums of squares of the orthogonalized stack");
   m.def("normuon_scale", &mint::normuon_scale, "NorMuon second moment update and per-row/column step scale");
-  m.def("normuon_apply", &mint::normuon_apply, "NorMuon update with cautious weight decay through a pointer table");
+  m.def("normuon_apply", &mint::normuon_apply,
+        "NorMuon update with cautious weight decay through a pointer table; with peer_ptrs the new values are "
+        "also stored into every data-parallel peer's copy (ZeRO-2 all-gather fused)",
+        py::arg("X"), py::arg("scale"), py::arg("pptrs"), py::arg("r0"), py::arg("c0"), py::arg("rs"), py::arg("cs"),
+        py::arg("tall"), py::arg("lr"), py::arg("wd"), py::arg("peer_ptrs") = py::none(), py::arg("rank") = 0,
+        py::arg("world") = 1);
+  m.def("zero_adamw_push", &mint::zero_adamw_push,
+        "ZeRO-2 sharded AdamW with the parameter all-gather fused in (peer stores of the new values)");
   m.def("sumsq_multi", &mint::sumsq_multi, "sum of squares over a table of fp32 segments (accumulated)");
   m.def("clip_coef", &mint::clip_coef, "gradient-norm clip coefficient on the device");
   m.def("cast_multi", &mint::cast_multi, "fp32 -> bf16 copies of a table of segments in one launch");

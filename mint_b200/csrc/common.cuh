@@ -6,6 +6,7 @@
 // * bounded mbarrier waits (%globaltimer based), TMA (cp.async.bulk.tensor) loads, tcgen05
 //   (UMMA) descriptors, MMA issue / commit and TMEM alloc / load, written as inline PTX.
 #pragma once
+#include <cmath>
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -51,6 +52,27 @@ __device__ __forceinline__ uint64_t wait_limit_ns(const uint32_t* status) {
 // cannot corrupt the model before the host reads the word and raises.
 __device__ __forceinline__ bool status_failed(const uint32_t* status) {
   return status != nullptr && *reinterpret_cast<const volatile uint32_t*>(status) != 0u;
+}
+
+// AdamW constants of one step: bias corrections folded into `step` = lr / (1 - b1^t) and
+// `inv_bc2` = 1 / (1 - b2^t); `decay` = 1 - lr * wd (decoupled weight decay).
+struct AdamWStep {
+  float b1, b2, eps, step, decay, inv_bc2;
+};
+
+inline AdamWStep adamw_step_consts(double lr, double b1, double b2, double eps, double wd, long long t) {
+  const double bc1 = 1.0 - std::pow(b1, static_cast<double>(t));
+  const double bc2 = 1.0 - std::pow(b2, static_cast<double>(t));
+  return AdamWStep{static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps),
+                   static_cast<float>(lr / bc1), static_cast<float>(1.0 - lr * wd), static_cast<float>(1.0 / bc2)};
+}
+
+// One element: m <- lerp(m, g, 1 - b1); v <- lerp(v, g^2, 1 - b2); returns the new parameter
+// p * decay - step * m / (sqrt(v * inv_bc2) + eps).
+__device__ __forceinline__ float adamw_elem(float p, float g, float& m, float& v, const AdamWStep& a) {
+  m = m + (1.f - a.b1) * (g - m);
+  v = v + (1.f - a.b2) * (g * g - v);
+  return p * a.decay - a.step * m / (sqrtf(v * a.inv_bc2) + a.eps);
 }
 
 __device__ __forceinline__ void record_status(uint32_t* status, uint32_t code) {

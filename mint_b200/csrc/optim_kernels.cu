@@ -168,10 +168,17 @@ __global__ void normuon_scale_kernel(const float* __restrict__ partial, float* _
 // or the whole matrix), row-major with row stride cs. grid (chunks, n); 8 columns per thread step.
 __global__ void normuon_apply_kernel(const __nv_bfloat16* __restrict__ X, const float* __restrict__ scale,
                                      const long long* __restrict__ pptrs, int R, int C, int r0, int c0, int rs, int cs,
-                                     bool tall, float lr, float wd, const uint32_t* __restrict__ status) {
+                                     bool tall, float lr, float wd, const long long* __restrict__ peer_ptrs,
+                                     int rank, int world, const uint32_t* __restrict__ status) {
   if (status_failed(status)) return;
   const int i = blockIdx.y;
   float* p = reinterpret_cast<float*>(pptrs[i]);
+  // ZeRO-2 owner-computes: the owner's new values also go straight into every data-parallel peer's
+  // copy of the matrix (peer_ptrs[i * world + q]), fusing the parameter all-gather into the update
+  float* peer[8] = {};
+  if (peer_ptrs != nullptr) {
+    for (int q = 0; q < world; ++q) peer[q] = q == rank ? nullptr : reinterpret_cast<float*>(peer_ptrs[i * world + q]);
+  }
   const __nv_bfloat16* Xi = X + static_cast<long long>(i) * R * C;
   const float* sc = scale + static_cast<long long>(i) * (tall ? R : C);
   const int cs8 = cs >> 3;
@@ -197,6 +204,15 @@ __global__ void normuon_apply_kernel(const __nv_bfloat16* __restrict__ X, const 
     }
     pp[0] = pa;
     pp[1] = pb;
+    if (peer_ptrs != nullptr) {
+      const long long o = static_cast<long long>(r) * cs + c;
+      for (int q = 0; q < world; ++q) {
+        if (peer[q] == nullptr) continue;
+        float4* d = reinterpret_cast<float4*>(peer[q] + o);
+        d[0] = pa;
+        d[1] = pb;
+      }
+    }
   }
 }
 
@@ -358,13 +374,19 @@ void normuon_scale(const at::Tensor& partial, at::Tensor& v2, at::Tensor& scale,
 }
 
 void normuon_apply(const at::Tensor& X, const at::Tensor& scale, const at::Tensor& pptrs, int64_t r0, int64_t c0,
-                   int64_t rs, int64_t cs, bool tall, double lr, double wd) {
+                   int64_t rs, int64_t cs, bool tall, double lr, double wd, const c10::optional<at::Tensor>& peer_ptrs,
+                   int64_t rank, int64_t world) {
   check_contig(X, "X");
   check_contig(scale, "scale");
   const int n = static_cast<int>(X.size(0)), R = static_cast<int>(X.size(1)), C = static_cast<int>(X.size(2));
   check_ptr_table(pptrs, n, "pptrs");
   MINT_CHECK(cs % 8 == 0 && c0 % 8 == 0, "shard columns must be multiples of 8");
   MINT_CHECK(r0 + rs <= R && c0 + cs <= C, "shard outside the matrix");
+  const bool push = peer_ptrs.has_value() && peer_ptrs->defined();
+  if (push) {
+    MINT_CHECK(world >= 2 && world <= 8 && rank >= 0 && rank < world, "normuon_apply: push needs 2..8 ranks");
+    check_ptr_table(*peer_ptrs, static_cast<int64_t>(n) * world, "peer_ptrs");
+  }
   if (n == 0 || rs == 0) return;
   c10::cuda::CUDAGuard g(X.device());
   const int dev = X.get_device();
@@ -373,7 +395,8 @@ void normuon_apply(const at::Tensor& X, const at::Tensor& scale, const at::Tenso
       reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), scale.data_ptr<float>(),
       reinterpret_cast<const long long*>(pptrs.data_ptr<int64_t>()), R, C, static_cast<int>(r0), static_cast<int>(c0),
       static_cast<int>(rs), static_cast<int>(cs), tall, static_cast<float>(lr), static_cast<float>(wd),
-      status_ptr(dev));
+      push ? reinterpret_cast<const long long*>(peer_ptrs->data_ptr<int64_t>()) : nullptr, static_cast<int>(rank),
+      static_cast<int>(world), status_ptr(dev));
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -335,19 +335,14 @@ __global__ void __launch_bounds__(512, 3) ce_grad_kernel(__nv_bfloat16* __restri
   row_write_grad(logits + static_cast<long long>(r) * V, V, valid, lse[r], targets[r] - vstart, mask[r] / *denom);
 }
 
-// p <- p (1 - lr wd); m <- lerp(m, g, 1 - b1); v <- lerp(v, g^2, 1 - b2);
-// p <- p - (lr / bc1) * m / (sqrt(v / bc2) + eps)
+// AdamW over a flat fp32 shard (adamw_elem, common.cuh).
 // Skipped entirely (parameters and moments unchanged) once any kernel recorded an error status.
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
-                             float* __restrict__ v, long long n, float lr, float b1, float b2, float eps, float wd,
-                             float bc1, float bc2, const float* __restrict__ gscale,
+                             float* __restrict__ v, long long n, AdamWStep a, const float* __restrict__ gscale,
                              const uint32_t* __restrict__ status) {
   if (status_failed(status)) return;
   // gradient-clipping coefficient computed on the device (1 when the caller passes none)
   const float gs = gscale != nullptr ? *gscale : 1.f;
-  const float step = lr / bc1;
-  const float decay = 1.f - lr * wd;
-  const float inv_bc2 = 1.f / bc2;
   const long long n4 = n / 4;
   float4* p4 = reinterpret_cast<float4*>(p);
   const float4* g4 = reinterpret_cast<const float4*>(g);
@@ -356,30 +351,20 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float4 pp = p4[i], gg = g4[i], mm = m4[i], vv = v4[i];
-    gg.x *= gs;
-    gg.y *= gs;
-    gg.z *= gs;
-    gg.w *= gs;
-    float* pa = &pp.x;
-    const float* ga = &gg.x;
-    float* ma = &mm.x;
-    float* va = &vv.x;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      ma[e] = ma[e] + (1.f - b1) * (ga[e] - ma[e]);
-      va[e] = va[e] + (1.f - b2) * (ga[e] * ga[e] - va[e]);
-      pa[e] = pa[e] * decay - step * ma[e] / (sqrtf(va[e] * inv_bc2) + eps);
-    }
+    pp.x = adamw_elem(pp.x, gg.x * gs, mm.x, vv.x, a);
+    pp.y = adamw_elem(pp.y, gg.y * gs, mm.y, vv.y, a);
+    pp.z = adamw_elem(pp.z, gg.z * gs, mm.z, vv.z, a);
+    pp.w = adamw_elem(pp.w, gg.w * gs, mm.w, vv.w, a);
     p4[i] = pp;
     m4[i] = mm;
     v4[i] = vv;
   }
   for (long long i = n4 * 4 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const float gi = g[i] * gs;
-    m[i] = m[i] + (1.f - b1) * (gi - m[i]);
-    v[i] = v[i] + (1.f - b2) * (gi * gi - v[i]);
-    p[i] = p[i] * decay - step * m[i] / (sqrtf(v[i] * inv_bc2) + eps);
+    float mi = m[i], vi = v[i];
+    p[i] = adamw_elem(p[i], g[i] * gs, mi, vi, a);
+    m[i] = mi;
+    v[i] = vi;
   }
 }
 
@@ -542,14 +527,11 @@ void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v
   const long long n = p.numel();
   MINT_CHECK(g.numel() == n && m.numel() == n && v.numel() == n, "adamw size mismatch");
   if (n == 0) return;
-  const double bc1 = 1.0 - std::pow(b1, static_cast<double>(step));
-  const double bc2 = 1.0 - std::pow(b2, static_cast<double>(step));
   c10::cuda::CUDAGuard gd(p.device());
   adamw_kernel<<<ew_grid((n + 3) / 4, p.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), n, static_cast<float>(lr),
-      static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
-      static_cast<float>(bc1), static_cast<float>(bc2),
-      gscale.has_value() ? gscale->data_ptr<float>() : nullptr, status_ptr(p.get_device()));
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), n,
+      adamw_step_consts(lr, b1, b2, eps, wd, step), gscale.has_value() ? gscale->data_ptr<float>() : nullptr,
+      status_ptr(p.get_device()));
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -5,6 +5,8 @@
 //   global gradient norm for clipping then needs one scalar all-reduce instead of a pass over the
 //   shards). The kernel announces that its own bucket is final, waits for every peer's
 //   announcement and pulls the peers' slices of its shard with 16-byte loads.
+// zero_adamw_push: the sharded AdamW update with the all-gather fused in (new values stored to
+//   every peer's copy as they are computed).
 // zero_all_gather: pushes this rank's (updated) shard of a flat parameter bucket into every
 //   peer's copy of the bucket; zero_barrier (one block, after the pushes of all buckets) announces
 //   it and waits until every peer's shards have landed in this rank's copies.
@@ -99,6 +101,37 @@ __global__ void __launch_bounds__(256) zero_push_kernel(Peers pe, const float* _
   }
 }
 
+// Sharded AdamW fused with the parameter all-gather: each element of this rank's shard is updated
+// once (p, m, v in local memory) and the new value is stored straight into every peer's copy of
+// the bucket, so no separate push pass re-reads the shard. Gated on the status word like every
+// update kernel: after a timed-out collective neither the local nor the peers' copies change.
+__global__ void __launch_bounds__(256) zero_adamw_push_kernel(Peers pe, float* __restrict__ p,
+                                                              const float* __restrict__ g, float* __restrict__ m,
+                                                              float* __restrict__ v, long long off, long long n,
+                                                              AdamWStep a, const float* __restrict__ gscale, int rank,
+                                                              int world, const uint32_t* __restrict__ status) {
+  if (status_failed(status)) return;
+  const float gs = gscale != nullptr ? *gscale : 1.f;
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 pp = reinterpret_cast<float4*>(p)[i];
+    const float4 gg = reinterpret_cast<const float4*>(g)[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    pp.x = adamw_elem(pp.x, gg.x * gs, mm.x, vv.x, a);
+    pp.y = adamw_elem(pp.y, gg.y * gs, mm.y, vv.y, a);
+    pp.z = adamw_elem(pp.z, gg.z * gs, mm.z, vv.z, a);
+    pp.w = adamw_elem(pp.w, gg.w * gs, mm.w, vv.w, a);
+    reinterpret_cast<float4*>(p)[i] = pp;
+    reinterpret_cast<float4*>(m)[i] = mm;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    for (int q = 0; q < world; ++q) {
+      if (q != rank) reinterpret_cast<float4*>(pe.dst[q] + off)[i] = pp;
+    }
+  }
+}
+
 // One block: the push kernel before it (stream order) has completed, so announce, then wait until
 // every peer announced that its shard landed in this rank's bucket.
 __global__ void zero_signal_kernel(Peers pe, const int* flag_local, int rank, int world, int seq, uint32_t* status) {
@@ -163,6 +196,35 @@ void zero_all_gather(const at::Tensor& shard, const std::vector<int64_t>& bucket
   const long long n = shard.numel();
   zc::zero_push_kernel<<<grid_for(n / 4, dev), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       pe, shard.data_ptr<float>(), rank * n, n, static_cast<int>(rank), static_cast<int>(world));
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+// AdamW on this rank's shard of a symmetric fp32 bucket (p = bucket_ptrs[rank] + rank * n) with the
+// updated values pushed into every peer's bucket at the same offset; zero_barrier publishes them.
+void zero_adamw_push(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
+                     double b2, double eps, double wd, int64_t step, const c10::optional<at::Tensor>& gscale,
+                     const std::vector<int64_t>& bucket_ptrs, int64_t rank, int64_t world) {
+  const at::Tensor* all[4] = {&p, &g, &m, &v};
+  for (const at::Tensor* t : all) {
+    check_contig(*t, "adamw tensor");
+    MINT_CHECK(t->scalar_type() == at::kFloat, "zero_adamw_push tensors must be fp32");
+    MINT_CHECK(reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0, "zero_adamw_push tensors must be 16-byte aligned");
+  }
+  const long long n = p.numel();
+  MINT_CHECK(n % 4 == 0 && g.numel() == n && m.numel() == n && v.numel() == n, "zero_adamw_push size mismatch");
+  MINT_CHECK(static_cast<int64_t>(bucket_ptrs.size()) == world, "one bucket pointer per rank");
+  MINT_CHECK(reinterpret_cast<int64_t>(p.data_ptr()) == bucket_ptrs[rank] + rank * n * 4,
+             "p must be this rank's shard of its own symmetric bucket");
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(p.device());
+  const int dev = p.get_device();
+  std::vector<int64_t> no_flags(world, 0);
+  zc::Peers pe = make_peers({}, bucket_ptrs, no_flags, world);
+  zc::zero_adamw_push_kernel<<<grid_for(n / 4, dev), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      pe, p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), rank * n, n,
+      adamw_step_consts(lr, b1, b2, eps, wd, step), gscale.has_value() ? gscale->data_ptr<float>() : nullptr,
+      static_cast<int>(rank), static_cast<int>(world), status_ptr(dev));
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

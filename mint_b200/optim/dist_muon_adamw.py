@@ -114,8 +114,18 @@ class DistMuonAdamW(Optimizer):
                     continue
                 st = self._ensure_bucket_state(b)
                 st["step"] += 1
-                adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
-                             group["eps"], group["weight_decay"], grad_scale=self._grad_scale())
+                if eng.push_fusable(b):
+                    # ZeRO-2: one kernel updates the shard and stores it into every peer's bucket
+                    from mint_b200.ops import _ext  # noqa: PLC0415
+
+                    _ext.require().zero_adamw_push(pv, gv, st["exp_avg"], st["exp_avg_sq"], float(group["lr"]),
+                                                   float(beta1), float(beta2), float(group["eps"]),
+                                                   float(group["weight_decay"]), int(st["step"]), self._grad_scale(),
+                                                   b.extra["symm_data"].ptrs, eng.rank, eng.dp)
+                    eng.mark_pushed(b)
+                else:
+                    adamw_update(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], beta1, beta2,
+                                 group["eps"], group["weight_decay"], grad_scale=self._grad_scale())
                 for sub in st["views"]:
                     sub["step"] = st["step"]
         for p in group["params"]:
@@ -207,9 +217,14 @@ class DistMuonAdamW(Optimizer):
                     dev = NorMuonStack(pviews, gviews, st["mb"], st["smb"].view(n, -1), tp_group=tp_group, tp_dim=tp_dim)
                     st["device_stack"] = dev
                 dev.bind(pviews, gviews)
+                push = self._push_table(st, members, pviews)
                 dev.step(lr=group["lr"], momentum=group["momentum"],
                          beta2=group["beta2"] if group.get("beta2") is not None else 0.0,
-                         wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5), grad_scale=self._grad_scale())
+                         wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5), grad_scale=self._grad_scale(),
+                         peer_ptrs=push, rank=self._engine.rank if push is not None else 0,
+                         world=self._engine.dp if push is not None else 1)
+                if push is not None:
+                    self._engine.mark_pushed(params=members)
                 continue
             grads = torch.stack([u[2].float() for u in units])
             gs = self._grad_scale()
@@ -221,6 +236,24 @@ class DistMuonAdamW(Optimizer):
                 beta2=group["beta2"] if group.get("beta2") is not None else 0.0,
                 wd=group["weight_decay"], ns_steps=group.get("ns_steps", 5), tp_group=tp_group, tp_dim=tp_dim,
             )
+
+    def _push_table(self, st: dict, members: list[torch.Tensor], pviews: list[torch.Tensor]) -> torch.Tensor | None:
+        """[n * dp] peer addresses of the owned matrices when their buckets live in symmetric peer
+        memory (ZeRO-2): ``normuon_apply`` then stores the new values into every peer's copy."""
+        eng = self._engine
+        if eng is None:
+            return None
+        buckets = [eng.slot(p)[0] for p in members]
+        if not all(eng.push_fusable(b) for b in buckets):
+            return None
+        key = tuple(v.data_ptr() for v in pviews)
+        cached = st.get("push_table")
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        rows = [eng.peer_pointers(b, v) for b, v in zip(buckets, pviews, strict=True)]
+        table = torch.tensor([a for row in rows for a in row], dtype=torch.int64, device=pviews[0].device)
+        st["push_table"] = (key, table)
+        return table
 
     def _tp_of(self, p: torch.Tensor):  # noqa: ANN202
         """(TP group, split dim) for a tensor-parallel sharded parameter, else (None, 0)."""

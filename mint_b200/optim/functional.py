@@ -303,7 +303,10 @@ class NorMuonStack:
 
     @torch.no_grad()
     def step(self, *, lr: float, momentum: float, beta2: float, wd: float, ns_steps: int,
-             grad_scale: torch.Tensor | None = None) -> None:
+             grad_scale: torch.Tensor | None = None, peer_ptrs: torch.Tensor | None = None, rank: int = 0,
+             world: int = 1) -> None:
+        """``peer_ptrs`` ([n * world] addresses of every data-parallel rank's copy of each matrix):
+        the update kernel also stores the new values there (ZeRO-2 all-gather fused)."""
         C = _ext.require()
         rows, cols = self.rows, self.cols
         rs, cs = self.shard_rows, self.shard_cols
@@ -320,7 +323,7 @@ class NorMuonStack:
         lr = lr * max(1.0, rows / cols) ** 0.5
         r0 = self.tp_rank * rs if self.tp_dim == 0 and self.tp > 1 else 0
         c0 = self.tp_rank * cs if self.tp_dim == 1 and self.tp > 1 else 0
-        C.normuon_apply(x, self.scale, self.pptrs, r0, c0, rs, cs, tall, float(lr), float(wd))
+        C.normuon_apply(x, self.scale, self.pptrs, r0, c0, rs, cs, tall, float(lr), float(wd), peer_ptrs, rank, world)
 
     def _gather_full(self) -> None:
         """Tensor parallelism: the Frobenius norms are summed over the TP group, every rank

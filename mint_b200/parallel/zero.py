@@ -125,6 +125,9 @@ class GradEngine:
         self.grad_scale: torch.Tensor | None = None
         self._norm_tables: dict[tuple, tuple[torch.Tensor, torch.Tensor, int]] = {}
         self._in_backward: set[str] = set()
+        self._pushed_buckets: set[int] = set()  # buckets / params whose update kernel already pushed them
+        self._pushed_params: set[int] = set()
+        self.fused_update_pushes = 0  # update kernels that stored their results into the peers' copies
         # ZeRO-2 on CUDA: gradient reduce-scatter and parameter all-gather as NVLink peer-memory kernels
         # (csrc/zero_comm.cu) over symmetric bucket buffers instead of NCCL; MINT_FUSED_ZERO=0 disables
         self.fused = self._fused_possible(model)
@@ -256,9 +259,11 @@ class GradEngine:
         return self._zc["seq"]
 
     def _fused_reduce_scatter(self, b: Bucket) -> torch.Tensor:
-        """This rank's shard of sum over ranks of the bucket's gradient, / dp, on the comm stream."""
+        """This rank's shard of sum over ranks of the bucket's gradient, / dp, on the comm stream,
+        written straight into ``grad_shard`` (zero before: at ZeRO-2 the reduce-scatter runs once per
+        optimizer step, on the last micro-batch)."""
         zc = self._zc
-        out = torch.empty_like(b.grad_shard)
+        out = b.grad_shard
         stream = zc["stream"]
         stream.wait_stream(torch.cuda.current_stream())  # every gradient of the bucket has landed
         with torch.cuda.stream(stream):
@@ -269,6 +274,31 @@ class GradEngine:
 
     def _fused_all_gather(self, b: Bucket) -> None:
         _ext_mod().zero_all_gather(b.shard_data, b.extra["symm_data"].ptrs, self.rank, self.dp)
+
+    def push_fusable(self, b: Bucket) -> bool:
+        """True when an update kernel may store bucket ``b``'s new values straight into the peers'
+        copies (ZeRO-2 over symmetric peer memory), so ``after_step`` needs no push for it."""
+        return self.level == 2 and self.distributed and "symm_data" in b.extra
+
+    def peer_pointers(self, b: Bucket, view: torch.Tensor) -> list[int]:
+        """Every rank's address of ``view`` (a piece of bucket ``b``'s parameters on this rank)."""
+        off = view.data_ptr() - b.data.data_ptr()
+        return [int(base) + off for base in b.extra["symm_data"].ptrs]
+
+    def mark_pushed(self, b: Bucket | None = None, params: list[torch.Tensor] = ()) -> None:
+        """An update kernel already pushed bucket ``b`` (this rank's whole shard) or ``params``."""
+        if b is not None:
+            self._pushed_buckets.add(b.index)
+        self._pushed_params.update(id(p) for p in params)
+        self.fused_update_pushes += 1
+
+    def _needs_push(self, b: Bucket) -> bool:
+        if b.index in self._pushed_buckets:
+            return False
+        if b.kind == "owner":
+            owned = [s for s in b.slots if s.owner == self.rank]
+            return not owned or not all(id(s.param) in self._pushed_params for s in owned)
+        return True
 
     # ------------------------------------------------------------------ grads
     def _install_grad_views(self, b: Bucket) -> None:
@@ -341,8 +371,7 @@ class GradEngine:
             return
         if isinstance(b.handle, tuple) and b.handle[0] == "fused":
             zc = self._zc
-            torch.cuda.current_stream().wait_stream(zc["stream"])
-            b.grad_shard.add_(b.handle[1])  # already scaled by 1/dp in the kernel
+            torch.cuda.current_stream().wait_stream(zc["stream"])  # the kernel wrote grad_shard, scaled
         elif isinstance(b.handle, tuple):
             h, out = b.handle
             h.wait()
@@ -435,7 +464,8 @@ class GradEngine:
         pushed = False
         for b in self.buckets:
             if "symm_data" in b.extra:
-                self._fused_all_gather(b)
+                if self._needs_push(b):
+                    self._fused_all_gather(b)
                 pushed = True
                 continue
             src = b.shard_data.clone()
@@ -447,6 +477,8 @@ class GradEngine:
             # reads this rank's gradient buckets, so the next zero_grad and forward may proceed
             zc = self._zc
             _ext_mod().zero_barrier(zc["ctrl"].ptrs, zc["flags"], self.rank, self.dp, self._next_seq())
+        self._pushed_buckets.clear()
+        self._pushed_params.clear()
 
     # ------------------------------------------------------------------ grad norm
     def _reduced_grad(self, b: Bucket) -> torch.Tensor | None:

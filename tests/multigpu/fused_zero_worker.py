@@ -5,7 +5,9 @@ Checks the ZeRO peer-memory collectives (csrc/zero_comm.cu) against NCCL:
      calls in a row (flags are sequence numbers, never reset);
   2. all-gather (push of every rank's shard + one barrier) into a symmetric bucket;
   3. ZeRO-2 training (dp = world, NorMuon + AdamW, global-norm clipping) for three steps: the
-     consolidated parameters with the fused transport against the NCCL transport.
+     consolidated parameters with the fused transport (reduce-scatter straight into the gradient
+     shard; AdamW / NorMuon update kernels that store the new values into every peer's copy)
+     against the NCCL transport, and every rank's full parameter buckets identical.
 Prints one line per check and exits non-zero on a mismatch.
 """
 
@@ -61,6 +63,14 @@ def train(fused: str, dev: torch.device) -> dict[str, torch.Tensor]:
         eng.clip_grad_norm(0.5)
         opt.step()
     torch.cuda.synchronize()
+    if fused == "1":
+        # the sharded updates stored their results into the peers' copies (AdamW buckets and the
+        # owners' NorMuon matrices): every rank's full bucket must equal rank 0's
+        assert eng.fused_update_pushes > 0, "no update kernel pushed its results"
+        for b in eng.buckets:
+            ref0 = b.data.clone()
+            dist.broadcast(ref0, 0)
+            assert torch.equal(ref0, b.data), f"bucket {b.index} differs from rank 0 after the fused push"
     return {k: v.detach().float().cpu() for k, v in consolidated_state_dict(model).items()}
 
 
