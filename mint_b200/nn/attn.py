@@ -92,11 +92,12 @@ class GroupedQueryAttention(nn.Module):
         doc_ids: torch.Tensor | None = None,
     ) -> torch.Tensor:
         dt = compute_dtype(x)
-        # sequence-parallel TP on CUDA: all-gather -> QKV GEMM and wo GEMM -> reduce-scatter as fused kernels
+        # TP on CUDA: QKV GEMM with its all-gather (SP) or backward all-reduce (no SP), wo GEMM with its
+        # reduce-scatter (SP) or all-reduce (no SP), each as fused kernels
         fuse = (kv_cache is None and self._fusable() and type(self.wo) is nn.Linear and dt == torch.bfloat16
                 and fused_tp.enabled(self.tp, x))
         if fuse:
-            bsz, seqlen = x.shape[0], x.shape[1] * self.tp.size
+            bsz, seqlen = x.shape[0], x.shape[1] * (self.tp.size if self.tp.sp else 1)
             qkv = fused_tp.column_parallel_linear(x, (self.wq.weight, self.wk.weight, self.wv.weight), self.tp)
             q, k, v, bias = self._norm_rope(qkv, start_pos)
         else:

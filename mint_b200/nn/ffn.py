@@ -29,7 +29,8 @@ class GLU(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = compute_dtype(x)
         if self._fusable() and dt == torch.bfloat16 and fused_tp.enabled(self.tp, x):
-            # all-gather -> fc1||fc2 GEMM and fc3 GEMM -> reduce-scatter as fused kernels
+            # fc1||fc2 GEMM with its all-gather (SP) / backward all-reduce (no SP), fc3 GEMM with its
+            # reduce-scatter (SP) / all-reduce (no SP), as fused kernels
             ab = fused_tp.column_parallel_linear(x, (self.fc1.weight, self.fc2.weight), self.tp)
             return fused_tp.row_parallel_linear(geglu(ab), self.fc3.weight, self.tp)
         x = tpc.enter_column_parallel(x, self.tp)

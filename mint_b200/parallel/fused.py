@@ -14,6 +14,12 @@ reduce-scatters after every row-parallel one with separate NCCL calls (mint/util
   backward -- all-gather of the output gradient -> GEMM for the input gradient, local GEMM for the
   weight gradient on the gathered output gradient.
 
+Without sequence parallelism (replicated activations) the row-parallel exit is an all-reduce:
+the GEMM -> reduce-scatter kernel writes each rank's reduced block of rows into its part of a
+symmetric buffer, one push kernel stores the block into every peer's buffer and a stream barrier
+over NVLink flags publishes it (the reference: ``_AllReduce`` at mint/utils/parallel.py:322-333).
+The column-parallel entry is then the identity and its backward the same fused all-reduce.
+
 Sequence-parallel activations are ``[B, T / tp, d]`` (a shard of every sequence); the gathered
 layout is ``[B, T, d]`` (rows of rank p's shard of sequence b at rows ``b*T + p*T/tp ...``).
 Gradients are those of the NCCL path in ``mint_b200.parallel.tp``; only the transport differs.
@@ -40,6 +46,7 @@ import torch
 import torch.distributed as dist
 
 from mint_b200.ops import _ext
+from mint_b200.ops.gemm import matmul
 from mint_b200.ops.linear import _cast_weight, weight_grads
 
 
@@ -90,6 +97,11 @@ class TPComm:
         self._last_use: list[int] = []  # sequence number of the fused call that last let peers read a slot
         self._ring: list[_Symm | None] = [None, None]
         self._ring_idx = 0
+        # all-reduce (no SP): output ring and the barrier's flags (bytes 128.. of the control block)
+        self._ar: list[_Symm | None] = [None, None]
+        self._ar_idx = 0
+        self.bar_flags = self.ctrl.view((self.world,), torch.int32, offset=128)
+        self.bar_ptrs = [p + 128 for p in self.ctrl.ptrs]
 
     # -------------------------------------------------------------- buffers
     def acquire(self, nbytes: int) -> tuple[int, _Symm]:
@@ -148,7 +160,8 @@ class TPComm:
                   self.rank, self.world, seg, self.next_seq())
         return out
 
-    def gemm_rs(self, A: torch.Tensor, w: torch.Tensor, b_kmajor: bool, seg: int) -> torch.Tensor:
+    def gemm_rs(self, A: torch.Tensor, w: torch.Tensor, b_kmajor: bool, seg: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's rows of ``sum over ranks (A @ op(w))`` (reduce-scatter fused into the GEMM)."""
         C = _ext.require()
         rows = A.shape[0]
@@ -164,10 +177,35 @@ class TPComm:
         push = [recv.ptrs[p] + self.rank * slot_bytes for p in range(self.world)]
         flag_ptrs = [self.ctrl.ptrs[p] + 256 + self.rank * self.MAX_FLAG_BLOCKS * 4 for p in range(self.world)]
         flags = self.rs_flags.view(self.world, self.MAX_FLAG_BLOCKS)
-        out = torch.empty(mc, n, dtype=torch.bfloat16, device=A.device)
+        if out is None:
+            out = torch.empty(mc, n, dtype=torch.bfloat16, device=A.device)
         C.gemm_rs(A, w, out, b_kmajor, push, recv_t, flag_ptrs, flags, self.arrive, self.arrive_ptrs,
                   self.rank, self.world, seg, self.next_seq())
         return out
+
+    def gemm_ar(self, A: torch.Tensor, w: torch.Tensor, b_kmajor: bool) -> torch.Tensor:
+        """``sum over ranks (A @ op(w))`` on every rank (tensor parallelism without SP).
+
+        The fused GEMM -> reduce-scatter kernel writes this rank's reduced rows (a contiguous
+        ``rows / world`` block) straight into its part of a symmetric buffer; one push kernel stores
+        that block into every peer's buffer at the same offset, and a stream barrier over NVLink flags
+        publishes the pushes. The result is copied out of the (two-deep) ring of buffers."""
+        C = _ext.require()
+        rows = A.shape[0]
+        n = w.shape[0] if b_kmajor else w.shape[1]
+        seg = rows // self.world
+        i = self._ar_idx
+        self._ar_idx ^= 1
+        full = self._ar[i]
+        if full is None or full.nbytes < rows * n * 2:
+            full = _Symm(rows * n * 2, self.group, self.device)
+            self._ar[i] = full
+        fullv = full.view((rows, n), torch.bfloat16)
+        mine = fullv[self.rank * seg : (self.rank + 1) * seg]
+        self.gemm_rs(A, w, b_kmajor, seg, out=mine)
+        C.zero_all_gather(mine.view(torch.float32).view(-1), full.ptrs, self.rank, self.world)
+        C.zero_barrier(self.bar_ptrs, self.bar_flags, self.rank, self.world, self.next_seq())
+        return fullv.clone()
 
 
 _COMMS: dict[Any, TPComm] = {}
@@ -269,24 +307,85 @@ class _RowParallelFn(torch.autograd.Function):
         return (dx, None, *grads)
 
 
+class _ColumnParallelARFn(torch.autograd.Function):
+    """No SP: ``y = x @ cat(weights)^T`` on the replicated input (a local GEMM); the backward's
+    ``dx = all_reduce(dy @ W)`` runs as the fused GEMM -> reduce-scatter + push all-gather."""
+
+    @staticmethod
+    def forward(ctx, x, comm, *weights):  # noqa: ANN001, ANN205
+        x2 = _bf16_2d(x)
+        w = _cast_weight(weights, torch.bfloat16)
+        y = matmul(x2, w, trans_b=True, out_dtype=torch.bfloat16)
+        ctx.comm, ctx.weights, ctx.x_shape, ctx.x_dtype = comm, weights, x.shape, x.dtype
+        ctx.save_for_backward(x2)
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        (x2,) = ctx.saved_tensors
+        dy2 = _bf16_2d(dy)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            w = _cast_weight(ctx.weights, torch.bfloat16)
+            dx = ctx.comm.gemm_ar(dy2, w, False).view(ctx.x_shape).to(ctx.x_dtype)
+        want = [ctx.needs_input_grad[2 + i] for i in range(len(ctx.weights))]
+        return (dx, None, *weight_grads(ctx.weights, want, dy2, x2))
+
+
+class _RowParallelARFn(torch.autograd.Function):
+    """No SP: ``y = all_reduce(x @ w^T)`` as one fused GEMM -> reduce-scatter plus a push
+    all-gather; the backward needs no collective (``dx = dy @ w`` on the replicated ``dy``)."""
+
+    @staticmethod
+    def forward(ctx, x, comm, w):  # noqa: ANN001, ANN205
+        x2 = _bf16_2d(x)
+        wc = _cast_weight((w,), torch.bfloat16)
+        y = comm.gemm_ar(x2, wc, True)
+        ctx.w, ctx.x_shape, ctx.x_dtype = w, x.shape, x.dtype
+        ctx.save_for_backward(x2)
+        return y.view(*x.shape[:-1], -1)
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        (x2,) = ctx.saved_tensors
+        dy2 = _bf16_2d(dy)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            wc = _cast_weight((ctx.w,), torch.bfloat16)
+            dx = matmul(dy2, wc, out_dtype=torch.bfloat16).view(ctx.x_shape).to(ctx.x_dtype)
+        return (dx, None, *weight_grads((ctx.w,), [ctx.needs_input_grad[2]], dy2, x2))
+
+
 def enabled(tp: Any, x: torch.Tensor) -> bool:
-    """Fused collectives apply to CUDA sequence-parallel TP groups whose shards are whole 256-row tiles."""
-    if os.environ.get("MINT_FUSED_TP", "1") == "0" or tp is None or tp.size < 2 or not tp.sp or not x.is_cuda:
+    """Fused collectives apply to CUDA TP groups of 2..8 ranks whose row chunks are whole 256-row
+    tiles: with SP the per-rank sequence shard, without SP the rows / tp block of the all-reduce."""
+    if os.environ.get("MINT_FUSED_TP", "1") == "0" or tp is None or tp.size < 2 or tp.size > 8 or not x.is_cuda:
         return False
-    if not _ext.kernels_enabled() or not hasattr(_ext.require(), "gemm_ag"):
+    if not _ext.kernels_enabled() or not hasattr(_ext.require(), "gemm_ag") or x.dim() != 3:
         return False
-    return x.dim() == 3 and x.shape[1] % 256 == 0
+    if tp.sp:
+        return x.shape[1] % 256 == 0
+    return (x.shape[0] * x.shape[1]) % (256 * tp.size) == 0
 
 
 def column_parallel_linear(x: torch.Tensor, weights: tuple[torch.Tensor, ...], tp: Any) -> torch.Tensor:
-    """Sequence-parallel input ``[B, T/tp, K]`` -> ``[B, T, sum N_i / tp]``."""
+    """SP: sequence-parallel input ``[B, T/tp, K]`` -> ``[B, T, sum N_i / tp]`` (all-gather fused
+    into the GEMM). No SP: replicated ``[B, T, K]`` -> ``[B, T, sum N_i / tp]`` (backward all-reduce
+    fused)."""
+    comm = get_comm(tp.group, x.device)
+    if not tp.sp:
+        return _ColumnParallelARFn.apply(x, comm, *weights)
     keep = torch.is_grad_enabled() and (x.requires_grad or any(w.requires_grad for w in weights))
-    return _ColumnParallelFn.apply(x, get_comm(tp.group, x.device), keep, *weights)
+    return _ColumnParallelFn.apply(x, comm, keep, *weights)
 
 
 def row_parallel_linear(x: torch.Tensor, w: torch.Tensor, tp: Any) -> torch.Tensor:
-    """``[B, T, K/tp]`` -> sequence-parallel output ``[B, T/tp, N]``."""
-    return _RowParallelFn.apply(x, get_comm(tp.group, x.device), w)
+    """``[B, T, K/tp]`` -> SP: sequence-parallel ``[B, T/tp, N]`` (reduce-scatter fused); no SP:
+    replicated ``[B, T, N]`` (all-reduce fused)."""
+    comm = get_comm(tp.group, x.device)
+    if not tp.sp:
+        return _RowParallelARFn.apply(x, comm, w)
+    return _RowParallelFn.apply(x, comm, w)
 
 
 def begin_forward(tp: Any, device: torch.device) -> None:  # noqa: ARG001

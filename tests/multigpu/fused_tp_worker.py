@@ -3,8 +3,9 @@
 Checks the fused tensor-parallel kernels against NCCL collectives + an fp32 reference GEMM:
   1. all-gather -> GEMM (weights K-major and MN-major), three calls in a row;
   2. GEMM -> reduce-scatter (both weight layouts), three calls in a row;
-  3. a small sequence-parallel Gemma (tp = world): loss and every gradient with the fused kernels
-     against the same model on the NCCL path.
+  3. GEMM -> all-reduce (tensor parallelism without SP), both weight layouts;
+  4. a small Gemma (tp = world), with and without sequence parallelism: loss and every gradient
+     with the fused kernels against the same model on the NCCL path.
 Prints one line per check and exits non-zero on a mismatch.
 """
 
@@ -72,6 +73,13 @@ def main() -> None:
             failures += not ok
             print(f"[rank {rank}] GEMM->reduce-scatter call {it} kmajor={kmajor}: rel err {e:.2e} "
                   f"{'OK' if ok else 'FAIL'}", flush=True)
+            # GEMM -> all-reduce (no SP): the full sum on every rank
+            full_out = comm.gemm_ar(a, wb, kmajor)
+            e = rel(full_out, total)
+            ok = e < 1e-2
+            failures += not ok
+            print(f"[rank {rank}] GEMM->all-reduce call {it} kmajor={kmajor}: rel err {e:.2e} "
+                  f"{'OK' if ok else 'FAIL'}", flush=True)
     torch.cuda.synchronize()
     _ext.check_device_status()
 
@@ -109,33 +117,34 @@ def main() -> None:
     from mint_b200.trainer.base import BasetrainConfig
     from mint_b200.utils.device import Device, DeviceConfig
 
-    device = Device(DeviceConfig(mixed_precision=True, tp_size=world, ddp_level=0, sp=True))
     cfg = GemmaConfig(embed_dim=256, hidden_dim=512, seq_length=256 * world, vocab_size=1024, n_layers=2, n_heads=2 * world,
                       n_kv_heads=2 * world, head_dim=128, rope_base_theta=10000)
     tcfg = BasetrainConfig(use_meta_device=True, compile_model=False, gradient_checkpointing=False)
-    results = {}
-    for mode in ("0", "1"):
-        os.environ["MINT_FUSED_TP"] = mode
-        model = build_model(cfg, tcfg, device, seed=7)
-        torch.manual_seed(11)
-        x = torch.randint(0, cfg.vocab_size, (2, cfg.seq_length), device=dev)
-        y = torch.randint(0, cfg.vocab_size, (2, cfg.seq_length), device=dev)
-        m = torch.ones(2, cfg.seq_length, device=dev)
-        with device.autocast():
-            loss = model.loss(x, y, m)
-        loss.backward()
-        grads = {n: p.grad.detach().float().clone() for n, p in model.named_parameters() if p.grad is not None}
-        results[mode] = (float(loss.detach()), grads)
-    l0, g0 = results["0"]
-    l1, g1 = results["1"]
-    ok = abs(l0 - l1) < 2e-2 * abs(l0)
-    failures += not ok
-    print(f"[rank {rank}] model loss NCCL {l0:.5f} fused {l1:.5f} {'OK' if ok else 'FAIL'}", flush=True)
-    worst = max(rel(g1[n], g0[n]) for n in g0)
-    ok = worst < 5e-2 and set(g0) == set(g1)
-    failures += not ok
-    print(f"[rank {rank}] model grads worst rel err {worst:.2e} over {len(g0)} params {'OK' if ok else 'FAIL'}",
-          flush=True)
+    for sp in (True, False):
+        device = Device(DeviceConfig(mixed_precision=True, tp_size=world, ddp_level=0, sp=sp))
+        results = {}
+        for mode in ("0", "1"):
+            os.environ["MINT_FUSED_TP"] = mode
+            model = build_model(cfg, tcfg, device, seed=7)
+            torch.manual_seed(11)
+            x = torch.randint(0, cfg.vocab_size, (2, cfg.seq_length), device=dev)
+            y = torch.randint(0, cfg.vocab_size, (2, cfg.seq_length), device=dev)
+            m = torch.ones(2, cfg.seq_length, device=dev)
+            with device.autocast():
+                loss = model.loss(x, y, m)
+            loss.backward()
+            grads = {n: p.grad.detach().float().clone() for n, p in model.named_parameters() if p.grad is not None}
+            results[mode] = (float(loss.detach()), grads)
+        l0, g0 = results["0"]
+        l1, g1 = results["1"]
+        ok = abs(l0 - l1) < 2e-2 * abs(l0)
+        failures += not ok
+        print(f"[rank {rank}] model sp={sp} loss NCCL {l0:.5f} fused {l1:.5f} {'OK' if ok else 'FAIL'}", flush=True)
+        worst = max(rel(g1[n], g0[n]) for n in g0)
+        ok = worst < 5e-2 and set(g0) == set(g1)
+        failures += not ok
+        print(f"[rank {rank}] model sp={sp} grads worst rel err {worst:.2e} over {len(g0)} params "
+              f"{'OK' if ok else 'FAIL'}", flush=True)
     torch.cuda.synchronize()
     _ext.check_device_status()
     dist.barrier()
