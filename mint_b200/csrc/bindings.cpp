@@ -44,6 +44,8 @@ void normuon_scale(const at::Tensor& partial, at::Tensor& v2, at::Tensor& scale,
 void normuon_apply(const at::Tensor& X, const at::Tensor& scale, const at::Tensor& pptrs, int64_t r0, int64_t c0,
                    int64_t rs, int64_t cs, bool tall, double lr, double wd, const c10::optional<at::Tensor>& peer_ptrs,
                    int64_t rank, int64_t world);
+void gemm_geglu_fwd(const at::Tensor& X, const at::Tensor& W12, at::Tensor& AB, at::Tensor& H);
+void gemm_geglu_bwd(const at::Tensor& DY, const at::Tensor& W3, const at::Tensor& AB, at::Tensor& DAB);
 void zero_adamw_push(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
                      double b2, double eps, double wd, int64_t step, const c10::optional<at::Tensor>& gscale,
                      const std::vector<int64_t>& bucket_ptrs, int64_t rank, int64_t world);
@@ -169,6 +171,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("doc"),
         py::arg("causal"), py::arg("window"), py::arg("scale"), py::arg("dbounds") = py::none());
   m.def("gemm_ag", &mint::gemm_ag, "tensor-parallel all-gather of A's rows fused into a CTA-pair tcgen05 GEMM");
+  m.def("gemm_geglu_fwd", &mint::gemm_geglu_fwd,
+        "fc1||fc2 GEMM with GeGLU in the epilogue: X @ [W1;W2]^T -> ab (kept) and h = gelu_tanh(a) * b");
+  m.def("gemm_geglu_bwd", &mint::gemm_geglu_bwd,
+        "fc3 input-gradient GEMM with the GeGLU backward in the epilogue: dab from dy @ W3 and the saved ab");
   m.def("gemm_rs", &mint::gemm_rs, "CTA-pair tcgen05 GEMM with the reduce-scatter of its output rows fused in");
   m.def("zero_reduce_scatter", &mint::zero_reduce_scatter,
         "ZeRO gradient reduce-scatter over NVLink peer memory, 1/dp scale and squared norm fused");

@@ -435,6 +435,10 @@ struct CommParams {
   const int* rs_flag_local;      // RS: our flags [world][rs_flag_stride], block of source s at s * stride
   long long rs_flag_stride;      // RS: flags per source rank (>= Mc / 128 * tiles_n * 4)
   long long mc;                  // rows per chunk (M / world)
+  // GeGLU modes (COMM 3 forward, 4 backward; no communication)
+  CUtensorMap geglu_map;         // 3: h [M, F] store map (32 x 64 bf16 boxes)
+  const __nv_bfloat16* geglu_ab; // 4: the forward's [a | b] rows [M, 2F] (read by the epilogue)
+  int geglu_f;                   // F (hidden width; multiple of 128)
 };
 
 __device__ __forceinline__ int chunk_of_row(const CommParams& c, long long g) {
@@ -626,6 +630,154 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
   return true;
 }
 
+// ---------------------------------------------------------------------------------------------
+// GeGLU fused into the fc1||fc2 GEMM and into the fc3 input-gradient GEMM.
+// gelu_tanh(x) = 0.5 x (1 + tanh(k0 (x + k1 x^3))), k0 = sqrt(2 / pi), k1 = 0.044715
+constexpr float kGeluK0 = 0.7978845608028654f;
+constexpr float kGeluK1 = 0.044715f;
+
+// Stage 32 rows x 64 bf16 columns (this lane's row in v[0..63]) in a 128B-swizzled 4 KB buffer of
+// the per-warp double buffer and store it with one TMA box at (x, y).
+__device__ __forceinline__ void stage_store_bf16(const CUtensorMap* map, const float* v, uint8_t* bufs, int lane,
+                                                 int& seq, int x, int y) {
+  uint8_t* buf = bufs + (seq & 1) * 4096;
+  if (lane == 0) bulk_wait_read<1>();  // the store issued two boxes ago has read this buffer
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+    u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(map, buf, x, y, 0);
+    bulk_commit();
+  }
+  ++seq;
+}
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Forward (COMM 3): the pair's B rows are fc1 rows [tn * BN/2, +BN/2) (leader) and fc2 rows
+// [F + tn * BN/2, +BN/2) (follower), so accumulator columns [0, BN/2) hold a and [BN/2, BN) hold
+// the matching b. The epilogue stores a and b into their places of ab [M, 2F] (kept for the
+// backward) and h = gelu_tanh(a) * b into h [M, F], from the bf16-rounded a and b (the same
+// values a separate GeGLU pass over the stored ab would read).
+template <int BN>
+__device__ __forceinline__ void epilogue_tile_geglu_fwd(const Params& p, const CommParams& c, const CUtensorMap* tmc,
+                                                        uint32_t tmem_acc, int row0, int tn, uint8_t* bufs, int lane,
+                                                        int& seq) {
+  const int F = c.geglu_f;
+#pragma unroll 1
+  for (int g = 0; g < BN / 128; ++g) {
+    uint32_t ra[2][32], rb[2][32];
+    tmem_ld_32x32b_x32(tmem_acc + g * 64, ra[0]);
+    tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, ra[1]);
+    tmem_ld_32x32b_x32(tmem_acc + BN / 2 + g * 64, rb[0]);
+    tmem_ld_32x32b_x32(tmem_acc + BN / 2 + g * 64 + 32, rb[1]);
+    tmem_ld_wait();
+    const int col0 = tn * (BN / 2) + g * 64;
+    if (col0 >= F || row0 >= p.M || (p.diag & 1)) continue;  // warp-uniform
+    float v[64];
+#pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = bf16_round(__uint_as_float(ra[j >> 5][j & 31]));
+    stage_store_bf16(tmc, v, bufs, lane, seq, col0, row0);
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const float b = bf16_round(__uint_as_float(rb[j >> 5][j & 31]));
+      const float a = v[j];
+      v[j] = b;
+      ra[j >> 5][j & 31] = __float_as_uint(0.5f * a * (1.f + tanhf(kGeluK0 * (a + kGeluK1 * a * a * a))) * b);
+    }
+    stage_store_bf16(tmc, v, bufs, lane, seq, F + col0, row0);
+#pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(ra[j >> 5][j & 31]);
+    stage_store_bf16(&c.geglu_map, v, bufs, lane, seq, col0, row0);
+  }
+}
+
+// Backward (COMM 4): the GEMM computes dh = dy @ W3 ([M, F]); for each 64-column group the
+// epilogue reads the forward's a and b of its 32 rows, rounds dh to bf16 (the value a separate pass
+// would read) and stores da = dh * b * gelu'(a) and db = dh * gelu(a) into dab [M, 2F]; dh itself
+// never reaches memory.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile_geglu_bwd(const Params& p, const CommParams& c, const CUtensorMap* tmc,
+                                                        uint32_t tmem_acc, int row0, int col_base, uint8_t* bufs,
+                                                        int lane, int& seq) {
+  const int F = c.geglu_f;
+  const int row = row0 + lane;
+#pragma unroll 1
+  for (int g = 0; g < BN / 64; ++g) {
+    const int col0 = col_base + g * 64;
+    uint4 ua[8], ub[8];
+    const bool live = col0 < F && row0 < p.M && !(p.diag & 1);  // warp-uniform
+    if (live && row < p.M) {
+      const __nv_bfloat16* arow = c.geglu_ab + static_cast<long long>(row) * 2 * F + col0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        ua[j] = *reinterpret_cast<const uint4*>(arow + 8 * j);
+        ub[j] = *reinterpret_cast<const uint4*>(arow + F + 8 * j);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ua[j] = ub[j] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    uint32_t r[2][32];
+    tmem_ld_32x32b_x32(tmem_acc + g * 64, r[0]);
+    tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, r[1]);
+    tmem_ld_wait();
+    if (!live) continue;
+    // da and db go straight into the two staging buffers, 8 columns at a time (both buffers free
+    // once every earlier store of this warp has read its source)
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+    uint8_t* bufa = bufs;
+    uint8_t* bufb = bufs + 4096;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&ua[j]);
+      const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&ub[j]);
+      uint32_t qa[4], qb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a2 = __bfloat1622float2(pa[e]);
+        const float2 b2 = __bfloat1622float2(pb[e]);
+        const float av[2] = {a2.x, a2.y}, bv[2] = {b2.x, b2.y};
+        float da[2], db[2];
+#pragma unroll
+        for (int z = 0; z < 2; ++z) {
+          const int k = 8 * j + 2 * e + z;
+          const float x = av[z];
+          const float gr = bf16_round(__uint_as_float(r[k >> 5][k & 31]));
+          const float t = tanhf(kGeluK0 * (x + kGeluK1 * x * x * x));
+          const float gelu = 0.5f * x * (1.f + t);
+          const float dgelu = 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * kGeluK0 * (1.f + 3.f * kGeluK1 * x * x);
+          da[z] = gr * bv[z] * dgelu;
+          db[z] = gr * gelu;
+        }
+        qa[e] = pack_bf16x2(da[0], da[1]);
+        qb[e] = pack_bf16x2(db[0], db[1]);
+      }
+      const int off = lane * 128 + ((j ^ (lane & 7)) << 4);
+      *reinterpret_cast<uint4*>(bufa + off) = make_uint4(qa[0], qa[1], qa[2], qa[3]);
+      *reinterpret_cast<uint4*>(bufb + off) = make_uint4(qb[0], qb[1], qb[2], qb[3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tmc, bufa, col0, row0, 0);
+      tma_store_3d(tmc, bufb, F + col0, row0, 0);
+      bulk_commit();
+    }
+    seq += 2;
+  }
+}
+
 constexpr int kAgPieces = 8;  // a 128-row block is copied as 8 pieces of 16 rows by different warps
 
 // ---------------------------------------------------------------------------------------------
@@ -700,7 +852,8 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, C_::kTmemCols);
-  if (COMM != 0 && blockIdx.x == 0 && threadIdx.x == 64) {
+  constexpr bool kTP = COMM == 1 || COMM == 2;  // modes that talk to peers
+  if (kTP && blockIdx.x == 0 && threadIdx.x == 64) {
     // this rank entered call seq: its inputs of the call are in place (stream order) and the buffers
     // peers write into for this call are no longer read by an earlier call
     __threadfence_system();
@@ -725,7 +878,7 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
     const int tile = w % tiles;
     const int split = w / tiles;
     tile_coords(tile, tiles_m2, p.tiles_n, tm, tn);
-    if constexpr (COMM != 0) tm = comm_tile_m(c, tm, tiles_m2, COMM == 1);
+    if constexpr (kTP) tm = comm_tile_m(c, tm, tiles_m2, COMM == 1);
     kb0 = split * p.kbps;
     nkb = min(kblocks, kb0 + p.kbps) - kb0;
   };
@@ -741,7 +894,9 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
         int bi, tm, tn, kb0, nkb;
         item(w, bi, tm, tn, kb0, nkb);
         const int m0 = tm * 256 + static_cast<int>(cr) * 128;
-        const int n0 = tn * BN + static_cast<int>(cr) * (BN / 2);
+        // GeGLU forward: the leader loads fc1 rows, the follower the matching fc2 rows (F below them)
+        const int n0 = COMM == 3 ? static_cast<int>(cr) * c.geglu_f + tn * (BN / 2)
+                                 : tn * BN + static_cast<int>(cr) * (BN / 2);
         if constexpr (COMM == 1) {
           // a peer's rows: wait until a copy warp has landed this 128-row block in our buffer
           if (chunk_of_row(c, m0) != c.rank) {
@@ -911,6 +1066,18 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
         if (!ok) break;
+        continue;
+      }
+      if constexpr (COMM == 3 || COMM == 4) {
+        const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+        if constexpr (COMM == 3) {
+          epilogue_tile_geglu_fwd<BN>(p, c, &tmc, tacc, row0, tn, bufs, lane, seq);
+        } else {
+          epilogue_tile_geglu_bwd<BN>(p, c, &tmc, tacc, row0, tn * BN, bufs, lane, seq);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
         continue;
       }
       epilogue_tile<kCols>(p, &tmc, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + half * kCols,
@@ -1201,6 +1368,61 @@ gemm::CommParams comm_common(int64_t rank, int64_t world, int64_t seg, int64_t s
 }
 
 }  // namespace
+
+// GeGLU MLP halves with the activation fused into the GEMM epilogues (CTA-pair kernel, BN 256).
+//   forward:  X [M, K] @ W12^T, W12 = [fc1; fc2] as one [2F, K] bf16 matrix -> AB [M, 2F] (a | b,
+//             kept for the backward) and H = gelu_tanh(a) * b [M, F]
+//   backward: dh = DY [M, D] @ W3 (W3 [D, F], the fc3 weight) never stored; DAB [M, 2F] =
+//             [dh * b * gelu'(a) | dh * gelu(a)] from AB
+void gemm_geglu_fwd(const at::Tensor& X, const at::Tensor& W12, at::Tensor& AB, at::Tensor& H) {
+  c10::cuda::CUDAGuard guard(X.device());
+  const int dev = X.get_device();
+  int64_t M, N2, K;
+  gemm::Params p = comm_params_base(X, W12, AB, true, dev, M, N2, K);
+  const int64_t F = N2 / 2;
+  MINT_CHECK(N2 % 256 == 0, "GeGLU GEMM needs the hidden width F a multiple of 128");
+  check_contig(H, "H");
+  MINT_CHECK(H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.size(0) == M && H.size(1) == F,
+             "H must be bf16 [M, F]");
+  MINT_CHECK(AB.size(0) == M && AB.size(1) == N2, "AB must be bf16 [M, 2F]");
+  if (M == 0) return;
+  gemm::CommParams c{};
+  c.geglu_f = static_cast<int>(F);
+  constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
+  c.geglu_map = make_tmap_3d(H.data_ptr(), BF, 2, F, M, 1, F, M * F, 64, 32, 1, SW128);
+  const CUtensorMap ta = make_tmap_3d(X.data_ptr(), BF, 2, K, M, 1, X.stride(0), M * X.stride(0), 64, 128, 1, SW128);
+  const uint64_t ldb = W12.stride(0);
+  const CUtensorMap tb = make_tmap_3d(W12.data_ptr(), BF, 2, K, N2, 1, ldb, N2 * ldb, 64, 128, 1, SW128);
+  const CUtensorMap tc = make_tmap_3d(AB.data_ptr(), BF, 2, N2, M, 1, N2, M * N2, 64, 32, 1, SW128);
+  gemm::launch_pair<256, false, false, 3>(ta, tb, tc, p, num_sms(dev), at::cuda::getCurrentCUDAStream(), c);
+}
+
+void gemm_geglu_bwd(const at::Tensor& DY, const at::Tensor& W3, const at::Tensor& AB, at::Tensor& DAB) {
+  c10::cuda::CUDAGuard guard(DY.device());
+  const int dev = DY.get_device();
+  int64_t M, F, K;
+  gemm::Params p = comm_params_base(DY, W3, DAB, false, dev, M, F, K);  // N = F (dh columns)
+  MINT_CHECK(F % 128 == 0, "GeGLU GEMM needs the hidden width F a multiple of 128");
+  check_contig(AB, "AB");
+  MINT_CHECK(AB.scalar_type() == at::kBFloat16 && AB.dim() == 2 && AB.size(0) == M && AB.size(1) == 2 * F,
+             "AB must be bf16 [M, 2F]");
+  MINT_CHECK(DAB.size(0) == M && DAB.size(1) == 2 * F, "DAB must be bf16 [M, 2F]");
+  if (M == 0) return;
+  p.N = static_cast<int>(F);
+  p.ldc = 2 * F;
+  p.tiles_n = static_cast<int>((F + 255) / 256);
+  gemm::CommParams c{};
+  c.geglu_f = static_cast<int>(F);
+  c.geglu_ab = reinterpret_cast<const __nv_bfloat16*>(AB.data_ptr());
+  constexpr int BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  constexpr int SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMap ta = make_tmap_3d(DY.data_ptr(), BF, 2, K, M, 1, DY.stride(0), M * DY.stride(0), 64, 128, 1, SW128);
+  const uint64_t ldb = W3.stride(0);
+  const CUtensorMap tb = make_tmap_3d(W3.data_ptr(), BF, 2, F, K, 1, ldb, K * ldb, 64, 64, 1, SW128);
+  const CUtensorMap tc = make_tmap_3d(DAB.data_ptr(), BF, 2, 2 * F, M, 1, 2 * F, M * 2 * F, 64, 32, 1, SW128);
+  gemm::launch_pair<256, false, true, 4>(ta, tb, tc, p, num_sms(dev), at::cuda::getCurrentCUDAStream(), c);
+}
 
 // C[M, N] = A[M, K] @ op(B) with the all-gather of A's rows over the tensor-parallel group fused in:
 // A is this rank's symmetric gathered buffer holding its own chunk; `src_ptrs[p]` is rank p's

@@ -1,6 +1,9 @@
 """GeGLU feed-forward ``fc3(gelu_tanh(fc1 x) * fc2 x)`` (mint/nn/ffn.py:5-15).
 
-fc1 and fc2 run as one GEMM over ``[W1; W2]`` followed by the fused GeGLU kernel.
+On CUDA the whole MLP is two GEMMs with the GeGLU in their epilogues (``ops.glu.geglu_mlp``):
+fc1 and fc2 run as one GEMM over ``[W1; W2]`` that also writes ``h``, and the backward's fc3
+input-gradient GEMM writes ``d[a | b]`` directly. Under tensor parallelism with the fused
+collectives, the GEMMs carry the collectives instead and GeGLU is a separate kernel.
 """
 
 from __future__ import annotations
@@ -9,7 +12,7 @@ import torch
 from torch import nn
 
 from mint_b200.nn.base import compute_dtype
-from mint_b200.ops.glu import geglu
+from mint_b200.ops.glu import geglu, geglu_mlp, geglu_mlp_fusable
 from mint_b200.ops.linear import linear
 from mint_b200.parallel import fused as fused_tp
 from mint_b200.parallel import tp as tpc
@@ -34,7 +37,10 @@ class GLU(nn.Module):
             ab = fused_tp.column_parallel_linear(x, (self.fc1.weight, self.fc2.weight), self.tp)
             return fused_tp.row_parallel_linear(geglu(ab), self.fc3.weight, self.tp)
         x = tpc.enter_column_parallel(x, self.tp)
-        if self._fusable():
+        if self._fusable() and geglu_mlp_fusable(x, self.fc1.weight, self.fc2.weight, self.fc3.weight, dt):
+            # GeGLU inside the fc1||fc2 GEMM's epilogue and its backward inside fc3's dgrad epilogue
+            out = geglu_mlp(x, self.fc1.weight, self.fc2.weight, self.fc3.weight, compute_dtype=dt)
+        elif self._fusable():
             ab = linear(x, self.fc1.weight, self.fc2.weight, compute_dtype=dt)
             h = geglu(ab)
             out = linear(h, self.fc3.weight, compute_dtype=dt)

@@ -189,3 +189,34 @@ def test_gemm_cta_pair_split_k_accumulate():
     exp = start + a.float().t() @ b.float()
     rel = ((out - exp).norm() / exp.norm()).item()
     assert rel < 1e-4, f"rel err {rel}"
+
+
+@pytest.mark.parametrize("M,d,F", [(1000, 256, 384), (4096, 768, 3072), (300, 128, 128)])
+def test_geglu_mlp_fused(M, d, F):
+    """GeGLU inside the GEMM epilogues (forward: fc1||fc2 GEMM writes ab and h; backward: the fc3
+    input-gradient GEMM writes d[a|b]) against fp32 PyTorch: output and every gradient."""
+    from mint_b200.ops.glu import _GeGLUMLPFn, geglu_mlp_fusable
+
+    torch.manual_seed(11)
+    x = (torch.randn(M, d, device="cuda") * 0.5).requires_grad_()
+    w1 = (torch.randn(F, d, device="cuda") * d ** -0.5).requires_grad_()
+    w2 = (torch.randn(F, d, device="cuda") * d ** -0.5).requires_grad_()
+    w3 = (torch.randn(d, F, device="cuda") * F ** -0.5).requires_grad_()
+    assert geglu_mlp_fusable(x, w1, w2, w3, torch.bfloat16)
+    gy = torch.randn(M, d, device="cuda")
+    y = _GeGLUMLPFn.apply(x, torch.bfloat16, w1, w2, w3)
+    (y.float() * gy).sum().backward()
+    xs, a1, a2, a3 = (t.detach().clone().requires_grad_() for t in (x, w1, w2, w3))
+    xb = xs.bfloat16().float()
+    a = xb @ a1.bfloat16().float().t()
+    b = xb @ a2.bfloat16().float().t()
+    h = torch.nn.functional.gelu(a, approximate="tanh") * b
+    y2 = h @ a3.bfloat16().float().t()
+    (y2 * gy).sum().backward()
+
+    def rel(u, v):
+        return ((u.float() - v.float()).norm() / v.float().norm()).item()
+
+    assert rel(y, y2) < 2e-2
+    for got, want in ((x.grad, xs.grad), (w1.grad, a1.grad), (w2.grad, a2.grad), (w3.grad, a3.grad)):
+        assert rel(got, want) < 3e-2, rel(got, want)

@@ -7,7 +7,8 @@ Checks the ZeRO peer-memory collectives (csrc/zero_comm.cu) against NCCL:
   3. ZeRO-2 training (dp = world, NorMuon + AdamW, global-norm clipping) for three steps: the
      consolidated parameters with the fused transport (reduce-scatter straight into the gradient
      shard; AdamW / NorMuon update kernels that store the new values into every peer's copy)
-     against the NCCL transport, and every rank's full parameter buckets identical.
+     against the NCCL transport, and every rank's full parameter buckets identical;
+  4. the same training at ZeRO-3 (NCCL parameter gathers per block) against ZeRO-2.
 Prints one line per check and exits non-zero on a mismatch.
 """
 
@@ -28,7 +29,7 @@ def rel(a: torch.Tensor, b: torch.Tensor) -> float:
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
-def train(fused: str, dev: torch.device) -> dict[str, torch.Tensor]:
+def train(fused: str, dev: torch.device, level: int = 2) -> dict[str, torch.Tensor]:
     from mint_b200.models.gemma import Gemma, GemmaConfig, configure_optimizer
     from mint_b200.optim.muon_adamw import MuonAdamWConfig
     from mint_b200.parallel.api import setup_parallel
@@ -40,12 +41,12 @@ def train(fused: str, dev: torch.device) -> dict[str, torch.Tensor]:
     os.environ["MINT_FUSED_ZERO"] = fused
     cfg = GemmaConfig(embed_dim=256, hidden_dim=512, seq_length=256, vocab_size=1024, n_layers=2, n_heads=2,
                       n_kv_heads=1, head_dim=128, rope_base_theta=10000)
-    pctx = ParallelContext.build(tp_size=1, ddp_level=2, device_type="cuda")
+    pctx = ParallelContext.build(tp_size=1, ddp_level=level, device_type="cuda")
     torch.manual_seed(1337)
     model = Gemma(cfg).to(dev)
     model = setup_parallel(model, pctx, bucket_cap_mb=0.5)
     eng = get_engine(model)
-    assert eng.fused == (fused == "1"), (eng.fused, fused)
+    assert eng.fused == (fused == "1" and level == 2), (eng.fused, fused, level)
     opt = configure_optimizer(model, cfg, SchedulerConfig(), MuonAdamWConfig(), dp_group=pctx.dp_group)
     g = torch.Generator(device="cpu").manual_seed(7)
     for _ in range(3):
@@ -63,7 +64,7 @@ def train(fused: str, dev: torch.device) -> dict[str, torch.Tensor]:
         eng.clip_grad_norm(0.5)
         opt.step()
     torch.cuda.synchronize()
-    if fused == "1":
+    if eng.fused:
         # the sharded updates stored their results into the peers' copies (AdamW buckets and the
         # owners' NorMuon matrices): every rank's full bucket must equal rank 0's
         assert eng.fused_update_pushes > 0, "no update kernel pushed its results"
@@ -142,6 +143,13 @@ def main() -> None:
     failures += not ok
     print(f"[rank {rank}] ZeRO-2 3 steps fused vs NCCL: worst param rel diff {worst:.2e} over {len(ref)} "
           f"{'OK' if ok else 'FAIL'}", flush=True)
+    # ZeRO-3 (parameters sharded too, gathered per block ahead of use) against ZeRO-2
+    z3 = train("0", dev, level=3)
+    worst3 = max(rel(z3[k], ref[k]) for k in ref)
+    ok = set(ref) == set(z3) and worst3 < 1e-3
+    failures += not ok
+    print(f"[rank {rank}] ZeRO-3 3 steps vs ZeRO-2: worst param rel diff {worst3:.2e} {'OK' if ok else 'FAIL'}",
+          flush=True)
     torch.cuda.synchronize()
     _ext.check_device_status()
     dist.barrier()
