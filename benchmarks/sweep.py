@@ -79,6 +79,12 @@ def build_cells(max_gpus: int, impls: list[str]) -> list[Cell]:
     for n in (2, 4, 8):
         port += 1
         cells.append(Cell("zero", f"zero_fused dp={n}", n, torchrun(n, port, "benchmarks/zero_fused.py"), 600))
+    for n in (1, 8):
+        for impl in impls:
+            port += 1
+            cells.append(Cell("dpo", f"dpo {impl} {n}gpu", n,
+                              torchrun(n, port, "benchmarks/dpo_step.py", "--gpus", str(n), "--impl", impl,
+                                       "--ddp-level", "3" if n > 1 else "0"), 900))
     return [c for c in cells if c.gpus <= max_gpus]
 
 
