@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import os
 import statistics
 import sys
 from pathlib import Path
@@ -96,6 +97,28 @@ def run_attn(a: argparse.Namespace) -> dict:
     causal = not a.no_causal
     extra = (bounds,) if bounds is not None else ()
     o, lse = C.flash_attn_fwd(q, k, v, doc, causal, a.window, scale, *extra)
+    if os.environ.get("MINT_FA_TRACE"):
+        # per-phase clock64 deltas of the longest query tile (diagnostic build path), median over tiles
+        for _ in range(3):
+            C.flash_attn_fwd(q, k, v, doc, causal, a.window, scale, *extra)
+        torch.cuda.synchronize()
+        tr = C.flash_attn_fwd_trace().view(-1).tolist()
+        steps, tiles = 10, 64
+        n = min(tiles, (T + 127) // 128)
+        names = ["s_wait", "tmem_ld", "max", "mx_xchg", "rescale", "exp", "pv_wait", "p_store", "fence_arrive"]
+        out = {}
+        for half in range(2):
+            base = half * tiles * steps
+            rows = [tr[base + t * steps: base + (t + 1) * steps] for t in range(n)]
+            for i, nm in enumerate(names):
+                out[f"h{half}_{nm}"] = statistics.median(r[i + 1] - r[i] for r in rows)
+            out[f"h{half}_tile"] = statistics.median(rows[t + 1][0] - rows[t][0] for t in range(n - 1))
+        mb = 2 * tiles * steps
+        mrows = [tr[mb + t * 4: mb + t * 4 + 4] for t in range(n)]
+        out["mma_issue_s"] = statistics.median(r[1] - r[0] for r in mrows)
+        out["mma_wait_p"] = statistics.median(r[2] - r[1] for r in mrows)
+        out["mma_issue_pv"] = statistics.median(r[3] - r[2] for r in mrows)
+        print(json.dumps({"fa_fwd_trace_cycles": out, "tiles": n}), flush=True)
     if a.once:
         C.flash_attn_bwd(do, q, k, v, o, lse, doc, causal, a.window, scale, *extra)
         torch.cuda.synchronize()

@@ -41,7 +41,13 @@ struct FwdParams {
   int diag;               // timing diagnostics (MINT_FA_DIAG bits): 1 exp2 replaced by a multiply-add,
                           // 2 MMAs not issued (results meaningless; for isolating pipeline stages)
   uint32_t* status;
+  // MINT_FA_TRACE=1: clock64 stamps of block (0, 0, 0) -- the longest causal query tile -- for the
+  // first kTraceTiles key tiles: [softmax half][tile][kTraceSteps] from lane 0 of warps 4 and 8,
+  // then [tile][4] from the MMA thread (diagnostics only; null otherwise)
+  unsigned long long* trace;
 };
+constexpr int kTraceTiles = 64;
+constexpr int kTraceSteps = 10;
 
 struct Smem {
   uint8_t q[kTileBytes];
@@ -183,7 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&s.s_full[0]);
         umma_commit(&s.k_empty[0]);
       }
+      unsigned long long* tr = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+                                   ? p.trace + 2 * kTraceTiles * kTraceSteps
+                                   : nullptr;
       for (int t = 0; t < n && ok; ++t) {
+        if (tr != nullptr && t < kTraceTiles) tr[t * 4] = clock64();
         if (t + 1 < n) {
           const int st = (t + 1) & 1;
           if (!mbar_wait(&s.k_full[st], ((t + 1) >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
@@ -192,10 +202,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&s.s_full[st]);
           umma_commit(&s.k_empty[st]);
         }
+        if (tr != nullptr && t < kTraceTiles) tr[t * 4 + 1] = clock64();
         if (!mbar_wait(&s.p_full, t & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
+        if (tr != nullptr && t < kTraceTiles) tr[t * 4 + 2] = clock64();
         if (!mbar_wait(&s.v_full[t & 1], (t >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
         tc_fence_after();
         if (!(p.diag & 2)) issue_pv(tmem_o, p_addr, smem_u32(s.v[t & 1]), t > 0);
+        if (tr != nullptr && t < kTraceTiles) tr[t * 4 + 3] = clock64();
         umma_commit(&s.pv_done);
         umma_commit(&s.v_empty[t & 1]);
       }
@@ -222,13 +235,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f;  // running max (shared by both halves of the row), this half's row sum
     bool ok = n > 0;
     int pv_waited = -1;  // index of the last PV whose completion this thread observed
+    unsigned long long* tr = (p.trace != nullptr && lane == 0 && (warp == 4 || warp == 8) && blockIdx.x == 0 &&
+                              blockIdx.y == 0 && blockIdx.z == 0)
+                                 ? p.trace + half * kTraceTiles * kTraceSteps
+                                 : nullptr;
+#define FA_STAMP(k) \
+  if (tr != nullptr && t < kTraceTiles) tr[t * kTraceSteps + (k)] = clock64();
     for (int t = 0; t < n && ok; ++t) {
       const int kb = (j0 + t) * kBN;
+      FA_STAMP(0)
       if (!mbar_wait_warp(&s.s_full[t & 1], (t >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      FA_STAMP(1)
       float x[64];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -262,9 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      FA_STAMP(2)
       float mt = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 64; ++c) mt = fmaxf(mt, x[c]);
+      FA_STAMP(3)
       // combine with the other half of the row; the buffer of this parity was last read two tiles
       // ago, before every softmax warp arrived on the previous tile's exchange
       s.mx[t & 1][half][r] = mt;
@@ -275,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       mt = fmaxf(mt, s.mx[t & 1][half ^ 1][r]);
+      FA_STAMP(4)
       const float m_new = fmaxf(m, mt);
       // tcgen05.ld/st are warp-collective: the rescale decision must be uniform across the warp; both
       // warps of a lane quadrant see the same row maxima and so decide alike
@@ -306,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if (m == -INFINITY) {
         m = m_new;  // nothing accumulated in this row yet
       }
+      FA_STAMP(5)
       // P = exp2(x - m) in bf16, this half's row sum in fp32
       uint32_t pk[32];
       float rs = 0.f;
@@ -323,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[c] = pack_bf16x2(a, bb);
       }
       l += rs;
+      FA_STAMP(6)
       // the single P buffer is free once PV_{t-1} completed
       if (t > 0 && pv_waited < t - 1) {
         if (!mbar_wait_warp(&s.pv_done, (t - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
@@ -331,17 +357,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pv_waited = t - 1;
       }
+      FA_STAMP(7)
       // 128B-swizzled K-major store of this half row: swizzle atom `half` (64 keys), 16B chunk c at c ^ (row % 8)
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint4 v4 = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
         *reinterpret_cast<uint4*>(s.p + half * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
       }
+      FA_STAMP(8)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.p_full);
+      FA_STAMP(9)
     }
+#undef FA_STAMP
     if (ok && n > 0 && pv_waited < n - 1) {
       ok = mbar_wait_warp(&s.pv_done, (n - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag);
     }
@@ -473,6 +503,17 @@ const int2* doc_bounds_ptr(const c10::optional<at::Tensor>& doc, const c10::opti
   return reinterpret_cast<const int2*>(holder.data_ptr<int>());
 }
 
+// MINT_FA_TRACE=1 diagnostics: the stamp buffer of the last forward (zeros if tracing is off)
+at::Tensor& fa_trace_buffer() {
+  static at::Tensor buf;
+  return buf;
+}
+
+at::Tensor flash_attn_fwd_trace() {
+  at::Tensor& buf = fa_trace_buffer();
+  return buf.defined() ? buf.clone() : at::zeros({(2 * fa::kTraceSteps + 4) * fa::kTraceTiles}, at::kLong);
+}
+
 std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
                                        double scale, const c10::optional<at::Tensor>& dbounds) {
@@ -514,6 +555,14 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k,
     return e == nullptr ? 0 : std::atoi(e);
   }();
   p.diag = diag;
+  static const bool trace = std::getenv("MINT_FA_TRACE") != nullptr;
+  if (trace) {
+    at::Tensor& buf = fa_trace_buffer();
+    if (!buf.defined() || buf.device() != q.device()) {
+      buf = at::zeros({(2 * fa::kTraceSteps + 4) * fa::kTraceTiles}, q.options().dtype(at::kLong));
+    }
+    p.trace = reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>());
+  }
   const CUtensorMap tq = make_tmap_3d_bf16(q.data_ptr(), fa::kD, Hq, static_cast<uint64_t>(B) * T, fa::kD,
                                            static_cast<uint64_t>(Hq) * fa::kD, 64, 1, 128, true);
   const CUtensorMap tk = make_tmap_3d_bf16(k.data_ptr(), fa::kD, Hkv, static_cast<uint64_t>(B) * T, fa::kD,

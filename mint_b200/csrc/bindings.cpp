@@ -61,6 +61,7 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
                                        double scale, const c10::optional<at::Tensor>& dbounds);
 at::Tensor doc_bounds(const at::Tensor& doc);
+at::Tensor flash_attn_fwd_trace();
 void zero_reduce_scatter(const std::vector<int64_t>& bucket_ptrs, at::Tensor& shard, double scale,
                          const c10::optional<at::Tensor>& sumsq, const std::vector<int64_t>& flag_ptrs,
                          const at::Tensor& flags_local, int64_t rank, int64_t world, int64_t seq);
@@ -180,5 +181,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "ZeRO gradient reduce-scatter over NVLink peer memory, 1/dp scale and squared norm fused");
   m.def("zero_all_gather", &mint::zero_all_gather, "ZeRO parameter all-gather: push this rank's shard to every peer");
   m.def("zero_barrier", &mint::zero_barrier, "stream-ordered barrier of a ZeRO group over NVLink peer flags");
+  m.def("flash_attn_fwd_trace", &mint::flash_attn_fwd_trace,
+        "MINT_FA_TRACE=1 diagnostics: clock64 stamps of the last forward's longest query tile");
   m.def("doc_bounds", &mint::doc_bounds, "[B, T, 2] int32 document run [start, end) of every token");
 }
