@@ -97,25 +97,27 @@ __device__ __forceinline__ void mma_mnmn(uint32_t d, uint32_t a, uint32_t b, boo
   for (int k = 0; k < 8; ++k) umma_bf16(d, mnmaj(a, k), mnmaj(b, k), idesc, (acc || k > 0) ? 1u : 0u);
 }
 
-// 64 columns (one swizzle atom `a`) of row r of a K-major 128B-swizzled bf16 tile from fp32 values
+// 64 columns (one swizzle atom `a`) of row r of a K-major 128B-swizzled bf16 tile from finite fp32
+// values (P or dS; converted on the integer pipe, which the exponentials do not use)
 __device__ __forceinline__ void store_half_row_sw128(uint8_t* tile, int a, int r, const float (&x)[64]) {
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const int e = c * 8;
-    uint4 v4 = make_uint4(pack_bf16x2(x[e], x[e + 1]), pack_bf16x2(x[e + 2], x[e + 3]),
-                          pack_bf16x2(x[e + 4], x[e + 5]), pack_bf16x2(x[e + 6], x[e + 7]));
+    uint4 v4 = make_uint4(pack_bf16x2_int(x[e], x[e + 1]), pack_bf16x2_int(x[e + 2], x[e + 3]),
+                          pack_bf16x2_int(x[e + 4], x[e + 5]), pack_bf16x2_int(x[e + 6], x[e + 7]));
     *reinterpret_cast<uint4*>(tile + a * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
   }
 }
 
 __device__ __forceinline__ void load_row64(uint32_t taddr, float (&x)[64]) {
+  uint32_t u0[32], u1[32];  // both loads in flight under one wait
+  tmem_ld_32x32b_x32(taddr, u0);
+  tmem_ld_32x32b_x32(taddr + 32, u1);
+  tmem_ld_wait();
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    uint32_t u[32];
-    tmem_ld_32x32b_x32(taddr + c * 32, u);
-    tmem_ld_wait();
-#pragma unroll
-    for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]);
+  for (int e = 0; e < 32; ++e) {
+    x[e] = __uint_as_float(u0[e]);
+    x[32 + e] = __uint_as_float(u1[e]);
   }
 }
 

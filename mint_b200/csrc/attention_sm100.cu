@@ -61,7 +61,8 @@ struct Smem {
   uint64_t p_full;
   uint64_t pv_done;
   uint64_t mma_done;
-  uint64_t mx_full;        // the 8 softmax warps published their partial row maxima (and, last, row sums)
+  uint64_t mx_full[4];     // per TMEM lane quadrant: both softmax warps of the quadrant published their
+                           // partial row maxima (and, last, row sums)
   float mx[2][2][kBM];     // [tile parity][column half][row] partial maxima of the current score tile
   float lsum[2][kBM];      // [column half][row] partial row sums, exchanged once at the end
   uint32_t tmem_base;
@@ -137,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.s_full[i], 1);
     }
     mbar_init(&s.p_full, 8);
-    mbar_init(&s.mx_full, 8);
+    for (int i = 0; i < 4; ++i) mbar_init(&s.mx_full[i], 2);
     mbar_init(&s.pv_done, 1);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
@@ -251,13 +252,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       FA_STAMP(1)
       float x[64];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + cb + c * 32, u);
+      {
+        uint32_t u0[32], u1[32];  // both loads in flight under one wait
+        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + cb, u0);
+        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + cb + 32, u1);
         tmem_ld_wait();
+        // raw scores: the softmax scale goes into the exponent's FMA (max commutes with a positive scale)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
+        for (int e = 0; e < 32; ++e) {
+          x[e] = __uint_as_float(u0[e]);
+          x[32 + e] = __uint_as_float(u1[e]);
+        }
       }
       const bool doc_mask = p.doc != nullptr && !(doc_sorted && dlast.x <= kb && dfirst.y >= kb + kBN);
       const bool need_mask = (p.causal && kb + kBN - 1 > q0) || (p.window >= 0 && q0 + kBM - 1 - kb > p.window) ||
@@ -292,14 +297,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ago, before every softmax warp arrived on the previous tile's exchange
       s.mx[t & 1][half][r] = mt;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.mx_full);
-      if (!mbar_wait_warp(&s.mx_full, t & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
+      if (lane == 0) mbar_arrive(&s.mx_full[q]);
+      if (!mbar_wait_warp(&s.mx_full[q], t & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
         ok = false;
         break;
       }
       mt = fmaxf(mt, s.mx[t & 1][half ^ 1][r]);
       FA_STAMP(4)
-      const float m_new = fmaxf(m, mt);
+      const float m_new = fmaxf(m, mt * p.scale_log2);  // running max in scaled log2 units
       // tcgen05.ld/st are warp-collective: the rescale decision must be uniform across the warp; both
       // warps of a lane quadrant see the same row maxima and so decide alike
       const bool grow = m != -INFINITY && m_new > m + kRescaleThreshold;
@@ -338,14 +343,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < 32; ++c) {
         float a, bb;
         if (p.diag & 1) {
-          a = (m == -INFINITY) ? 0.f : fmaf(x[2 * c] - m, 0.01f, 1.f);
-          bb = (m == -INFINITY) ? 0.f : fmaf(x[2 * c + 1] - m, 0.01f, 1.f);
+          a = (m == -INFINITY) ? 0.f : fmaf(fmaf(x[2 * c], p.scale_log2, -m), 0.01f, 1.f);
+          bb = (m == -INFINITY) ? 0.f : fmaf(fmaf(x[2 * c + 1], p.scale_log2, -m), 0.01f, 1.f);
         } else {
-          a = (m == -INFINITY) ? 0.f : exp2f(x[2 * c] - m);
-          bb = (m == -INFINITY) ? 0.f : exp2f(x[2 * c + 1] - m);
+          a = (m == -INFINITY) ? 0.f : exp2f(fmaf(x[2 * c], p.scale_log2, -m));
+          bb = (m == -INFINITY) ? 0.f : exp2f(fmaf(x[2 * c + 1], p.scale_log2, -m));
         }
         rs += a + bb;
-        pk[c] = pack_bf16x2(a, bb);
+        pk[c] = pack_bf16x2_int(a, bb);
       }
       l += rs;
       FA_STAMP(6)
@@ -379,8 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && n > 0) {
       s.lsum[half][r] = l;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.mx_full);
-      ok = mbar_wait_warp(&s.mx_full, n & 1, p.status, kStatusTimeoutAttention, abort_flag);
+      if (lane == 0) mbar_arrive(&s.mx_full[q]);
+      ok = mbar_wait_warp(&s.mx_full[q], n & 1, p.status, kStatusTimeoutAttention, abort_flag);
       if (ok) l += s.lsum[half ^ 1][r];
     }
     ok = __all_sync(0xffffffffu, ok);

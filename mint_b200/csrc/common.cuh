@@ -502,6 +502,14 @@ __device__ __forceinline__ float exp2_poly(float t) {
   return t >= -125.f ? __int_as_float(bits) : (t < -125.f ? 0.f : t);
 }
 
+// Two finite floats to bf16x2 on the integer pipe: adding half a bf16 ulp (0x8000) to the
+// sign-magnitude bit pattern and keeping the upper halves rounds the magnitude to nearest, ties
+// away from zero (a carry into the exponent is the correct round-up); one PRMT packs both. Keeps the
+// conversion off the pipe the exponentials use. Not for NaN / Inf inputs.
+__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -663,6 +663,14 @@ __device__ __forceinline__ void stage_store_bf16(const CUtensorMap* map, const f
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// tanh as the single-instruction hardware approximation (relative error ~2^-11, far below the bf16
+// rounding of the values it feeds)
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Forward (COMM 3): the pair's B rows are fc1 rows [tn * BN/2, +BN/2) (leader) and fc2 rows
 // [F + tn * BN/2, +BN/2) (follower), so accumulator columns [0, BN/2) hold a and [BN/2, BN) hold
 // the matching b. The epilogue stores a and b into their places of ab [M, 2F] (kept for the
@@ -670,11 +678,12 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 // values a separate GeGLU pass over the stored ab would read).
 template <int BN>
 __device__ __forceinline__ void epilogue_tile_geglu_fwd(const Params& p, const CommParams& c, const CUtensorMap* tmc,
-                                                        uint32_t tmem_acc, int row0, int tn, uint8_t* bufs, int lane,
-                                                        int& seq) {
+                                                        uint32_t tmem_acc, int row0, int tn, int half, uint8_t* bufs,
+                                                        int lane, int& seq) {
+  static_assert(BN == 256, "two epilogue warps per lane quadrant take one 64-column group of a each");
   const int F = c.geglu_f;
-#pragma unroll 1
-  for (int g = 0; g < BN / 128; ++g) {
+  {
+    const int g = half;
     uint32_t ra[2][32], rb[2][32];
     tmem_ld_32x32b_x32(tmem_acc + g * 64, ra[0]);
     tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, ra[1]);
@@ -682,7 +691,7 @@ __device__ __forceinline__ void epilogue_tile_geglu_fwd(const Params& p, const C
     tmem_ld_32x32b_x32(tmem_acc + BN / 2 + g * 64 + 32, rb[1]);
     tmem_ld_wait();
     const int col0 = tn * (BN / 2) + g * 64;
-    if (col0 >= F || row0 >= p.M || (p.diag & 1)) continue;  // warp-uniform
+    if (col0 >= F || row0 >= p.M || (p.diag & 1)) return;  // warp-uniform
     float v[64];
 #pragma unroll
     for (int j = 0; j < 64; ++j) v[j] = bf16_round(__uint_as_float(ra[j >> 5][j & 31]));
@@ -692,7 +701,7 @@ __device__ __forceinline__ void epilogue_tile_geglu_fwd(const Params& p, const C
       const float b = bf16_round(__uint_as_float(rb[j >> 5][j & 31]));
       const float a = v[j];
       v[j] = b;
-      ra[j >> 5][j & 31] = __float_as_uint(0.5f * a * (1.f + tanhf(kGeluK0 * (a + kGeluK1 * a * a * a))) * b);
+      ra[j >> 5][j & 31] = __float_as_uint(0.5f * a * (1.f + tanh_hw(kGeluK0 * (a + kGeluK1 * a * a * a))) * b);
     }
     stage_store_bf16(tmc, v, bufs, lane, seq, F + col0, row0);
 #pragma unroll
@@ -712,7 +721,7 @@ __device__ __forceinline__ void epilogue_tile_geglu_bwd(const Params& p, const C
   const int F = c.geglu_f;
   const int row = row0 + lane;
 #pragma unroll 1
-  for (int g = 0; g < BN / 64; ++g) {
+  for (int g = 0; g < BN / 128; ++g) {  // this warp's half of the tile's columns
     const int col0 = col_base + g * 64;
     uint4 ua[8], ub[8];
     const bool live = col0 < F && row0 < p.M && !(p.diag & 1);  // warp-uniform
@@ -754,7 +763,7 @@ __device__ __forceinline__ void epilogue_tile_geglu_bwd(const Params& p, const C
           const int k = 8 * j + 2 * e + z;
           const float x = av[z];
           const float gr = bf16_round(__uint_as_float(r[k >> 5][k & 31]));
-          const float t = tanhf(kGeluK0 * (x + kGeluK1 * x * x * x));
+          const float t = tanh_hw(kGeluK0 * (x + kGeluK1 * x * x * x));
           const float gelu = 0.5f * x * (1.f + t);
           const float dgelu = 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * kGeluK0 * (1.f + 3.f * kGeluK1 * x * x);
           da[z] = gr * bv[z] * dgelu;
@@ -790,17 +799,18 @@ constexpr int kAgPieces = 8;  // a 128-row block is copied as 8 pieces of 16 row
 // Barriers: full[s] and tempty[] live in the leader (the follower's TMA completes bytes on the
 // leader's full[s]; both epilogues arrive on the leader's tempty[]); empty[s] and tfull[] live in
 // both CTAs and the leader's MMA thread commits to each explicitly.
-template <int BN>
+template <int BN, int EPI = 4>
 struct Cfg2 {
-  static constexpr int kStages = 6;                  // 192 KB of operands in flight per SM
+  static constexpr int kStages = EPI == 8 ? 5 : 6;   // 192 KB of operands in flight per SM (160 with 8 epilogue warps)
   static constexpr int kABytes = 128 * BK * 2;       // this CTA's 128 rows of A
   static constexpr int kBBytes = (BN / 2) * BK * 2;  // this CTA's BN/2 rows of B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 1024;  // barriers, TMEM slot, abort flag; bytes 256..767 RS flag queues
   // epilogue warps: 4 (one per TMEM lane quadrant) or 8 (two per quadrant, half the columns each);
-  // measured alike, so the shared memory goes to a sixth operand stage instead
-  static constexpr int kEpiWarps = 4;
+  // measured alike for plain epilogues, so those keep a sixth operand stage; the GeGLU epilogues
+  // (transcendentals per element) use 8
+  static constexpr int kEpiWarps = EPI;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
   static constexpr int kCopyWarps = 2;  // all-gather mode: warps pulling peers' rows
   static constexpr int kStagingBytes = kEpiWarps * 2 * 4096;
@@ -808,16 +818,22 @@ struct Cfg2 {
   static_assert(kSmemBytes <= 232448, "shared-memory layout exceeds the per-block opt-in limit");
 };
 
+template <int COMM>
+constexpr int pair_epi_warps() {
+  return (COMM == 3 || COMM == 4) ? 8 : 4;
+}
+
 template <int BN, int COMM>
 constexpr int pair_threads() {
-  return Cfg2<BN>::kThreads + (COMM == 1 ? Cfg2<BN>::kCopyWarps * 32 : 0);
+  using C_ = Cfg2<BN, pair_epi_warps<COMM>()>;
+  return C_::kThreads + (COMM == 1 ? C_::kCopyWarps * 32 : 0);
 }
 
 template <int BN, bool A_MN, bool B_MN, int COMM>
 __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                      const __grid_constant__ CUtensorMap tmc, Params p, const __grid_constant__ CommParams c) {
-  using C_ = Cfg2<BN>;
+  using C_ = Cfg2<BN, pair_epi_warps<COMM>()>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -1071,9 +1087,10 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
       if constexpr (COMM == 3 || COMM == 4) {
         const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
         if constexpr (COMM == 3) {
-          epilogue_tile_geglu_fwd<BN>(p, c, &tmc, tacc, row0, tn, bufs, lane, seq);
+          epilogue_tile_geglu_fwd<BN>(p, c, &tmc, tacc, row0, tn, half, bufs, lane, seq);
         } else {
-          epilogue_tile_geglu_bwd<BN>(p, c, &tmc, tacc, row0, tn * BN, bufs, lane, seq);
+          epilogue_tile_geglu_bwd<BN>(p, c, &tmc, tacc + half * kCols, row0, tn * BN + half * kCols, bufs, lane,
+                                      seq);
         }
         tc_fence_before();
         __syncwarp();
@@ -1103,7 +1120,7 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
 template <int BN, bool A_MN, bool B_MN, int COMM = 0>
 void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p, int sms,
                  cudaStream_t stream, const CommParams& comm = CommParams{}) {
-  using C_ = Cfg2<BN>;
+  using C_ = Cfg2<BN, pair_epi_warps<COMM>()>;
   auto kern = gemm_pair_kernel<BN, A_MN, B_MN, COMM>;
   static bool configured[64] = {};
   int dev = 0;
