@@ -676,14 +676,17 @@ __device__ __forceinline__ float tanh_hw(float x) {
 // the matching b. The epilogue stores a and b into their places of ab [M, 2F] (kept for the
 // backward) and h = gelu_tanh(a) * b into h [M, F], from the bf16-rounded a and b (the same
 // values a separate GeGLU pass over the stored ab would read).
-template <int BN>
+template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile_geglu_fwd(const Params& p, const CommParams& c, const CUtensorMap* tmc,
                                                         uint32_t tmem_acc, int row0, int tn, int half, uint8_t* bufs,
                                                         int lane, int& seq) {
-  static_assert(BN == 256, "two epilogue warps per lane quadrant take one 64-column group of a each");
+  // EPI 4: one warp per lane quadrant takes every 64-column group of a; EPI 8: two warps, one group each
+  static_assert(BN == 256 && (EPI == 4 || EPI == 8), "GeGLU forward epilogue layout");
   const int F = c.geglu_f;
-  {
-    const int g = half;
+  constexpr int kGroups = EPI == 4 ? BN / 128 : 1;
+#pragma unroll 1
+  for (int gi = 0; gi < kGroups; ++gi) {
+    const int g = EPI == 4 ? gi : half;
     uint32_t ra[2][32], rb[2][32];
     tmem_ld_32x32b_x32(tmem_acc + g * 64, ra[0]);
     tmem_ld_32x32b_x32(tmem_acc + g * 64 + 32, ra[1]);
@@ -691,7 +694,7 @@ __device__ __forceinline__ void epilogue_tile_geglu_fwd(const Params& p, const C
     tmem_ld_32x32b_x32(tmem_acc + BN / 2 + g * 64 + 32, rb[1]);
     tmem_ld_wait();
     const int col0 = tn * (BN / 2) + g * 64;
-    if (col0 >= F || row0 >= p.M || (p.diag & 1)) return;  // warp-uniform
+    if (col0 >= F || row0 >= p.M || (p.diag & 1)) continue;  // warp-uniform
     float v[64];
 #pragma unroll
     for (int j = 0; j < 64; ++j) v[j] = bf16_round(__uint_as_float(ra[j >> 5][j & 31]));
@@ -808,8 +811,8 @@ struct Cfg2 {
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 1024;  // barriers, TMEM slot, abort flag; bytes 256..767 RS flag queues
   // epilogue warps: 4 (one per TMEM lane quadrant) or 8 (two per quadrant, half the columns each);
-  // measured alike for plain epilogues, so those keep a sixth operand stage; the GeGLU epilogues
-  // (transcendentals per element) use 8
+  // measured alike for plain epilogues, so those keep a sixth operand stage; the GeGLU backward
+  // epilogue (two global loads and a transcendental per element) uses 8
   static constexpr int kEpiWarps = EPI;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
   static constexpr int kCopyWarps = 2;  // all-gather mode: warps pulling peers' rows
@@ -820,7 +823,7 @@ struct Cfg2 {
 
 template <int COMM>
 constexpr int pair_epi_warps() {
-  return (COMM == 3 || COMM == 4) ? 8 : 4;
+  return COMM == 4 ? 8 : 4;  // the GeGLU backward epilogue (loads + transcendentals) gets two warps per quadrant
 }
 
 template <int BN, int COMM>
@@ -1087,7 +1090,7 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
       if constexpr (COMM == 3 || COMM == 4) {
         const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
         if constexpr (COMM == 3) {
-          epilogue_tile_geglu_fwd<BN>(p, c, &tmc, tacc, row0, tn, half, bufs, lane, seq);
+          epilogue_tile_geglu_fwd<BN, C_::kEpiWarps>(p, c, &tmc, tacc, row0, tn, half, bufs, lane, seq);
         } else {
           epilogue_tile_geglu_bwd<BN>(p, c, &tmc, tacc + half * kCols, row0, tn * BN + half * kCols, bufs, lane,
                                       seq);

@@ -11,6 +11,8 @@ the fc3 input-gradient GEMM's epilogue turns ``dh`` into ``dab`` without ``dh`` 
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F  # noqa: N812
 
@@ -42,6 +44,11 @@ def geglu(ab: torch.Tensor) -> torch.Tensor:
     return F.gelu(a, approximate="tanh") * b
 
 
+# The backward's fused form (GeGLU backward inside the fc3 input-gradient GEMM) moves the same bytes
+# as the separate kernel but inside a compute-bound GEMM's epilogue; MINT_GEGLU_BWD_FUSED selects it.
+_FUSED_BWD = os.environ.get("MINT_GEGLU_BWD_FUSED", "1") == "1"
+
+
 class _GeGLUMLPFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, dtype, w1, w2, w3):  # noqa: ANN001, ANN205
@@ -71,8 +78,11 @@ class _GeGLUMLPFn(torch.autograd.Function):
         if dy2.dtype != dtype or not dy2.is_contiguous():
             dy2 = dy2.to(dtype).contiguous()
         (dw3,) = weight_grads((w3,), [ctx.needs_input_grad[4]], dy2, h)
-        dab = torch.empty_like(ab)
-        C.gemm_geglu_bwd(dy2, _cast_weight((w3,), dtype), ab, dab)
+        if _FUSED_BWD:
+            dab = torch.empty_like(ab)
+            C.gemm_geglu_bwd(dy2, _cast_weight((w3,), dtype), ab, dab)
+        else:  # fc3 input-gradient GEMM, then the GeGLU backward kernel
+            dab = C.geglu_bwd(matmul(dy2, _cast_weight((w3,), dtype), out_dtype=dtype), ab)
         dx = None
         if ctx.needs_input_grad[0]:
             dx = matmul(dab, _cast_weight((w1, w2), dtype), out_dtype=dtype).view(ctx.x_shape)
