@@ -119,6 +119,23 @@ def run_attn(a: argparse.Namespace) -> dict:
         out["mma_wait_p"] = statistics.median(r[2] - r[1] for r in mrows)
         out["mma_issue_pv"] = statistics.median(r[3] - r[2] for r in mrows)
         print(json.dumps({"fa_fwd_trace_cycles": out, "tiles": n}), flush=True)
+        for _ in range(3):
+            C.flash_attn_bwd(do, q, k, v, o, lse, doc, causal, a.window, scale, *extra)
+        torch.cuda.synchronize()
+        tr = C.flash_attn_bwd_trace().view(-1).tolist()
+        steps = 12
+        nb = min(tiles, (T + 127) // 128) * (Hq // Hkv)
+        bnames = ["stage_lse", "s_wait", "s_load", "mask_exp", "p_store_arrive", "dp_wait", "dp_load_ds",
+                  "dv_wait", "ds_store_arrive", "dq_wait", "dq_drain"]
+        rows = [tr[t * steps: (t + 1) * steps] for t in range(nb)]
+        outb = {nm: statistics.median(r[i + 1] - r[i] for r in rows) for i, nm in enumerate(bnames)}
+        outb["tile"] = statistics.median(rows[t + 1][0] - rows[t][0] for t in range(nb - 1))
+        mb = tiles * steps
+        mrows = [tr[mb + t * 4: mb + t * 4 + 4] for t in range(nb - 1)]
+        outb["mma_wait_p"] = statistics.median(r[1] - r[0] for r in mrows)
+        outb["mma_dv_s_wait_ds"] = statistics.median(r[2] - r[1] for r in mrows)
+        outb["mma_dkdq_wait_dqfree"] = statistics.median(r[3] - r[2] for r in mrows)
+        print(json.dumps({"fa_bwd_trace_cycles": outb, "tiles": nb}), flush=True)
     if a.once:
         C.flash_attn_bwd(do, q, k, v, o, lse, doc, causal, a.window, scale, *extra)
         torch.cuda.synchronize()

@@ -51,7 +51,13 @@ struct BwdParams {
   int causal, window;
   float scale, scale_log2;
   uint32_t* status;
+  // MINT_FA_TRACE=1: clock64 stamps of block (0, 0, 0) -- key tile 0, the one with the most query
+  // tiles under a causal mask -- for the first kTraceTiles query tiles: [tile][kTraceSteps] from
+  // lane 0 of math warp 4, then [tile][4] from the MMA thread (diagnostics only; null otherwise)
+  unsigned long long* trace;
 };
+constexpr int kTraceTiles = 64;
+constexpr int kTraceSteps = 12;
 
 struct Smem {
   uint8_t k[kTileBytes];
@@ -223,11 +229,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_kk(t_dp, a_v, smem_u32(s.dout[0]), false);  // dP^T_0 = V dO_0^T
         umma_commit(&s.dp_full);
       }
+      unsigned long long* tr = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+                                   ? p.trace + kTraceTiles * kTraceSteps
+                                   : nullptr;
       for (int it = 0; it < n && ok; ++it) {
         const int st = it & 1;
         const uint32_t ph = it & 1;
         const uint32_t a_q = smem_u32(s.q[st]), a_do = smem_u32(s.dout[st]);
+        if (tr != nullptr && it < kTraceTiles) tr[it * 4] = clock64();
         if (!(ok = mbar_wait(&s.p_ready, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+        if (tr != nullptr && it < kTraceTiles) tr[it * 4 + 1] = clock64();
         tc_fence_after();
         mma_kmn(t_dv, a_pds, a_do, it > 0);  // dV += P^T dO
         umma_commit(&s.dv_done);
@@ -241,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&s.s_full);
         }
         if (!(ok = mbar_wait(&s.ds_ready, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+        if (tr != nullptr && it < kTraceTiles) tr[it * 4 + 2] = clock64();
         tc_fence_after();
         mma_kmn(t_dk, a_pds, a_q, it > 0);  // dK += dS^T Q
         mma_mnmn(t_dq, a_pds, a_k, false);  // dQ_i = dS K (dP^T_i was consumed before ds_ready_i)
@@ -252,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t pn = ((it + 1) >> 1) & 1;
           if (!(ok = mbar_wait(&s.do_full[sn], pn, p.status, kStatusTimeoutAttention, abort_flag))) break;
           if (!(ok = mbar_wait(&s.dq_free, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+          if (tr != nullptr && it < kTraceTiles) tr[it * 4 + 3] = clock64();
           tc_fence_after();
           mma_kk(t_dp, a_v, smem_u32(s.dout[sn]), false);  // dP^T_{i+1}
           umma_commit(&s.dp_full);
@@ -282,7 +295,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       return qi < p.T ? p.delta[rowbase + qi] : 0.f;
     };
     float staged = n > 0 ? stage_value(0) : 0.f;
+    unsigned long long* tr = (p.trace != nullptr && lane == 0 && warp == 4 && blockIdx.x == 0 && blockIdx.y == 0 &&
+                              blockIdx.z == 0)
+                                 ? p.trace
+                                 : nullptr;
+#define FAB_STAMP(k) \
+  if (tr != nullptr && it < kTraceTiles) tr[it * kTraceSteps + (k)] = clock64();
     for (int it = 0; it < n && ok; ++it) {
+      FAB_STAMP(0)
       const uint32_t ph = it & 1;
       const int h = hk * G + it / nq;
       const int q0 = (i0 + it % nq) * kB;
@@ -298,12 +318,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.stg_full);
       if (!(ok = mbar_wait_warp(&s.stg_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      FAB_STAMP(1)
       const float* lse2 = s.lse2 + cb;
       const float* dlt = s.dlt + cb;
       if (!(ok = mbar_wait_warp(&s.s_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      FAB_STAMP(2)
       tc_fence_after();
       float x[64];
       load_row64(t_s + lane_off + cb, x);
+      FAB_STAMP(3)
       const int lo_i = min(k0, q0), hi_i = max(k_last, q_last);
       const bool doc_mask = p.doc != nullptr && !(doc_sorted && db[lo_i].y > hi_i);
       const bool need_mask = (p.causal && k0 + kB - 1 > q0) || (p.window >= 0 && q0 + kB - 1 - k0 > p.window) ||
@@ -327,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           x[c] = (c & 1) ? exp2_poly(t) : exp2f(t);
         }
       }
+      FAB_STAMP(4)
       // the shared P/dS tile is free: dK_{i-1} / dQ_{i-1} (dq_full_{i-1}) finished reading dS_{i-1}, and
       // this warp's dQ_{i-1} reduce-adds (staged in the same bytes it now writes) read their source
       if (lane == 0) bulk_wait_read<0>();
@@ -336,7 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.p_ready);
+      FAB_STAMP(5)
       if (!(ok = mbar_wait_warp(&s.dp_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      FAB_STAMP(6)
       tc_fence_after();
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {
@@ -351,14 +377,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.stg_free);  // this warp's last read of lse2 / dlt for the tile
+      FAB_STAMP(7)
       // dS overwrites P only after dV has consumed it
       if (!(ok = mbar_wait_warp(&s.dv_done, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      FAB_STAMP(8)
       store_half_row_sw128(s.pds, half, r, x);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.ds_ready);
+      FAB_STAMP(9)
       if (!(ok = mbar_wait_warp(&s.dq_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      FAB_STAMP(10)
       tc_fence_after();
       // dQ rows: TMEM lane = query index within the tile; this warp drains 64 of the 128 head dims.
       // The P/dS tile is free now (the dK / dQ MMAs that read dS completed): each warp stages its
@@ -388,7 +418,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.dq_free);
+      FAB_STAMP(11)
     }
+#undef FAB_STAMP
     // the dQ reductions have read their shared-memory sources before it is released (their global
     // writes complete with the grid, before any later kernel on the stream reads dQ)
     if (lane == 0) bulk_wait_read<0>();
@@ -482,6 +514,17 @@ static CUtensorMap dq_acc_map(float* dq_acc, int B, int T, int Hq) {
   return make_tmap_4d(dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// MINT_FA_TRACE=1 diagnostics: the stamp buffer of the last backward (zeros if tracing is off)
+at::Tensor& fab_trace_buffer() {
+  static at::Tensor buf;
+  return buf;
+}
+
+at::Tensor flash_attn_bwd_trace() {
+  at::Tensor& buf = fab_trace_buffer();
+  return buf.defined() ? buf.clone() : at::zeros({(fab::kTraceSteps + 4) * fab::kTraceTiles}, at::kLong);
+}
+
 std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
@@ -532,6 +575,14 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   p.scale = static_cast<float>(scale);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.status = status_ptr(q.get_device());
+  static const bool fa_trace = std::getenv("MINT_FA_TRACE") != nullptr;
+  if (fa_trace) {
+    at::Tensor& buf = fab_trace_buffer();
+    if (!buf.defined() || buf.device() != q.device()) {
+      buf = at::zeros({(fab::kTraceSteps + 4) * fab::kTraceTiles}, q.options().dtype(at::kLong));
+    }
+    p.trace = reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>());
+  }
   auto map = [&](const at::Tensor& t, int H) {
     return make_tmap_3d_bf16(t.data_ptr(), fab::kD, H, static_cast<uint64_t>(B) * T, fab::kD,
                              static_cast<uint64_t>(H) * fab::kD, 64, 1, 128, true);

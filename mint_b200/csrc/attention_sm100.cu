@@ -112,6 +112,9 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_addr, uint3
   }
 }
 
+// POLY: a quarter of the exponentials (the second of every other pair) run as the FMA-pipe
+// polynomial exp2_poly instead of on the MUFU unit, which the exponentials otherwise saturate
+template <bool POLY>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, FwdParams p) {
@@ -346,8 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           a = (m == -INFINITY) ? 0.f : fmaf(fmaf(x[2 * c], p.scale_log2, -m), 0.01f, 1.f);
           bb = (m == -INFINITY) ? 0.f : fmaf(fmaf(x[2 * c + 1], p.scale_log2, -m), 0.01f, 1.f);
         } else {
-          a = (m == -INFINITY) ? 0.f : exp2f(fmaf(x[2 * c], p.scale_log2, -m));
-          bb = (m == -INFINITY) ? 0.f : exp2f(fmaf(x[2 * c + 1], p.scale_log2, -m));
+          const float ta = fmaf(x[2 * c], p.scale_log2, -m), tb = fmaf(x[2 * c + 1], p.scale_log2, -m);
+          a = (m == -INFINITY) ? 0.f : exp2f(ta);
+          bb = (m == -INFINITY) ? 0.f : ((POLY && (c & 1)) ? exp2_poly(tb) : exp2f(tb));
         }
         rs += a + bb;
         pk[c] = pack_bf16x2_int(a, bb);
@@ -577,16 +581,22 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k,
   const int smem = static_cast<int>(sizeof(fa::Smem)) + 1024;
   static bool configured[64] = {};  // the attribute is per device
   const int dev = q.get_device();
+  // MINT_FA_POLY=1: a quarter of the exponentials on the FMA pipe (A/B switch)
+  static const bool poly = [] {
+    const char* e = std::getenv("MINT_FA_POLY");
+    return e != nullptr && e[0] == '1';
+  }();
+  auto kern = poly ? fa::fa_fwd_kernel<true> : fa::fa_fwd_kernel<false>;
   if (!configured[dev & 63]) {
     check_smem_optin(smem, dev, "fa_fwd_kernel");
-    MINT_CUDA_CHECK(cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev & 63] = true;
   }
   dim3 grid((T + fa::kBM - 1) / fa::kBM, Hq, B);
   // O leaves in 32-row x 64-dim boxes, one TMA store per softmax warp
   const CUtensorMap to = make_tmap_3d_bf16(o.data_ptr(), fa::kD, Hq, static_cast<uint64_t>(B) * T, fa::kD,
                                            static_cast<uint64_t>(Hq) * fa::kD, 64, 1, 32, true);
-  fa::fa_fwd_kernel<<<grid, fa::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, to, p);
+  kern<<<grid, fa::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, to, p);
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
   return {o, lse};

@@ -62,6 +62,7 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                                        double scale, const c10::optional<at::Tensor>& dbounds);
 at::Tensor doc_bounds(const at::Tensor& doc);
 at::Tensor flash_attn_fwd_trace();
+at::Tensor flash_attn_bwd_trace();
 void zero_reduce_scatter(const std::vector<int64_t>& bucket_ptrs, at::Tensor& shard, double scale,
                          const c10::optional<at::Tensor>& sumsq, const std::vector<int64_t>& flag_ptrs,
                          const at::Tensor& flags_local, int64_t rank, int64_t world, int64_t seq);
@@ -183,5 +184,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("zero_barrier", &mint::zero_barrier, "stream-ordered barrier of a ZeRO group over NVLink peer flags");
   m.def("flash_attn_fwd_trace", &mint::flash_attn_fwd_trace,
         "MINT_FA_TRACE=1 diagnostics: clock64 stamps of the last forward's longest query tile");
+  m.def("flash_attn_bwd_trace", &mint::flash_attn_bwd_trace,
+        "MINT_FA_TRACE=1 diagnostics: clock64 stamps of the last backward's key tile 0");
   m.def("doc_bounds", &mint::doc_bounds, "[B, T, 2] int32 document run [start, end) of every token");
 }
