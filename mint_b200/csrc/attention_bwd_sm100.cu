@@ -115,6 +115,15 @@ __device__ __forceinline__ void store_half_row_sw128(uint8_t* tile, int a, int r
   }
 }
 
+// 64 columns (one swizzle atom `a`) of row r of a K-major 128B-swizzled bf16 tile, already packed
+__device__ __forceinline__ void store_half_row_packed(uint8_t* tile, int a, int r, const uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    *reinterpret_cast<uint4*>(tile + a * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) =
+        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+  }
+}
+
 __device__ __forceinline__ void load_row64(uint32_t taddr, float (&x)[64]) {
   uint32_t u0[32], u1[32];  // both loads in flight under one wait
   tmem_ld_32x32b_x32(taddr, u0);
@@ -339,15 +348,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.causal) keep = keep && kj <= qi;
           if (p.window >= 0) keep = keep && qi - kj <= p.window;
           if (p.doc != nullptr && !doc_sorted && keep) keep = p.doc[static_cast<long long>(b) * p.T + qi] == doc_k;
-          const float t = fmaf(x[c], p.scale_log2, -lse2[c]);
-          x[c] = keep ? ((c & 1) ? exp2_poly(t) : exp2f(t)) : 0.f;
+          if (!keep) x[c] = -INFINITY;
         }
-      } else {
+      }
+      // P^T = exp2(S^T * scale - lse), two elements per instruction (packed fp32 FMA, bf16x2 MUFU
+      // exponential straight into the bf16 operand layout); masked entries give 2^-inf = 0
+      uint32_t pk[32];
+      {
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          // half of the exponentials on the MUFU unit, half as a polynomial on the FMA pipe
-          const float t = fmaf(x[c], p.scale_log2, -lse2[c]);
-          x[c] = (c & 1) ? exp2_poly(t) : exp2f(t);
+        for (int c = 0; c < 32; ++c) {
+          const float2 l2 = *reinterpret_cast<const float2*>(lse2 + 2 * c);
+          const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, make_float2(-l2.x, -l2.y));
+          pk[c] = ex2_bf16x2(t.x, t.y);
         }
       }
       FAB_STAMP(4)
@@ -355,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this warp's dQ_{i-1} reduce-adds (staged in the same bytes it now writes) read their source
       if (lane == 0) bulk_wait_read<0>();
       __syncwarp();
-      store_half_row_sw128(s.pds, half, r, x);
+      store_half_row_packed(s.pds, half, r, pk);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -364,15 +377,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait_warp(&s.dp_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       FAB_STAMP(6)
       tc_fence_after();
-#pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(t_dp + lane_off + cb + c2 * 32, u);
+      // dS^T = P^T (dP^T - delta), in packed fp32 pairs from the bf16 P the dV MMA used
+      {
+        uint32_t u0[32], u1[32];  // both loads in flight under one wait
+        tmem_ld_32x32b_x32(t_dp + lane_off + cb, u0);
+        tmem_ld_32x32b_x32(t_dp + lane_off + cb + 32, u1);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int c = c2 * 32 + e;
-          x[c] = x[c] * (__uint_as_float(u[e]) - dlt[c]);
+        for (int c = 0; c < 32; ++c) {
+          const uint32_t* u = c < 16 ? u0 : u1;
+          const int e = (2 * c) & 31;
+          const float2 d2 = *reinterpret_cast<const float2*>(dlt + 2 * c);
+          const float2 g = fadd2(make_float2(__uint_as_float(u[e]), __uint_as_float(u[e + 1])),
+                                 make_float2(-d2.x, -d2.y));
+          const float2 ds = fmul2(bf16x2_to_float2(pk[c]), g);
+          pk[c] = pack_bf16x2(ds.x, ds.y);
         }
       }
       __syncwarp();
@@ -381,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // dS overwrites P only after dV has consumed it
       if (!(ok = mbar_wait_warp(&s.dv_done, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       FAB_STAMP(8)
-      store_half_row_sw128(s.pds, half, r, x);
+      store_half_row_packed(s.pds, half, r, pk);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();

@@ -112,9 +112,6 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_addr, uint3
   }
 }
 
-// POLY: a quarter of the exponentials (the second of every other pair) run as the FMA-pipe
-// polynomial exp2_poly instead of on the MUFU unit, which the exponentials otherwise saturate
-template <bool POLY>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, FwdParams p) {
@@ -292,9 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       FA_STAMP(2)
-      float mt = -INFINITY;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
-      for (int c = 0; c < 64; ++c) mt = fmaxf(mt, x[c]);
+      for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+      float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       FA_STAMP(3)
       // combine with the other half of the row; the buffer of this parity was last read two tiles
       // ago, before every softmax warp arrived on the previous tile's exchange
@@ -339,22 +337,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;  // nothing accumulated in this row yet
       }
       FA_STAMP(5)
-      // P = exp2(x - m) in bf16, this half's row sum in fp32
+      // P = exp2(x * scale - m) in bf16, two elements per instruction (packed fp32 FMA, bf16x2 MUFU
+      // exponential); the row sum adds the bf16 values the PV MMA uses. A row with nothing kept yet
+      // (m = -inf) has every x = -inf, so m is taken as 0 there and every p comes out 0.
       uint32_t pk[32];
       float rs = 0.f;
+      {
+        const float mm = (m == -INFINITY) ? 0.f : m;
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-mm, -mm);
+        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // two chains for ILP
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        float a, bb;
-        if (p.diag & 1) {
-          a = (m == -INFINITY) ? 0.f : fmaf(fmaf(x[2 * c], p.scale_log2, -m), 0.01f, 1.f);
-          bb = (m == -INFINITY) ? 0.f : fmaf(fmaf(x[2 * c + 1], p.scale_log2, -m), 0.01f, 1.f);
-        } else {
-          const float ta = fmaf(x[2 * c], p.scale_log2, -m), tb = fmaf(x[2 * c + 1], p.scale_log2, -m);
-          a = (m == -INFINITY) ? 0.f : exp2f(ta);
-          bb = (m == -INFINITY) ? 0.f : ((POLY && (c & 1)) ? exp2_poly(tb) : exp2f(tb));
+        for (int c = 0; c < 32; ++c) {
+          const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, nm2);
+          uint32_t e;
+          if (p.diag & 1) {
+            e = pack_bf16x2(fmaf(t.x, 0.01f, 1.f), fmaf(t.y, 0.01f, 1.f));
+          } else {
+            e = ex2_bf16x2(t.x, t.y);
+          }
+          pk[c] = e;
+          acc2[c & 1] = fadd2(acc2[c & 1], bf16x2_to_float2(e));
         }
-        rs += a + bb;
-        pk[c] = pack_bf16x2_int(a, bb);
+        rs = (acc2[0].x + acc2[1].x) + (acc2[0].y + acc2[1].y);
       }
       l += rs;
       FA_STAMP(6)
@@ -581,12 +585,7 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k,
   const int smem = static_cast<int>(sizeof(fa::Smem)) + 1024;
   static bool configured[64] = {};  // the attribute is per device
   const int dev = q.get_device();
-  // MINT_FA_POLY=1: a quarter of the exponentials on the FMA pipe (A/B switch)
-  static const bool poly = [] {
-    const char* e = std::getenv("MINT_FA_POLY");
-    return e != nullptr && e[0] == '1';
-  }();
-  auto kern = poly ? fa::fa_fwd_kernel<true> : fa::fa_fwd_kernel<false>;
+  auto kern = fa::fa_fwd_kernel;
   if (!configured[dev & 63]) {
     check_smem_optin(smem, dev, "fa_fwd_kernel");
     MINT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));

@@ -61,6 +61,8 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                                        const c10::optional<at::Tensor>& doc, bool causal, int64_t window,
                                        double scale, const c10::optional<at::Tensor>& dbounds);
 at::Tensor doc_bounds(const at::Tensor& doc);
+at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal,
+                            int64_t window, double scale);
 at::Tensor flash_attn_fwd_trace();
 at::Tensor flash_attn_bwd_trace();
 void zero_reduce_scatter(const std::vector<int64_t>& bucket_ptrs, at::Tensor& shard, double scale,
@@ -186,5 +188,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "MINT_FA_TRACE=1 diagnostics: clock64 stamps of the last forward's longest query tile");
   m.def("flash_attn_bwd_trace", &mint::flash_attn_bwd_trace,
         "MINT_FA_TRACE=1 diagnostics: clock64 stamps of the last backward's key tile 0");
+  m.def("decode_attention", &mint::decode_attention,
+        "split-KV attention of a few query rows against a KV cache prefix (bottom-right causal, window)");
   m.def("doc_bounds", &mint::doc_bounds, "[B, T, 2] int32 document run [start, end) of every token");
 }

@@ -502,6 +502,53 @@ __device__ __forceinline__ float exp2_poly(float t) {
   return t >= -125.f ? __int_as_float(bits) : (t < -125.f ? 0.f : t);
 }
 
+// Packed fp32 pairs (Blackwell f32x2 instructions): one instruction for two lanes' worth of math.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rc, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+      "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "mul.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^t for two arguments in one MUFU operation at bf16 precision: the arguments are rounded to bf16
+// (one conversion instruction), the results come back packed as bf16x2 (lo in the low half), ready
+// for a bf16 MMA operand. 2^-inf = +0. For softmax probabilities (t <= 0) the argument rounding
+// costs at most ~0.2 % of p near p = 1/2 and less elsewhere -- the size of the bf16 rounding of p.
+__device__ __forceinline__ uint32_t ex2_bf16x2(float lo, float hi) {
+  uint32_t in, out;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(hi), "f"(lo));
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(out) : "r"(in));
+  return out;
+}
+
+// exact widening of a bf16x2 word to two floats
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
 // Two finite floats to bf16x2 on the integer pipe: adding half a bf16 ulp (0x8000) to the
 // sign-magnitude bit pattern and keeping the upper halves rounds the magnitude to nearest, ties
 // away from zero (a carry into the exponent is the correct round-up); one PRMT packs both. Keeps the

@@ -123,6 +123,19 @@ def _kernel_supported(q: torch.Tensor, k: torch.Tensor) -> bool:
     )
 
 
+def _decode_supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
+    """Decoding against a KV cache (fewer query than key rows, at most 16 query rows per KV head):
+    the split-KV decode kernel, which reads the cache prefix in place (rows contiguous)."""
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        return False
+    if q.shape[-1] != 128 or k.shape[-1] != 128 or q.shape[1] >= k.shape[1] or q.shape[2] % k.shape[2]:
+        return False
+    if (q.shape[2] // k.shape[2]) * q.shape[1] > 16 or k.stride() != v.stride():
+        return False
+    return k.stride(3) == 1 and k.stride(2) == 128 and k.stride(1) == k.shape[2] * 128 and hasattr(
+        _ext.require(), "decode_attention")
+
+
 def attention(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -146,6 +159,15 @@ def attention(
         d, bounds = _doc_inputs(doc_ids)
         return _FlashAttnFn.apply(q.contiguous(), k.contiguous(), v.contiguous(), causal, window_left, d, scale,
                                   bounds)
+    if (
+        _ext.use_cuda_kernels(q)
+        and attn_mask is None
+        and bias is None
+        and doc_ids is None
+        and _decode_supported(q, k, v)
+        and not (torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad))
+    ):
+        return _ext.require().decode_attention(q.contiguous(), k, v, bool(causal), int(window_left), float(scale))
     if q.is_cuda and _ext.kernels_enabled():
         if attn_mask is not None or bias is not None:
             _ext.fallback("attention", "explicit mask or bias")

@@ -191,11 +191,15 @@ def test_gemm_cta_pair_split_k_accumulate():
     assert rel < 1e-4, f"rel err {rel}"
 
 
+@pytest.mark.parametrize("fused_bwd", [False, True])
 @pytest.mark.parametrize("M,d,F", [(1000, 256, 384), (4096, 768, 3072), (300, 128, 128)])
-def test_geglu_mlp_fused(M, d, F):
-    """GeGLU inside the GEMM epilogues (forward: fc1||fc2 GEMM writes ab and h; backward: the fc3
-    input-gradient GEMM writes d[a|b]) against fp32 PyTorch: output and every gradient."""
+def test_geglu_mlp_fused(M, d, F, fused_bwd, monkeypatch):
+    """GeGLU inside the GEMM epilogues (forward: fc1||fc2 GEMM writes ab and h; backward, opt-in:
+    the fc3 input-gradient GEMM writes d[a|b]) against fp32 PyTorch: output and every gradient."""
+    from mint_b200.ops import glu
     from mint_b200.ops.glu import _GeGLUMLPFn, geglu_mlp_fusable
+
+    monkeypatch.setattr(glu, "_FUSED_BWD", fused_bwd)
 
     torch.manual_seed(11)
     x = (torch.randn(M, d, device="cuda") * 0.5).requires_grad_()
