@@ -65,12 +65,8 @@ struct Smem {
   uint8_t q[2][kTileBytes];
   uint8_t dout[2][kTileBytes];
   uint8_t pds[kTileBytes];  // P^T, then dS^T of the same query tile
-  float lse2[kB];           // log2-scaled LSE of the current query tile
-  float dlt[kB];            // delta of the current query tile
   uint64_t kv_full, q_full[2], q_empty[2], do_full[2], do_empty[2];
   uint64_t s_full, dp_full, p_ready, dv_done, ds_ready, dq_full, dq_free, mma_done;
-  uint64_t stg_full;  // the 8 math warps staged this tile's LSE / delta
-  uint64_t stg_free;  // the 8 math warps finished reading them
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -170,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.q_full[i], 1);
       mbar_init(&s.q_empty[i], 1);
       mbar_init(&s.do_full[i], 1);
-      mbar_init(&s.do_empty[i], 1);
+      mbar_init(&s.do_empty[i], 8);  // the math warps, once their dQ staging in it has been read
     }
     mbar_init(&s.s_full, 1);
     mbar_init(&s.dp_full, 1);
@@ -179,8 +175,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&s.ds_ready, 8);
     mbar_init(&s.dq_full, 1);
     mbar_init(&s.dq_free, 8);
-    mbar_init(&s.stg_full, 8);
-    mbar_init(&s.stg_free, 8);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -266,8 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_kmn(t_dk, a_pds, a_q, it > 0);  // dK += dS^T Q
         mma_mnmn(t_dq, a_pds, a_k, false);  // dQ_i = dS K (dP^T_i was consumed before ds_ready_i)
         umma_commit(&s.dq_full);
-        umma_commit(&s.q_empty[st]);
-        umma_commit(&s.do_empty[st]);
+        umma_commit(&s.q_empty[st]);  // dO_i's buffer is released by the math warps (dQ staging)
         if (more) {
           const int sn = (it + 1) & 1;
           const uint32_t pn = ((it + 1) >> 1) & 1;
@@ -288,22 +281,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 4) >> 2;
     const int cb = half * 64;
     const int r = q * 32 + lane;
-    const int mt = (warp - 4) * 32 + lane;  // 0..255 over the math warps
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int kj = k0 + r;
     const int doc_k = (p.doc != nullptr && kj < p.T) ? p.doc[static_cast<long long>(b) * p.T + kj] : 0;
     const int2 dk = (doc_sorted && kj < p.T) ? db[kj] : make_int2(0, p.T);
     bool ok = n > 0;
-    // this thread's LSE (threads 0..127, log2 units) or delta (128..255) value of query tile `it`,
-    // loaded one iteration ahead so the global-memory latency overlaps the previous tile's work
-    auto stage_value = [&](int it) -> float {
-      const int h = hk * G + it / nq;
-      const int qi = (i0 + it % nq) * kB + (mt & (kB - 1));
-      const long long rowbase = (static_cast<long long>(b) * p.Hq + h) * p.T;
-      if (mt < kB) return qi < p.T ? p.lse[rowbase + qi] * 1.4426950408889634f : INFINITY;
-      return qi < p.T ? p.delta[rowbase + qi] : 0.f;
-    };
-    float staged = n > 0 ? stage_value(0) : 0.f;
     unsigned long long* tr = (p.trace != nullptr && lane == 0 && warp == 4 && blockIdx.x == 0 && blockIdx.y == 0 &&
                               blockIdx.z == 0)
                                  ? p.trace
@@ -316,20 +298,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = hk * G + it / nq;
       const int q0 = (i0 + it % nq) * kB;
       const int q_last = min(p.T, q0 + kB) - 1;
-      // stage this query tile's LSE and delta once every math warp is done with the previous tile's
-      if (it > 0 && !(ok = mbar_wait_warp(&s.stg_free, ph ^ 1u, p.status, kStatusTimeoutAttention, abort_flag))) break;
-      if (mt < kB) {
-        s.lse2[mt] = staged;
-      } else {
-        s.dlt[mt - kB] = staged;
-      }
-      if (it + 1 < n) staged = stage_value(it + 1);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.stg_full);
-      if (!(ok = mbar_wait_warp(&s.stg_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
+      // this query tile's LSE (natural log) and delta rows, read straight from global memory (every
+      // lane of a warp reads the same 64 values: broadcast loads, L1-resident after the first warp);
+      // columns past T read the row's last valid value (their probabilities are masked to 0)
+      const long long rowbase = (static_cast<long long>(b) * p.Hq + h) * p.T + q0 + cb;
+      const float* lse_row = p.lse + rowbase;
+      const float* dlt_row = p.delta + rowbase;
+      const bool full_cols = q0 + cb + 64 <= p.T;
+      const int last_col = p.T - 1 - (q0 + cb);
       FAB_STAMP(1)
-      const float* lse2 = s.lse2 + cb;
-      const float* dlt = s.dlt + cb;
       if (!(ok = mbar_wait_warp(&s.s_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       FAB_STAMP(2)
       tc_fence_after();
@@ -356,17 +333,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t pk[32];
       {
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nl2e = make_float2(-1.4426950408889634f, -1.4426950408889634f);
+        if (full_cols) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float2 l2 = *reinterpret_cast<const float2*>(lse2 + 2 * c);
-          const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, make_float2(-l2.x, -l2.y));
-          pk[c] = ex2_bf16x2(t.x, t.y);
+          for (int c = 0; c < 32; ++c) {
+            const float2 l2 = __ldg(reinterpret_cast<const float2*>(lse_row) + c);
+            const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, fmul2(l2, nl2e));
+            pk[c] = ex2_bf16x2(t.x, t.y);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float2 l2 = make_float2(__ldg(lse_row + min(2 * c, last_col)), __ldg(lse_row + min(2 * c + 1, last_col)));
+            const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, fmul2(l2, nl2e));
+            pk[c] = ex2_bf16x2(t.x, t.y);
+          }
         }
       }
       FAB_STAMP(4)
       // the shared P/dS tile is free: dK_{i-1} / dQ_{i-1} (dq_full_{i-1}) finished reading dS_{i-1}, and
-      // this warp's dQ_{i-1} reduce-adds (staged in the same bytes it now writes) read their source
-      if (lane == 0) bulk_wait_read<0>();
+      // this warp's dQ_{i-1} reduce-adds (staged in the same bytes it now writes, and in dO_{i-1}'s
+      // buffer, which is released to the producer here) read their sources
+      if (lane == 0) {
+        bulk_wait_read<0>();
+        if (it > 0) mbar_arrive(&s.do_empty[(it - 1) & 1]);
+      }
       __syncwarp();
       store_half_row_packed(s.pds, half, r, pk);
       fence_proxy_async_smem();
@@ -387,15 +378,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 32; ++c) {
           const uint32_t* u = c < 16 ? u0 : u1;
           const int e = (2 * c) & 31;
-          const float2 d2 = *reinterpret_cast<const float2*>(dlt + 2 * c);
+          const float2 d2 = full_cols ? __ldg(reinterpret_cast<const float2*>(dlt_row) + c)
+                                      : make_float2(__ldg(dlt_row + min(2 * c, last_col)),
+                                                    __ldg(dlt_row + min(2 * c + 1, last_col)));
           const float2 g = fadd2(make_float2(__uint_as_float(u[e]), __uint_as_float(u[e + 1])),
                                  make_float2(-d2.x, -d2.y));
           const float2 ds = fmul2(bf16x2_to_float2(pk[c]), g);
           pk[c] = pack_bf16x2(ds.x, ds.y);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.stg_free);  // this warp's last read of lse2 / dlt for the tile
       FAB_STAMP(7)
       // dS overwrites P only after dV has consumed it
       if (!(ok = mbar_wait_warp(&s.dv_done, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
@@ -410,27 +401,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       FAB_STAMP(10)
       tc_fence_after();
       // dQ rows: TMEM lane = query index within the tile; this warp drains 64 of the 128 head dims.
-      // The P/dS tile is free now (the dK / dQ MMAs that read dS completed): each warp stages its
-      // 32 rows x 32 columns of dQ in its own 4 KB of it (the bytes it writes P rows into) and
-      // reduce-adds them into the fp32 accumulator with one TMA bulk reduction per box.
-      uint8_t* stage = s.pds + (warp - 4) * 4096;
-#pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(t_dq + lane_off + cb + c2 * 32, u);
+      // The P/dS tile and dO_i's buffer are free now (the dK / dQ MMAs that read dS completed, and
+      // before them dV_i, the last reader of dO_i): each warp stages its two 32 rows x 32 columns
+      // boxes of dQ in its own 4 KB of each and reduce-adds them into the fp32 accumulator with one
+      // TMA bulk reduction per box; nothing waits for those reads until the next tile.
+      {
+        uint32_t u0[32], u1[32];  // both loads in flight under one wait
+        tmem_ld_32x32b_x32(t_dq + lane_off + cb, u0);
+        tmem_ld_32x32b_x32(t_dq + lane_off + cb + 32, u1);
         tmem_ld_wait();
-        if (c2 > 0 && lane == 0) bulk_wait_read<0>();  // the first box's reduction read the stage
-        __syncwarp();
+        uint8_t* stage0 = s.pds + (warp - 4) * 4096;
+        uint8_t* stage1 = s.dout[it & 1] + (warp - 4) * 4096;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-              make_float4(__uint_as_float(u[4 * j]) * p.scale, __uint_as_float(u[4 * j + 1]) * p.scale,
-                          __uint_as_float(u[4 * j + 2]) * p.scale, __uint_as_float(u[4 * j + 3]) * p.scale);
+          const int off = lane * 128 + ((j ^ (lane & 7)) << 4);
+          *reinterpret_cast<float4*>(stage0 + off) =
+              make_float4(__uint_as_float(u0[4 * j]) * p.scale, __uint_as_float(u0[4 * j + 1]) * p.scale,
+                          __uint_as_float(u0[4 * j + 2]) * p.scale, __uint_as_float(u0[4 * j + 3]) * p.scale);
+          *reinterpret_cast<float4*>(stage1 + off) =
+              make_float4(__uint_as_float(u1[4 * j]) * p.scale, __uint_as_float(u1[4 * j + 1]) * p.scale,
+                          __uint_as_float(u1[4 * j + 2]) * p.scale, __uint_as_float(u1[4 * j + 3]) * p.scale);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_reduce_add_4d(&tdq, stage, cb + c2 * 32, h, q0 + q * 32, b);  // rows past T are clipped
+          tma_reduce_add_4d(&tdq, stage0, cb, h, q0 + q * 32, b);  // rows past T are clipped
+          tma_reduce_add_4d(&tdq, stage1, cb + 32, h, q0 + q * 32, b);
           bulk_commit();
         }
       }

@@ -29,7 +29,8 @@ def rel(a: torch.Tensor, b: torch.Tensor) -> float:
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
-def train(fused: str, dev: torch.device, level: int = 2) -> dict[str, torch.Tensor]:
+def train(fused: str, dev: torch.device, level: int = 2, matrix_optimizer: str = "muon",
+          losses: list | None = None) -> dict[str, torch.Tensor]:
     from mint_b200.models.gemma import Gemma, GemmaConfig, configure_optimizer
     from mint_b200.optim.muon_adamw import MuonAdamWConfig
     from mint_b200.parallel.api import setup_parallel
@@ -47,7 +48,8 @@ def train(fused: str, dev: torch.device, level: int = 2) -> dict[str, torch.Tens
     model = setup_parallel(model, pctx, bucket_cap_mb=0.5)
     eng = get_engine(model)
     assert eng.fused == (fused == "1" and level == 2), (eng.fused, fused, level)
-    opt = configure_optimizer(model, cfg, SchedulerConfig(), MuonAdamWConfig(), dp_group=pctx.dp_group)
+    opt = configure_optimizer(model, cfg, SchedulerConfig(), MuonAdamWConfig(matrix_optimizer=matrix_optimizer),
+                              dp_group=pctx.dp_group)
     g = torch.Generator(device="cpu").manual_seed(7)
     for _ in range(3):
         x = torch.randint(0, cfg.vocab_size, (2 * pctx.dp_size, cfg.seq_length), generator=g)
@@ -63,6 +65,10 @@ def train(fused: str, dev: torch.device, level: int = 2) -> dict[str, torch.Tens
         eng._synced = True
         eng.clip_grad_norm(0.5)
         opt.step()
+        if losses is not None:
+            t = loss.detach().float().clone()
+            dist.all_reduce(t)
+            losses.append(round(float(t) / pctx.dp_size, 5))
     torch.cuda.synchronize()
     if eng.fused:
         # the sharded updates stored their results into the peers' copies (AdamW buckets and the
@@ -143,13 +149,18 @@ def main() -> None:
     failures += not ok
     print(f"[rank {rank}] ZeRO-2 3 steps fused vs NCCL: worst param rel diff {worst:.2e} over {len(ref)} "
           f"{'OK' if ok else 'FAIL'}", flush=True)
-    # ZeRO-3 (parameters sharded too, gathered per block ahead of use) against ZeRO-2
-    z3 = train("0", dev, level=3)
-    worst3 = max(rel(z3[k], ref[k]) for k in ref)
-    ok = set(ref) == set(z3) and worst3 < 1e-3
-    failures += not ok
-    print(f"[rank {rank}] ZeRO-3 3 steps vs ZeRO-2: worst param rel diff {worst3:.2e} {'OK' if ok else 'FAIL'}",
-          flush=True)
+    # ZeRO-3 (parameters sharded too, gathered per block ahead of use) against ZeRO-2, with NorMuon
+    # and with AdamW on the matrices; per-step losses and the worst parameters are printed
+    for mopt in ("adamw", "muon"):
+        l2, l3 = [], []
+        z2 = train("0", dev, level=2, matrix_optimizer=mopt, losses=l2)
+        z3 = train("0", dev, level=3, matrix_optimizer=mopt, losses=l3)
+        diffs = sorted(((rel(z3[k], z2[k]), k) for k in z2), reverse=True)
+        worst3 = diffs[0][0]
+        ok = set(z2) == set(z3) and worst3 < 1e-3
+        failures += not ok
+        print(f"[rank {rank}] ZeRO-3 vs ZeRO-2 ({mopt}) 3 steps: losses {l3} vs {l2}; worst "
+              f"{[(k, f'{d:.1e}') for d, k in diffs[:4]]} {'OK' if ok else 'FAIL'}", flush=True)
     torch.cuda.synchronize()
     _ext.check_device_status()
     dist.barrier()
