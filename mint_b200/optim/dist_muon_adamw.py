@@ -166,8 +166,9 @@ class DistMuonAdamW(Optimizer):
                 if not eng.owns_whole(p):
                     continue
                 (pv, gv, off, n), = eng.segments(p)
-                assert off == 0 and n == p.numel(), "owner buckets hold whole matrices"
                 _b, slot = eng.slot(p)
+                # (ZeRO-3 has released p's full storage by now: compare against the slot)
+                assert off == 0 and n == slot.numel, "owner buckets hold whole matrices"
                 units.append((p, pv.view(slot.shape), gv.view(slot.shape)))
             else:
                 if p.grad is None:

@@ -144,7 +144,7 @@ def test_dp2_zero_levels_match_single_process(level):
     _run(2, 1, level, False, muon=False)
 
 
-@pytest.mark.parametrize("level", [1, 2])
+@pytest.mark.parametrize("level", [1, 2, 3])
 def test_dp2_normuon_owner_sharding_matches_single_process(level):
     _run(2, 1, level, False, muon=True)
 
