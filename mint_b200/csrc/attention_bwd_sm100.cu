@@ -306,6 +306,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* dlt_row = p.delta + rowbase;
       const bool full_cols = q0 + cb + 64 <= p.T;
       const int last_col = p.T - 1 - (q0 + cb);
+      // this tile's LSE pairs, loaded before the S wait so their latency hides behind it
+      float2 lse_pk[32];
+      if (full_cols) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) lse_pk[c] = __ldg(reinterpret_cast<const float2*>(lse_row) + c);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          lse_pk[c] = make_float2(__ldg(lse_row + min(2 * c, last_col)), __ldg(lse_row + min(2 * c + 1, last_col)));
+        }
+      }
       FAB_STAMP(1)
       if (!(ok = mbar_wait_warp(&s.s_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       FAB_STAMP(2)
@@ -334,20 +345,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 nl2e = make_float2(-1.4426950408889634f, -1.4426950408889634f);
-        if (full_cols) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float2 l2 = __ldg(reinterpret_cast<const float2*>(lse_row) + c);
-            const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, fmul2(l2, nl2e));
-            pk[c] = ex2_bf16x2(t.x, t.y);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float2 l2 = make_float2(__ldg(lse_row + min(2 * c, last_col)), __ldg(lse_row + min(2 * c + 1, last_col)));
-            const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, fmul2(l2, nl2e));
-            pk[c] = ex2_bf16x2(t.x, t.y);
-          }
+        for (int c = 0; c < 32; ++c) {
+          const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, fmul2(lse_pk[c], nl2e));
+          pk[c] = ex2_bf16x2(t.x, t.y);
         }
       }
       FAB_STAMP(4)
@@ -364,6 +365,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.p_ready);
+      // this tile's delta pairs, loaded before the dP wait
+      float2 dlt_pk[32];
+      if (full_cols) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) dlt_pk[c] = __ldg(reinterpret_cast<const float2*>(dlt_row) + c);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          dlt_pk[c] = make_float2(__ldg(dlt_row + min(2 * c, last_col)), __ldg(dlt_row + min(2 * c + 1, last_col)));
+        }
+      }
       FAB_STAMP(5)
       if (!(ok = mbar_wait_warp(&s.dp_full, ph, p.status, kStatusTimeoutAttention, abort_flag))) break;
       FAB_STAMP(6)
@@ -378,9 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 32; ++c) {
           const uint32_t* u = c < 16 ? u0 : u1;
           const int e = (2 * c) & 31;
-          const float2 d2 = full_cols ? __ldg(reinterpret_cast<const float2*>(dlt_row) + c)
-                                      : make_float2(__ldg(dlt_row + min(2 * c, last_col)),
-                                                    __ldg(dlt_row + min(2 * c + 1, last_col)));
+          const float2 d2 = dlt_pk[c];
           const float2 g = fadd2(make_float2(__uint_as_float(u[e]), __uint_as_float(u[e + 1])),
                                  make_float2(-d2.x, -d2.y));
           const float2 ds = fmul2(bf16x2_to_float2(pk[c]), g);

@@ -25,7 +25,9 @@ namespace fa {
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kD = 128;
-constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warps 4..11 softmax (2 per TMEM lane quadrant)
+constexpr int kSplit = 4;                       // softmax warps per TMEM lane quadrant
+constexpr int kCols = 128 / kSplit;              // score / output columns per softmax thread
+constexpr int kThreads = (4 + 4 * kSplit) * 32;  // warp 0 TMA, warp 1 MMA, warps 4.. softmax
 constexpr int kTileBytes = kBM * kD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-wide swizzle atoms)
 constexpr int kAtomBytes = kTileBytes / 2;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -61,10 +63,10 @@ struct Smem {
   uint64_t p_full;
   uint64_t pv_done;
   uint64_t mma_done;
-  uint64_t mx_full[4];     // per TMEM lane quadrant: both softmax warps of the quadrant published their
+  uint64_t mx_full[4];     // per TMEM lane quadrant: every softmax warp of the quadrant published its
                            // partial row maxima (and, last, row sums)
-  float mx[2][2][kBM];     // [tile parity][column half][row] partial maxima of the current score tile
-  float lsum[2][kBM];      // [column half][row] partial row sums, exchanged once at the end
+  float mx[2][kSplit][kBM];  // [tile parity][column part][row] partial maxima of the current score tile
+  float lsum[kSplit][kBM];   // [column part][row] partial row sums, exchanged once at the end
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -137,8 +139,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
     }
-    mbar_init(&s.p_full, 8);
-    for (int i = 0; i < 4; ++i) mbar_init(&s.mx_full[i], 2);
+    mbar_init(&s.p_full, 4 * kSplit);
+    for (int i = 0; i < 4; ++i) mbar_init(&s.mx_full[i], kSplit);
     mbar_init(&s.pv_done, 1);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
@@ -217,10 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&s.mma_done, 0, p.status, kStatusTimeoutAttention, nullptr);
     }
   } else if (warp >= 4) {
-    // warp 4 + 4h + q: TMEM lane quadrant q (query rows q*32 .. q*32+31), score / O columns [64h, 64h + 64)
+    // warp 4 + 4 part + q: TMEM lane quadrant q (query rows q*32 .. q*32+31), score / O columns
+    // [kCols part, kCols part + kCols)
     const int q = warp & 3;
-    const int half = (warp - 4) >> 2;
-    const int cb = half * 64;
+    const int part = (warp - 4) >> 2;
+    const int cb = part * kCols;
     const int r = q * 32 + lane;
     const int qi = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
@@ -233,12 +236,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the first key and the first row's document ends after the last key
     const int2 dfirst = doc_sorted ? db[q0] : make_int2(0, p.T);
     const int2 dlast = doc_sorted ? db[min(p.T, q0 + kBM) - 1] : make_int2(0, p.T);
-    float m = -INFINITY, l = 0.f;  // running max (shared by both halves of the row), this half's row sum
+    float m = -INFINITY, l = 0.f;  // running max (shared by every part of the row), this part's row sum
     bool ok = n > 0;
     int pv_waited = -1;  // index of the last PV whose completion this thread observed
-    unsigned long long* tr = (p.trace != nullptr && lane == 0 && (warp == 4 || warp == 8) && blockIdx.x == 0 &&
-                              blockIdx.y == 0 && blockIdx.z == 0)
-                                 ? p.trace + half * kTraceTiles * kTraceSteps
+    unsigned long long* tr = (p.trace != nullptr && lane == 0 && (warp == 4 || warp == 4 + 4 * (kSplit - 1)) &&
+                              blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+                                 ? p.trace + (part == 0 ? 0 : 1) * kTraceTiles * kTraceSteps
                                  : nullptr;
 #define FA_STAMP(k) \
   if (tr != nullptr && t < kTraceTiles) tr[t * kTraceSteps + (k)] = clock64();
@@ -251,18 +254,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       FA_STAMP(1)
-      float x[64];
+      float x[kCols];  // raw scores: the softmax scale goes into the exponent's FMA
       {
-        uint32_t u0[32], u1[32];  // both loads in flight under one wait
-        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + cb, u0);
-        tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + cb + 32, u1);
-        tmem_ld_wait();
-        // raw scores: the softmax scale goes into the exponent's FMA (max commutes with a positive scale)
+        uint32_t u[kCols];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          x[e] = __uint_as_float(u0[e]);
-          x[32 + e] = __uint_as_float(u1[e]);
+        for (int c = 0; c < kCols / 32; ++c) {
+          tmem_ld_32x32b_x32(tmem + (t & 1) * 128 + lane_off + cb + c * 32,
+                             *reinterpret_cast<uint32_t(*)[32]>(u + c * 32));
         }
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < kCols; ++e) x[e] = __uint_as_float(u[e]);
       }
       const bool doc_mask = p.doc != nullptr && !(doc_sorted && dlast.x <= kb && dfirst.y >= kb + kBN);
       const bool need_mask = (p.causal && kb + kBN - 1 > q0) || (p.window >= 0 && q0 + kBM - 1 - kb > p.window) ||
@@ -270,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (need_mask) {
         if (doc_sorted || p.doc == nullptr) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
+          for (int c = 0; c < kCols; ++c) {
             const int kj = kb + cb + c;
             bool keep = kj < p.T && kj >= d_lo && kj < d_hi;
             if (p.causal) keep = keep && kj <= qi;
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!keep) x[c] = -INFINITY;
           }
         } else {
-          for (int c = 0; c < 64; ++c) {
+          for (int c = 0; c < kCols; ++c) {
             const int kj = kb + cb + c;
             bool keep = kj < p.T;
             if (p.causal) keep = keep && kj <= qi;
@@ -291,26 +293,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       FA_STAMP(2)
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
-      for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+      for (int c = 0; c < kCols; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
       float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       FA_STAMP(3)
-      // combine with the other half of the row; the buffer of this parity was last read two tiles
-      // ago, before every softmax warp arrived on the previous tile's exchange
-      s.mx[t & 1][half][r] = mt;
+      // combine with the other parts of the row; the buffer of this parity was last read two tiles
+      // ago, before every warp of the quadrant arrived on the previous tile's exchange
+      s.mx[t & 1][part][r] = mt;
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.mx_full[q]);
       if (!mbar_wait_warp(&s.mx_full[q], t & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
         ok = false;
         break;
       }
-      mt = fmaxf(mt, s.mx[t & 1][half ^ 1][r]);
+#pragma unroll
+      for (int o2 = 0; o2 < kSplit; ++o2) {
+        if (o2 != part) mt = fmaxf(mt, s.mx[t & 1][o2][r]);
+      }
       FA_STAMP(4)
       const float m_new = fmaxf(m, mt * p.scale_log2);  // running max in scaled log2 units
-      // tcgen05.ld/st are warp-collective: the rescale decision must be uniform across the warp; both
+      // tcgen05.ld/st are warp-collective: the rescale decision must be uniform across the warp; the
       // warps of a lane quadrant see the same row maxima and so decide alike
       const bool grow = m != -INFINITY && m_new > m + kRescaleThreshold;
       if (t > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds PV_0..PV_{t-1}: wait for PV_{t-1}, then rescale this half of the rows in TMEM
+        // O holds PV_0..PV_{t-1}: wait for PV_{t-1}, then rescale this part of the rows in TMEM
         if (pv_waited < t - 1) {
           if (!mbar_wait_warp(&s.pv_done, (t - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
             ok = false;
@@ -322,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float alpha = (m == -INFINITY || m_new == -INFINITY) ? 0.f : exp2f(m - m_new);
         l *= alpha;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < kCols / 16; ++c) {
           uint32_t u[16];
           tmem_ld_32x32b_x16(tmem_o + lane_off + cb + c * 16, u);
           tmem_ld_wait();
@@ -340,20 +345,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = exp2(x * scale - m) in bf16, two elements per instruction (packed fp32 FMA, bf16x2 MUFU
       // exponential); the row sum adds the bf16 values the PV MMA uses. A row with nothing kept yet
       // (m = -inf) has every x = -inf, so m is taken as 0 there and every p comes out 0.
-      uint32_t pk[32];
+      uint32_t pk[kCols / 2];
       float rs = 0.f;
       {
         const float mm = (m == -INFINITY) ? 0.f : m;
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-mm, -mm);
         float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // two chains for ILP
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float2 t = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, nm2);
+        for (int c = 0; c < kCols / 2; ++c) {
+          const float2 tt = ffma2(make_float2(x[2 * c], x[2 * c + 1]), sc2, nm2);
           uint32_t e;
           if (p.diag & 1) {
-            e = pack_bf16x2(fmaf(t.x, 0.01f, 1.f), fmaf(t.y, 0.01f, 1.f));
+            e = pack_bf16x2(fmaf(tt.x, 0.01f, 1.f), fmaf(tt.y, 0.01f, 1.f));
           } else {
-            e = ex2_bf16x2(t.x, t.y);
+            e = ex2_bf16x2(tt.x, tt.y);
           }
           pk[c] = e;
           acc2[c & 1] = fadd2(acc2[c & 1], bf16x2_to_float2(e));
@@ -371,11 +376,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         pv_waited = t - 1;
       }
       FA_STAMP(7)
-      // 128B-swizzled K-major store of this half row: swizzle atom `half` (64 keys), 16B chunk c at c ^ (row % 8)
+      // 128B-swizzled K-major store of this part of the row: 64-key swizzle atom cb / 64, 16-byte
+      // chunk (cb % 64) / 8 + c at that index ^ (row % 8)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 v4 = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
-        *reinterpret_cast<uint4*>(s.p + half * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4)) = v4;
+      for (int c = 0; c < kCols / 8; ++c) {
+        const int chunk = (cb & 63) / 8 + c;
+        const uint4 v4 = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+        *reinterpret_cast<uint4*>(s.p + (cb >> 6) * kAtomBytes + r * 128 + ((chunk ^ (r & 7)) << 4)) = v4;
       }
       FA_STAMP(8)
       fence_proxy_async_smem();
@@ -388,26 +395,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && n > 0 && pv_waited < n - 1) {
       ok = mbar_wait_warp(&s.pv_done, (n - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag);
     }
-    // row sum over both halves (a final exchange round on mx_full, phase n)
+    // row sum over every part (a final exchange round on mx_full, phase n)
     if (ok && n > 0) {
-      s.lsum[half][r] = l;
+      s.lsum[part][r] = l;
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.mx_full[q]);
       ok = mbar_wait_warp(&s.mx_full[q], n & 1, p.status, kStatusTimeoutAttention, abort_flag);
-      if (ok) l += s.lsum[half ^ 1][r];
+      if (ok) {
+        l = 0.f;
+#pragma unroll
+        for (int o2 = 0; o2 < kSplit; ++o2) l += s.lsum[o2][r];
+      }
     }
     ok = __all_sync(0xffffffffu, ok);
     if (ok && n > 0) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = qi < p.T;
-      // rows of warps whose 32 rows all lie inside the sequence leave through shared memory (the Q
-      // tile is free: every MMA reading it completed) and one TMA store per warp; the others (the
-      // sequence's ragged last tile) store directly, so no row of the next sequence is touched
-      const bool via_tma = q0 + q * 32 + 32 <= p.T;
+      // each thread stores its row's kCols output columns directly (rows past the sequence end skip)
       __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + (row_ok ? qi : 0)) * p.Hq + h) * kD + cb;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kCols / 32; ++c) {
         uint32_t u[32];
         tmem_ld_32x32b_x32(tmem_o + lane_off + cb + c * 32, u);  // warp-collective: every lane loads
         tmem_ld_wait();
@@ -419,33 +427,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           v4.y = pack_bf16x2(__uint_as_float(u[e + 2]) * inv, __uint_as_float(u[e + 3]) * inv);
           v4.z = pack_bf16x2(__uint_as_float(u[e + 4]) * inv, __uint_as_float(u[e + 5]) * inv);
           v4.w = pack_bf16x2(__uint_as_float(u[e + 6]) * inv, __uint_as_float(u[e + 7]) * inv);
-          if (via_tma) {
-            const int chunk = c * 4 + (e >> 3);  // 16-byte chunk of this half row, 128B swizzle
-            *reinterpret_cast<uint4*>(s.q + half * kAtomBytes + r * 128 + ((chunk ^ (r & 7)) << 4)) = v4;
-          } else {
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v4;
-          }
+          *reinterpret_cast<uint4*>(orow + c * 32 + e) = v4;
         }
-      }
-      if (via_tma) {
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&to, s.q + half * kAtomBytes + q * 32 * 128, cb, h, b * p.T + q0 + q * 32);
-          bulk_commit();
-          bulk_wait_read<0>();  // the shared memory must stay valid until the store has read it
-        }
-        __syncwarp();
       }
       // natural-log LSE of the scaled scores: (m + log2 l) * ln 2
-      if (row_ok && half == 0) {
+      if (row_ok && part == 0) {
         p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] =
             l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
       }
     } else if (n == 0 && qi < p.T) {
       __nv_bfloat16* orow = p.o + ((static_cast<long long>(b) * p.T + qi) * p.Hq + h) * kD + cb;
-      for (int c = 0; c < 64; ++c) orow[c] = __float2bfloat16_rn(0.f);
-      if (half == 0) p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] = -INFINITY;
+      for (int c = 0; c < kCols; ++c) orow[c] = __float2bfloat16_rn(0.f);
+      if (part == 0) p.lse[(static_cast<long long>(b) * p.Hq + h) * p.T + qi] = -INFINITY;
     }
   }
 
