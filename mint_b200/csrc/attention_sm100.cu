@@ -1,18 +1,20 @@
 // FlashAttention forward for sm_100a on tcgen05 tensor cores (head_dim 128, bf16, GQA).
 //
-// One CTA per (128-query tile, query head, batch); 256 threads:
+// One CTA per (128-query tile, query head, batch); 384 threads:
 //   warp 0      TMA producer: Q once, then K_j / V_j tiles into 2-stage rings (128B swizzle)
 //   warp 1      TMEM owner + single-thread MMA issue:
 //                 S_j = Q K_j^T   (M=128 queries, N=128 keys, K=128)  -> TMEM S buffer j%2
 //                 O  += P_j V_j   (M=128, N=128 head dims, K=128 keys, P from shared memory)
 //               S_{j+1} is issued before PV_j so the softmax of tile j+1 overlaps PV_j.
-//   warps 4..11 softmax, two per TMEM lane quadrant: each thread owns half (64 columns) of one
+//   warps 4..   softmax, kSplit per TMEM lane quadrant: each thread owns kCols columns of one
 //               query row, loads its scores with tcgen05.ld, applies causal / sliding-window /
 //               document / sequence-end masks, exchanges its partial row maximum with the other
-//               half through shared memory, exp2 with a lazily updated running max (its half of O
-//               is rescaled in TMEM only when the max grows by more than 2^8), writes its half of
-//               P (bf16) in the 128B-swizzled K-major layout the PV MMA reads, and finally
-//               normalizes its half of O and stores O and the log-sum-exp.
+//               parts of the row through shared memory (one mbarrier per quadrant), computes
+//               P = exp2(s * scale - m) two elements per instruction (packed fp32 FMA, bf16x2 MUFU
+//               exponential) with a lazily updated running max (its columns of O are rescaled in
+//               TMEM only when the max grows by more than 2^8), writes its part of P (bf16) in the
+//               128B-swizzled K-major layout the PV MMA reads, and finally normalizes its columns
+//               of O, stores them and the log-sum-exp.
 // Tiles outside the causal / window band are never visited. All waits are bounded.
 #include <cstdlib>
 
@@ -25,7 +27,7 @@ namespace fa {
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kD = 128;
-constexpr int kSplit = 4;                       // softmax warps per TMEM lane quadrant
+constexpr int kSplit = 2;                       // softmax warps per TMEM lane quadrant (4 measured slower)
 constexpr int kCols = 128 / kSplit;              // score / output columns per softmax thread
 constexpr int kThreads = (4 + 4 * kSplit) * 32;  // warp 0 TMA, warp 1 MMA, warps 4.. softmax
 constexpr int kTileBytes = kBM * kD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-wide swizzle atoms)
