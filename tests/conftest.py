@@ -7,6 +7,8 @@ import pytest
 ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT))
 os.environ.setdefault("MINT_LOG_LEVEL", "WARNING")
+# trainers built by the tests must not write wandb run folders into the working tree
+os.environ.setdefault("WANDB_MODE", "disabled")
 
 
 def pytest_configure(config):
