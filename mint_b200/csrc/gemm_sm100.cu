@@ -450,43 +450,12 @@ __device__ __forceinline__ long long local_row_of(const CommParams& c, long long
 __device__ __forceinline__ long long gathered_row_of(const CommParams& c, int p, long long l) {
   return ((l / c.seg) * c.world + p) * c.seg + l % c.seg;
 }
-// 256-row tile ordinal -> tile index.
-// All-gather: own chunk first (its rows are local), then the peers' chunks in rotation order.
-// Reduce-scatter: peers' tiles and own tiles interleaved, so the pushes over NVLink spread over the
-// whole kernel instead of filling its first half: local tile index li contributes the peers' tiles
-// li and then this rank's own tile li - D (D = min(8, tiles per chunk) -- one tile group of the
-// schedule), the remaining own tiles come last. Every rank uses the same order, so a peer pushes
-// the partial of own tile k at an earlier ordinal than the one at which this rank reduces tile k.
+// 256-row tile ordinal -> tile index: own chunk first (all-gather) or last (reduce-scatter)
 __device__ __forceinline__ int comm_tile_m(const CommParams& c, int o, int tiles_m2, bool own_first) {
-  const int w = c.world;
-  const int tpc = tiles_m2 / w;  // 256-row tiles per chunk
-  int p, li;
-  if (own_first) {
-    const int cp = o / tpc;
-    p = (c.rank + cp) % w;
-    li = o % tpc;
-  } else {
-    const int D = min(8, tpc);
-    const int head = D * (w - 1);
-    if (o < head) {
-      li = o / (w - 1);
-      p = (c.rank + 1 + o % (w - 1)) % w;
-    } else if (o - head < (tpc - D) * w) {
-      const int o2 = o - head;
-      const int k = o2 % w;
-      if (k < w - 1) {
-        li = D + o2 / w;
-        p = (c.rank + 1 + k) % w;
-      } else {
-        li = o2 / w;  // own tile (D + o2 / w) - D
-        p = c.rank;
-      }
-    } else {
-      li = tpc - D + (o - head - (tpc - D) * w);
-      p = c.rank;
-    }
-  }
-  const long long l = static_cast<long long>(li) * 256;  // local row of the tile's first row
+  const int tpc = tiles_m2 / c.world;  // 256-row tiles per chunk
+  const int cp = o / tpc;
+  const int p = (c.rank + (own_first ? 0 : 1) + cp) % c.world;
+  const long long l = static_cast<long long>(o % tpc) * 256;  // local row of the tile's first row
   return static_cast<int>(gathered_row_of(c, p, l) / 256);
 }
 
