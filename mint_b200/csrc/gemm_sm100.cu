@@ -450,12 +450,43 @@ __device__ __forceinline__ long long local_row_of(const CommParams& c, long long
 __device__ __forceinline__ long long gathered_row_of(const CommParams& c, int p, long long l) {
   return ((l / c.seg) * c.world + p) * c.seg + l % c.seg;
 }
-// 256-row tile ordinal -> tile index: own chunk first (all-gather) or last (reduce-scatter)
+// 256-row tile ordinal -> tile index.
+// All-gather: own chunk first (its rows are local), then the peers' chunks in rotation order.
+// Reduce-scatter: peers' tiles and own tiles interleaved, so the pushes over NVLink spread over the
+// whole kernel instead of filling its first half: local tile index li contributes the peers' tiles
+// li and then this rank's own tile li - D (D = min(8, tiles per chunk) -- one tile group of the
+// schedule), the remaining own tiles come last. Every rank uses the same order, so a peer pushes
+// the partial of own tile k at an earlier ordinal than the one at which this rank reduces tile k.
 __device__ __forceinline__ int comm_tile_m(const CommParams& c, int o, int tiles_m2, bool own_first) {
-  const int tpc = tiles_m2 / c.world;  // 256-row tiles per chunk
-  const int cp = o / tpc;
-  const int p = (c.rank + (own_first ? 0 : 1) + cp) % c.world;
-  const long long l = static_cast<long long>(o % tpc) * 256;  // local row of the tile's first row
+  const int w = c.world;
+  const int tpc = tiles_m2 / w;  // 256-row tiles per chunk
+  int p, li;
+  if (own_first) {
+    const int cp = o / tpc;
+    p = (c.rank + cp) % w;
+    li = o % tpc;
+  } else {
+    const int D = min(8, tpc);
+    const int head = D * (w - 1);
+    if (o < head) {
+      li = o / (w - 1);
+      p = (c.rank + 1 + o % (w - 1)) % w;
+    } else if (o - head < (tpc - D) * w) {
+      const int o2 = o - head;
+      const int k = o2 % w;
+      if (k < w - 1) {
+        li = D + o2 / w;
+        p = (c.rank + 1 + k) % w;
+      } else {
+        li = o2 / w;  // own tile (D + o2 / w) - D
+        p = c.rank;
+      }
+    } else {
+      li = tpc - D + (o - head - (tpc - D) * w);
+      p = c.rank;
+    }
+  }
+  const long long l = static_cast<long long>(li) * 256;  // local row of the tile's first row
   return static_cast<int>(gathered_row_of(c, p, l) / 256);
 }
 
@@ -465,14 +496,17 @@ constexpr int kRsLag = 2;    // a pushed tile's flag is released once two newer 
 
 // Publish the flags of every tile this warp pushed: wait until all of this lane's TMA stores have
 // been performed, order them (async proxy, then system scope) before the releases.
-__device__ __forceinline__ void rs_flush(const CommParams& c, int* pend, int& npend, int lane) {
+// (No separate system fence: `st.release.sys` already orders every earlier write of the thread;
+// one per tile measured 1.3 ms of 4.6 at M=131072 N=8192 tp=2.)
+__device__ __forceinline__ void rs_flush_lane0(const CommParams& c, const int* pend, int& npend) {
   if (npend == 0) return;
-  if (lane == 0) {
-    bulk_wait_all();
-    fence_proxy_async_global();
-    __threadfence_system();
-    for (int i = 0; i < npend; ++i) st_release_sys(c.rs_flag_peer[pend[2 * i]] + pend[2 * i + 1], c.seq);
-  }
+  bulk_wait_all();
+  fence_proxy_async_global();
+  for (int i = 0; i < npend; ++i) st_release_sys(c.rs_flag_peer[pend[2 * i]] + pend[2 * i + 1], c.seq);
+  npend = 0;
+}
+__device__ __forceinline__ void rs_flush(const CommParams& c, int* pend, int& npend, int lane) {
+  if (lane == 0) rs_flush_lane0(c, pend, npend);
   __syncwarp();
   npend = 0;
 }
@@ -485,7 +519,6 @@ __device__ __forceinline__ void rs_release_lagged(const CommParams& c, int* pend
   if (lane == 0) {
     bulk_wait<kRsLag * kG>();
     fence_proxy_async_global();
-    __threadfence_system();
     st_release_sys(c.rs_flag_peer[pend[0]] + pend[1], c.seq);
     for (int i = 1; i < npend; ++i) {
       pend[2 * (i - 1)] = pend[2 * i];
@@ -554,17 +587,25 @@ __device__ __forceinline__ bool epilogue_tile_rs(const Params& p, const CommPara
     rs_release_lagged<BN / 64>(c, pend, npend, lane);
     return true;
   }
-  // own rows: publish what this warp pushed (peers may be waiting on it), then wait for every
-  // peer's partial of these 32 rows, reduce and store
-  rs_flush(c, pend, npend, lane);
+  // own rows: wait for every peer's partial of these 32 rows, reduce and store. A warp that has to
+  // wait first publishes every tile it pushed (a peer may be waiting on one of them), so no two
+  // ranks can wait on each other; when the partials are already there, its pushes stay in flight.
   bool ok = true;
   if (lane == 0) {
-    for (int src = 0; src < c.world && ok; ++src) {
-      if (src == c.rank) continue;
-      ok = wait_flag(c.rs_flag_local + src * c.rs_flag_stride + fidx, c.seq, true, p.status, kStatusTimeoutPeer,
-                     abort_flag);
+    bool ready = true;
+    for (int src = 0; src < c.world && ready; ++src) {
+      if (src != c.rank) ready = ld_acquire_sys(c.rs_flag_local + src * c.rs_flag_stride + fidx) >= c.seq;
+    }
+    if (!ready) {
+      rs_flush_lane0(c, pend, npend);
+      for (int src = 0; src < c.world && ok; ++src) {
+        if (src == c.rank) continue;
+        ok = wait_flag(c.rs_flag_local + src * c.rs_flag_stride + fidx, c.seq, true, p.status, kStatusTimeoutPeer,
+                       abort_flag);
+      }
     }
   }
+  npend = __shfl_sync(0xffffffffu, npend, 0);
   if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
   const long long lrow = lrow0 + lane;
 #pragma unroll 1
@@ -1073,6 +1114,13 @@ __global__ void __launch_bounds__(pair_threads<BN, COMM>(), 1)
     for (int w = pair; w < num_tiles; w += npairs, ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
+      if constexpr (COMM == 2) {
+        // the next accumulator may depend (through the MMA and the other epilogue warps) on a peer
+        // that waits for a tile this warp pushed: publish them all before blocking on it
+        if (__any_sync(0xffffffffu, npend > 0 && !mbar_try_wait(smem_u32(&tfull[acc]), acc_phase))) {
+          rs_flush(c, pend, npend, lane);
+        }
+      }
       if (!mbar_wait_warp(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       int bi, tm, tn, kb0_, nkb_;

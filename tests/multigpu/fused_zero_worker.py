@@ -48,11 +48,14 @@ def train(fused: str, dev: torch.device, level: int = 2, matrix_optimizer: str =
     model = setup_parallel(model, pctx, bucket_cap_mb=0.5)
     eng = get_engine(model)
     assert eng.fused == (fused == "1" and level == 2), (eng.fused, fused, level)
-    opt = configure_optimizer(model, cfg, SchedulerConfig(), MuonAdamWConfig(matrix_optimizer=matrix_optimizer),
+    # AdamW eps 1e-3 instead of the recipe's 1e-10, and the recipe's learning rates x 0.1: with
+    # eps 1e-10 every AdamW step is a per-element sign step, so the run-to-run noise of the attention
+    # kernel's dQ reductions decides the direction of every near-zero gradient and runs of the same
+    # layout already differ by up to 1e-2; with a larger eps the update depends smoothly on the
+    # gradient and the layouts can be compared closely
+    opt = configure_optimizer(model, cfg, SchedulerConfig(),
+                              MuonAdamWConfig(matrix_optimizer=matrix_optimizer, adamw_eps=1e-3),
                               dp_group=pctx.dp_group)
-    # the recipe's learning rates x 0.1: at full rates uniform-random targets push AdamW (eps 1e-10,
-    # per-element normalized steps) into a regime where the run-to-run noise of the attention
-    # kernel's dQ reductions decides the sign of near-zero gradients, and layouts cannot be compared
     for g in opt.param_groups:
         g["lr"] *= 0.1
         g["initial_lr"] = g["lr"]
@@ -148,25 +151,39 @@ def main() -> None:
         print(f"[rank {rank}] all-gather call {it}: {'OK' if ok else 'FAIL'}", flush=True)
     _ext.check_device_status()
 
+    # The attention backward's dQ and the split-K weight gradients are accumulated with fp32
+    # reduce-adds whose order changes from run to run. Each comparison is therefore also held to
+    # the run-to-run difference of the reference layout itself (two identical runs), measured here.
     ref = train("0", dev)
+    ref2 = train("0", dev)
     got = train("1", dev)
+    noise = max(rel(ref2[k], ref[k]) for k in ref)
     worst = max(rel(got[k], ref[k]) for k in ref)
-    ok = set(ref) == set(got) and worst < 2e-3
+    tol = max(2e-3, 4.0 * noise)
+    ok = set(ref) == set(got) and worst <= tol
     failures += not ok
     print(f"[rank {rank}] ZeRO-2 3 steps fused vs NCCL: worst param rel diff {worst:.2e} over {len(ref)} "
-          f"{'OK' if ok else 'FAIL'}", flush=True)
+          f"(NCCL run-to-run {noise:.2e}, tolerance {tol:.2e}) {'OK' if ok else 'FAIL'}", flush=True)
     # ZeRO-3 (parameters sharded too, gathered per block ahead of use) against ZeRO-2, with NorMuon
     # and with AdamW on the matrices; per-step losses and the worst parameters are printed
     for mopt in ("adamw", "muon"):
-        l2, l3 = [], []
+        l2, l2b, l3 = [], [], []
         z2 = train("0", dev, level=2, matrix_optimizer=mopt, losses=l2)
+        z2b = train("0", dev, level=2, matrix_optimizer=mopt, losses=l2b)
         z3 = train("0", dev, level=3, matrix_optimizer=mopt, losses=l3)
         diffs = sorted(((rel(z3[k], z2[k]), k) for k in z2), reverse=True)
         worst3 = diffs[0][0]
-        ok = set(z2) == set(z3) and worst3 < 2e-3 and all(abs(a - b) <= 1e-3 * abs(b) for a, b in zip(l3, l2))
+        noise3 = max(rel(z2b[k], z2[k]) for k in z2)
+        tol3 = max(2e-3, 4.0 * noise3)
+        lnoise = max(abs(a - b) / abs(b) for a, b in zip(l2b, l2))
+        ltol = max(1e-4, 4.0 * lnoise)
+        # the first step sees identical parameters: its loss may differ by reduction order only
+        ok = (set(z2) == set(z3) and worst3 <= tol3 and abs(l3[0] - l2[0]) <= 1e-4 * abs(l2[0])
+              and all(abs(a - b) <= ltol * abs(b) for a, b in zip(l3, l2)))
         failures += not ok
         print(f"[rank {rank}] ZeRO-3 vs ZeRO-2 ({mopt}) 3 steps: losses {l3} vs {l2}; worst "
-              f"{[(k, f'{d:.1e}') for d, k in diffs[:4]]} {'OK' if ok else 'FAIL'}", flush=True)
+              f"{[(k, f'{d:.1e}') for d, k in diffs[:4]]} (ZeRO-2 run-to-run {noise3:.1e}, losses {lnoise:.1e}) "
+              f"{'OK' if ok else 'FAIL'}", flush=True)
     torch.cuda.synchronize()
     _ext.check_device_status()
     dist.barrier()
