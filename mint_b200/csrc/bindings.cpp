@@ -69,6 +69,7 @@ void zero_reduce_scatter(const std::vector<int64_t>& bucket_ptrs, at::Tensor& sh
                          const c10::optional<at::Tensor>& sumsq, const std::vector<int64_t>& flag_ptrs,
                          const at::Tensor& flags_local, int64_t rank, int64_t world, int64_t seq);
 void zero_all_gather(const at::Tensor& shard, const std::vector<int64_t>& bucket_ptrs, int64_t rank, int64_t world);
+void zero_gather_pull(const std::vector<int64_t>& shard_ptrs, at::Tensor& full, int64_t rank, int64_t world);
 void zero_barrier(const std::vector<int64_t>& flag_ptrs, const at::Tensor& flags_local, int64_t rank, int64_t world,
                   int64_t seq);
 void gemm_ag(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool b_kmajor, const std::vector<int64_t>& src_ptrs,
@@ -183,6 +184,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("zero_reduce_scatter", &mint::zero_reduce_scatter,
         "ZeRO gradient reduce-scatter over NVLink peer memory, 1/dp scale and squared norm fused");
   m.def("zero_all_gather", &mint::zero_all_gather, "ZeRO parameter all-gather: push this rank's shard to every peer");
+  m.def("zero_gather_pull", &mint::zero_gather_pull, "ZeRO-3 parameter gather: pull every rank's shard over NVLink");
   m.def("zero_barrier", &mint::zero_barrier, "stream-ordered barrier of a ZeRO group over NVLink peer flags");
   m.def("flash_attn_fwd_trace", &mint::flash_attn_fwd_trace,
         "MINT_FA_TRACE=1 diagnostics: clock64 stamps of the last forward's longest query tile");

@@ -7,6 +7,7 @@
 //   announcement and pulls the peers' slices of its shard with 16-byte loads.
 // zero_adamw_push: the sharded AdamW update with the all-gather fused in (new values stored to
 //   every peer's copy as they are computed).
+// zero_gather_pull: ZeRO-3's parameter gather, every rank's shard pulled into a local full buffer.
 // zero_all_gather: pushes this rank's (updated) shard of a flat parameter bucket into every
 //   peer's copy of the bucket; zero_barrier (one block, after the pushes of all buckets) announces
 //   it and waits until every peer's shards have landed in this rank's copies.
@@ -97,6 +98,29 @@ __global__ void __launch_bounds__(256) zero_push_kernel(Peers pe, const float* _
     const float4 v = reinterpret_cast<const float4*>(shard)[i];
     for (int q = 0; q < world; ++q) {
       if (q != rank) reinterpret_cast<float4*>(pe.dst[q] + off)[i] = v;
+    }
+  }
+}
+
+// ZeRO-3 parameter gather: full[q * n .. (q + 1) * n) = rank q's shard (16-byte loads over NVLink
+// from every peer's symmetric shard buffer, four in flight per thread). Shards change only in the
+// optimizer step, which is fenced on both sides (see zero_gather_pull), so no flags are read here.
+__global__ void __launch_bounds__(256) zero_gather_pull_kernel(Peers pe, float* __restrict__ full, long long n,
+                                                               int world) {
+  const long long n4 = n / 4;
+  const long long total = n4 * world;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i0 < total; i0 += 4 * stride) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < total) v[u] = reinterpret_cast<const float4*>(pe.src[i / n4])[i % n4];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < total) reinterpret_cast<float4*>(full)[i] = v[u];
     }
   }
 }
@@ -196,6 +220,28 @@ void zero_all_gather(const at::Tensor& shard, const std::vector<int64_t>& bucket
   const long long n = shard.numel();
   zc::zero_push_kernel<<<grid_for(n / 4, dev), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       pe, shard.data_ptr<float>(), rank * n, n, static_cast<int>(rank), static_cast<int>(world));
+  MINT_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+// ZeRO-3: full [world * n] fp32 = every rank's shard (shard_ptrs[q] = rank q's shard of n elements,
+// in symmetric memory). The caller orders it after a zero_barrier that followed the last change of
+// any shard, and no rank changes its shard before every peer's gathers have completed.
+void zero_gather_pull(const std::vector<int64_t>& shard_ptrs, at::Tensor& full, int64_t rank, int64_t world) {
+  check_contig(full, "full");
+  MINT_CHECK(full.scalar_type() == at::kFloat && full.numel() % (4 * world) == 0,
+             "full must be fp32 with numel a multiple of 4 x world");
+  MINT_CHECK(static_cast<int64_t>(shard_ptrs.size()) == world, "one shard pointer per rank");
+  for (int64_t q = 0; q < world; ++q) MINT_CHECK(shard_ptrs[q] % 16 == 0, "shards must be 16-byte aligned");
+  (void)rank;
+  c10::cuda::CUDAGuard guard(full.device());
+  const int dev = full.get_device();
+  std::vector<int64_t> no_flags(world, 0);
+  zc::Peers pe = make_peers(shard_ptrs, {}, no_flags, world);
+  const long long n = full.numel() / world;
+  if (n == 0) return;
+  zc::zero_gather_pull_kernel<<<grid_for(n * world / 16, dev), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      pe, full.data_ptr<float>(), n, static_cast<int>(world));
   MINT_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -131,6 +131,10 @@ class GradEngine:
         # ZeRO-2 on CUDA: gradient reduce-scatter and parameter all-gather as NVLink peer-memory kernels
         # (csrc/zero_comm.cu) over symmetric bucket buffers instead of NCCL; MINT_FUSED_ZERO=0 disables
         self.fused = self._fused_possible(model)
+        # ZeRO-3 on CUDA: parameter shards in symmetric memory, gathered by a kernel that pulls every
+        # peer's shard over NVLink (on a side stream, one group ahead) instead of NCCL all-gathers
+        self.fused3 = self._fused3_possible(model)
+        self._z3_dirty = True  # shards changed since the last barrier: the next gather starts with one
         self._zc = None
         self.buckets: list[Bucket] = []
         self.by_param: dict[int, tuple[Bucket, Slot]] = {}
@@ -211,7 +215,12 @@ class GradEngine:
             s.param._orig_shape = s.shape  # logical shape while ZeRO-3 keeps only a shard
         lo = self.rank * shard
         if self.level == 3 and self.dp > 1:
-            b.shard_data = data[lo : lo + shard].clone()
+            if self.fused3 and dtype == torch.float32 and shard % 4 == 0:
+                b.extra["symm_shard"] = self._symm(shard * 4, dev)
+                b.shard_data = b.extra["symm_shard"].view((shard,), torch.float32)
+                b.shard_data.copy_(data[lo : lo + shard])
+            else:
+                b.shard_data = data[lo : lo + shard].clone()
             b.data = None
             b.gathered = False
             for s in slots:
@@ -243,6 +252,27 @@ class GradEngine:
         from mint_b200.ops import _ext  # noqa: PLC0415
 
         return _ext.kernels_enabled() and hasattr(_ext.require(), "zero_reduce_scatter")
+
+    def _fused3_possible(self, model: nn.Module) -> bool:
+        import os  # noqa: PLC0415
+
+        if os.environ.get("MINT_FUSED_ZERO", "1") == "0" or self.level != 3 or not self.distributed:
+            return False
+        if self.dp > 8 or not torch.cuda.is_available():
+            return False
+        dev = next((p.device for p in model.parameters()), torch.device("cpu"))
+        if dev.type != "cuda":
+            return False
+        from mint_b200.ops import _ext  # noqa: PLC0415
+
+        return _ext.kernels_enabled() and hasattr(_ext.require(), "zero_gather_pull")
+
+    def _zero3_barrier(self) -> None:
+        """Stream-ordered barrier of the dp group (ZeRO-3 over peer memory): every rank's shard
+        changes queued before it are complete before any peer's later gather reads them."""
+        zc = self._zc
+        _ext_mod().zero_barrier(zc["ctrl"].ptrs, zc["flags"], self.rank, self.dp, self._next_seq())
+        self._z3_dirty = False
 
     def _symm(self, nbytes: int, dev: torch.device):  # noqa: ANN202
         from mint_b200.parallel.fused import _Symm  # noqa: PLC0415
@@ -458,7 +488,17 @@ class GradEngine:
         if self.level == 3:
             for grp in self.group_order:
                 self.free_group(grp)
+            for b in self.buckets:  # a gather prefetched but never bound holds the old values
+                if b.gather_handle is not None and not isinstance(b.gather_handle, tuple):
+                    b.gather_handle.wait()
+                b.gather_handle = None
+                b.extra.pop("full", None)
             self._in_backward.clear()
+            if self.fused3:
+                # the updated shards are published before any peer's next gather reads them; the
+                # update itself started only after every peer's gathers of this step had completed
+                # (they precede each rank's last gradient reduce-scatter, which the update waits for)
+                self._zero3_barrier()
             return
         handles = []
         pushed = False
@@ -576,6 +616,22 @@ class GradEngine:
         if b.gathered or b.gather_handle is not None:
             return
         full = torch.empty(b.size, dtype=b.dtype, device=b.shard_data.device)
+        if "symm_shard" in b.extra:
+            # pull every peer's shard over NVLink on the side stream; _bind_full joins it
+            if self._z3_dirty:
+                self._zero3_barrier()
+            stream = self._zc["stream"]
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):
+                _ext_mod().zero_gather_pull(b.extra["symm_shard"].ptrs, full, self.rank, self.dp)
+            full.record_stream(stream)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            b.extra["full"] = full
+            b.gather_handle = ("pull", ev)
+            if not async_op:
+                self._bind_full(b)
+            return
         h = dist.all_gather_into_tensor(full, b.shard_data, group=self.group, async_op=async_op)
         b.extra["full"] = full
         if async_op:
@@ -584,7 +640,10 @@ class GradEngine:
             self._bind_full(b)
 
     def _bind_full(self, b: Bucket) -> None:
-        if b.gather_handle is not None:
+        if isinstance(b.gather_handle, tuple):
+            torch.cuda.current_stream().wait_event(b.gather_handle[1])
+            b.gather_handle = None
+        elif b.gather_handle is not None:
             b.gather_handle.wait()
             b.gather_handle = None
         full = b.extra.pop("full", None)
@@ -698,6 +757,7 @@ class GradEngine:
 
     def load_full_param(self, p: torch.Tensor, value: torch.Tensor) -> None:
         self.epoch += 1
+        self._z3_dirty = True
         b, s = self.by_param[id(p)]
         flat = value.reshape(-1).to(b.dtype)
         lo = self.rank * b.shard

@@ -8,7 +8,9 @@ Checks the ZeRO peer-memory collectives (csrc/zero_comm.cu) against NCCL:
      consolidated parameters with the fused transport (reduce-scatter straight into the gradient
      shard; AdamW / NorMuon update kernels that store the new values into every peer's copy)
      against the NCCL transport, and every rank's full parameter buckets identical;
-  4. the same training at ZeRO-3 (NCCL parameter gathers per block) against ZeRO-2.
+  4. the same training at ZeRO-3 (NCCL parameter gathers per block) against ZeRO-2 run with the same
+     (unchained) trunk, and ZeRO-3 with its gathers as peer-memory pulls (zero_gather_pull) against
+     ZeRO-3 over NCCL.
 Prints one line per check and exits non-zero on a mismatch.
 """
 
@@ -30,7 +32,7 @@ def rel(a: torch.Tensor, b: torch.Tensor) -> float:
 
 
 def train(fused: str, dev: torch.device, level: int = 2, matrix_optimizer: str = "muon",
-          losses: list | None = None) -> dict[str, torch.Tensor]:
+          losses: list | None = None, chain: bool = True) -> dict[str, torch.Tensor]:
     from mint_b200.models.gemma import Gemma, GemmaConfig, configure_optimizer
     from mint_b200.optim.muon_adamw import MuonAdamWConfig
     from mint_b200.parallel.api import setup_parallel
@@ -47,7 +49,13 @@ def train(fused: str, dev: torch.device, level: int = 2, matrix_optimizer: str =
     model = Gemma(cfg).to(dev)
     model = setup_parallel(model, pctx, bucket_cap_mb=0.5)
     eng = get_engine(model)
+    if not chain:
+        # the trunk without the chained residual-add + next-norm kernels, the form ZeRO-3 runs (its
+        # blocks' parameters exist only inside their own block): the bf16 roundings then happen at
+        # the same places, so ZeRO-3 can be compared with ZeRO-2 closely
+        model._chainable = lambda: False
     assert eng.fused == (fused == "1" and level == 2), (eng.fused, fused, level)
+    assert eng.fused3 == (fused == "1" and level == 3), (eng.fused3, fused, level)
     # AdamW eps 1e-3 instead of the recipe's 1e-10, and the recipe's learning rates x 0.1: with
     # eps 1e-10 every AdamW step is a per-element sign step, so the run-to-run noise of the attention
     # kernel's dQ reductions decides the direction of every near-zero gradient and runs of the same
@@ -168,9 +176,11 @@ def main() -> None:
     # and with AdamW on the matrices; per-step losses and the worst parameters are printed
     for mopt in ("adamw", "muon"):
         l2, l2b, l3 = [], [], []
-        z2 = train("0", dev, level=2, matrix_optimizer=mopt, losses=l2)
-        z2b = train("0", dev, level=2, matrix_optimizer=mopt, losses=l2b)
+        z2 = train("0", dev, level=2, matrix_optimizer=mopt, losses=l2, chain=False)
+        z2b = train("0", dev, level=2, matrix_optimizer=mopt, losses=l2b, chain=False)
         z3 = train("0", dev, level=3, matrix_optimizer=mopt, losses=l3)
+        l3f = []
+        z3f = train("1", dev, level=3, matrix_optimizer=mopt, losses=l3f)
         diffs = sorted(((rel(z3[k], z2[k]), k) for k in z2), reverse=True)
         worst3 = diffs[0][0]
         noise3 = max(rel(z2b[k], z2[k]) for k in z2)
@@ -181,6 +191,12 @@ def main() -> None:
         ok = (set(z2) == set(z3) and worst3 <= tol3 and abs(l3[0] - l2[0]) <= 1e-4 * abs(l2[0])
               and all(abs(a - b) <= ltol * abs(b) for a, b in zip(l3, l2)))
         failures += not ok
+        # ZeRO-3 with the parameter gathers as peer-memory pulls against ZeRO-3 over NCCL
+        worst3f = max(rel(z3f[k], z3[k]) for k in z3)
+        ok3f = set(z3f) == set(z3) and worst3f <= tol3 and all(abs(a - b) <= ltol * abs(b) for a, b in zip(l3f, l3))
+        failures += not ok3f
+        print(f"[rank {rank}] ZeRO-3 peer-memory gathers vs NCCL ({mopt}): losses {l3f} vs {l3}; worst param rel "
+              f"diff {worst3f:.1e} {'OK' if ok3f else 'FAIL'}", flush=True)
         print(f"[rank {rank}] ZeRO-3 vs ZeRO-2 ({mopt}) 3 steps: losses {l3} vs {l2}; worst "
               f"{[(k, f'{d:.1e}') for d, k in diffs[:4]]} (ZeRO-2 run-to-run {noise3:.1e}, losses {lnoise:.1e}) "
               f"{'OK' if ok else 'FAIL'}", flush=True)
