@@ -167,6 +167,20 @@ def run_attn(a: argparse.Namespace) -> dict:
         t_sb = time_fn(lambda: torch.autograd.grad(ot, (qt, kt, vt), dot, retain_graph=True), a.iters)
         res.update(sdpa_fwd_ms=t_sf, sdpa_bwd_ms=t_sb, sdpa_fwd_tflops=fwd_flop / t_sf / 1e9,
                    sdpa_bwd_tflops=2.5 * fwd_flop / t_sb / 1e9)
+        try:  # the flash-attn package: what the reference's attention dispatches to on this box
+            from flash_attn import flash_attn_func  # noqa: PLC0415
+        except ImportError:
+            flash_attn_func = None
+        if flash_attn_func is not None:
+            qf, kf, vf = (t.detach().requires_grad_() for t in (q, k, v))
+
+            def fa2_fwd():  # noqa: ANN202
+                return flash_attn_func(qf, kf, vf, causal=causal)
+
+            of = fa2_fwd()
+            t_ff = time_fn(fa2_fwd, a.iters)
+            t_fb = time_fn(lambda: torch.autograd.grad(of, (qf, kf, vf), do, retain_graph=True), a.iters)
+            res.update(flash_attn_fwd_ms=t_ff, flash_attn_bwd_ms=t_fb)
     return res
 
 
