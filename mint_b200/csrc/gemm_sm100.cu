@@ -435,6 +435,7 @@ struct CommParams {
   const int* rs_flag_local;      // RS: our flags [world][rs_flag_stride], block of source s at s * stride
   long long rs_flag_stride;      // RS: flags per source rank (>= Mc / 128 * tiles_n * 4)
   long long mc;                  // rows per chunk (M / world)
+  int rs_lag;                    // RS: own tile k follows the peers' tile k by this many 256-row tiles
   // GeGLU modes (COMM 3 forward, 4 backward; no communication)
   CUtensorMap geglu_map;         // 3: h [M, F] store map (32 x 64 bf16 boxes)
   const __nv_bfloat16* geglu_ab; // 4: the forward's [a | b] rows [M, 2F] (read by the epilogue)
@@ -454,8 +455,8 @@ __device__ __forceinline__ long long gathered_row_of(const CommParams& c, int p,
 // All-gather: own chunk first (its rows are local), then the peers' chunks in rotation order.
 // Reduce-scatter: peers' tiles and own tiles interleaved, so the pushes over NVLink spread over the
 // whole kernel instead of filling its first half: local tile index li contributes the peers' tiles
-// li and then this rank's own tile li - D (D = min(8, tiles per chunk) -- one tile group of the
-// schedule), the remaining own tiles come last. Every rank uses the same order, so a peer pushes
+// li and then this rank's own tile li - D (D = min(rs_lag, tiles per chunk); rs_lag = 8 by default:
+// one tile group of the schedule), the remaining own tiles come last. Every rank uses the same order, so a peer pushes
 // the partial of own tile k at an earlier ordinal than the one at which this rank reduces tile k.
 __device__ __forceinline__ int comm_tile_m(const CommParams& c, int o, int tiles_m2, bool own_first) {
   const int w = c.world;
@@ -466,7 +467,7 @@ __device__ __forceinline__ int comm_tile_m(const CommParams& c, int o, int tiles
     p = (c.rank + cp) % w;
     li = o % tpc;
   } else {
-    const int D = min(8, tpc);
+    const int D = min(c.rs_lag, tpc);
     const int head = D * (w - 1);
     if (o < head) {
       li = o / (w - 1);
@@ -1569,6 +1570,12 @@ void gemm_rs(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, bool b_k
       c.rs_push_map[q] = make_tmap_3d(c.rs_push[q], BF, 2, N, c.mc, 1, N, c.mc * N, 64, 32, 1, SW128);
     }
   }
+  // MINT_RS_LAG: how many 256-row tiles this rank's own tile k trails the peers' tile k (default 8)
+  static const int rs_lag = [] {
+    const char* e = std::getenv("MINT_RS_LAG");
+    return e == nullptr ? 8 : std::max(1, std::atoi(e));
+  }();
+  c.rs_lag = rs_lag;
   c.rs_recv = reinterpret_cast<const __nv_bfloat16*>(recv.data_ptr());
   c.rs_flag_local = flags.data_ptr<int>();
   const CUtensorMap ta = make_tmap_3d(A.data_ptr(), BF, 2, K, M, 1, A.stride(0), M * A.stride(0), 64, 128, 1, SW128);
