@@ -4,19 +4,17 @@
 //   warp 0      TMA producer: Q once, then K_j / V_j tiles into 2-stage rings (128B swizzle)
 //   warp 1      TMEM owner + single-thread MMA issue:
 //                 S_j = Q K_j^T   (M=128 queries, N=128 keys, K=128)  -> TMEM S buffer j%2
-//                 O  += P_j V_j   (M=128, N=128 head dims, K=128 keys, P read from tensor memory)
-//               S_{j+1} is issued before PV_j (once PV_{j-1} has read P_{j-1} from the columns
-//               S_{j+1} overwrites), so the softmax of tile j+1 overlaps PV_j.
+//                 O  += P_j V_j   (M=128, N=128 head dims, K=128 keys, P from shared memory)
+//               S_{j+1} is issued before PV_j so the softmax of tile j+1 overlaps PV_j.
 //   warps 4..   softmax, kSplit per TMEM lane quadrant: each thread owns kCols columns of one
 //               query row, loads its scores with tcgen05.ld, applies causal / sliding-window /
 //               document / sequence-end masks, exchanges its partial row maximum with the other
 //               parts of the row through shared memory (one mbarrier per quadrant), computes
 //               P = exp2(s * scale - m) two elements per instruction (packed fp32 FMA, bf16x2 MUFU
 //               exponential) with a lazily updated running max (its columns of O are rescaled in
-//               TMEM only when the max grows by more than 2^8), writes its part of P (bf16 pairs)
-//               over the first 64 columns of the tile's S buffer with one tcgen05.st (every part
-//               of the row has read its scores by then: the max exchange orders it), and finally
-//               normalizes its columns of O, stores them and the log-sum-exp.
+//               TMEM only when the max grows by more than 2^8), writes its part of P (bf16) in the
+//               128B-swizzled K-major layout the PV MMA reads, and finally normalizes its columns
+//               of O, stores them and the log-sum-exp.
 // Tiles outside the causal / window band are never visited. All waits are bounded.
 #include <cstdlib>
 
@@ -31,7 +29,6 @@ constexpr int kBN = 128;
 constexpr int kD = 128;
 constexpr int kSplit = 2;                       // softmax warps per TMEM lane quadrant (4 measured slower)
 constexpr int kCols = 128 / kSplit;              // score / output columns per softmax thread
-static_assert(kCols == 64, "P leaves each softmax thread as one 32-column tcgen05.st");
 constexpr int kThreads = (4 + 4 * kSplit) * 32;  // warp 0 TMA, warp 1 MMA, warps 4.. softmax
 constexpr int kTileBytes = kBM * kD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-wide swizzle atoms)
 constexpr int kAtomBytes = kTileBytes / 2;
@@ -60,6 +57,7 @@ struct Smem {
   uint8_t q[kTileBytes];
   uint8_t k[2][kTileBytes];
   uint8_t v[2][kTileBytes];
+  uint8_t p[kTileBytes];
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
@@ -106,15 +104,15 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint3
   }
 }
 
-// O += P V: P read from tensor memory (bf16 pairs in the first 64 columns of the tile's S buffer,
-// 16 keys = 8 columns per K step); V MN-major (head dim contiguous): atoms of 64 head dims x 128 key
-// rows (16 KB apart), 16 keys = 2048 bytes per K step.
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_addr, bool accumulate) {
+// O += P V: P K-major (keys contiguous, 2 atoms along K); V MN-major (head dim contiguous):
+// atoms of 64 head dims x 128 key rows (16 KB apart), 16 keys = 2048 bytes per K step.
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_addr, uint32_t v_addr, bool accumulate) {
   constexpr uint32_t idesc = umma_idesc_bf16(kBM, kD, false, true);
 #pragma unroll
   for (int k = 0; k < kBN / 16; ++k) {
-    umma_bf16_tmem_a(d_tmem, p_tmem + k * 8, umma_desc_sw128(v_addr + k * 2048, kAtomBytes, 1024), idesc,
-                     (accumulate || k > 0) ? 1u : 0u);
+    const uint32_t poff = (k >> 2) * kAtomBytes + (k & 3) * 32;
+    umma_bf16(d_tmem, umma_desc_sw128(p_addr + poff, 16, 1024), umma_desc_sw128(v_addr + k * 2048, kAtomBytes, 1024),
+              idesc, (accumulate || k > 0) ? 1u : 0u);
   }
 }
 
@@ -188,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {
       const uint32_t q_addr = smem_u32(s.q);
+      const uint32_t p_addr = smem_u32(s.p);
       bool ok = mbar_wait(&s.q_full, 0, p.status, kStatusTimeoutAttention, abort_flag);
       if (ok && (ok = mbar_wait(&s.k_full[0], 0, p.status, kStatusTimeoutAttention, abort_flag))) {
         tc_fence_after();
@@ -202,8 +201,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tr != nullptr && t < kTraceTiles) tr[t * 4] = clock64();
         if (t + 1 < n) {
           const int st = (t + 1) & 1;
-          // S_{t+1} overwrites the columns that held P_{t-1}: PV_{t-1} must have read them
-          if (t > 0 && !mbar_wait(&s.pv_done, (t - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
           if (!mbar_wait(&s.k_full[st], ((t + 1) >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
           tc_fence_after();
           if (!(p.diag & 2)) issue_qk(tmem + st * 128, q_addr, smem_u32(s.k[st]));
@@ -215,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tr != nullptr && t < kTraceTiles) tr[t * 4 + 2] = clock64();
         if (!mbar_wait(&s.v_full[t & 1], (t >> 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) break;
         tc_fence_after();
-        if (!(p.diag & 2)) issue_pv(tmem_o, tmem + (t & 1) * 128, smem_u32(s.v[t & 1]), t > 0);
+        if (!(p.diag & 2)) issue_pv(tmem_o, p_addr, smem_u32(s.v[t & 1]), t > 0);
         if (tr != nullptr && t < kTraceTiles) tr[t * 4 + 3] = clock64();
         umma_commit(&s.pv_done);
         umma_commit(&s.v_empty[t & 1]);
@@ -304,15 +301,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // combine with the other parts of the row; the buffer of this parity was last read two tiles
       // ago, before every warp of the quadrant arrived on the previous tile's exchange
       s.mx[t & 1][part][r] = mt;
-      // past this exchange every part of the row has read its scores: P may overwrite them
-      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.mx_full[q]);
       if (!mbar_wait_warp(&s.mx_full[q], t & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
         ok = false;
         break;
       }
-      tc_fence_after();
 #pragma unroll
       for (int o2 = 0; o2 < kSplit; ++o2) {
         if (o2 != part) mt = fmaxf(mt, s.mx[t & 1][o2][r]);
@@ -375,13 +369,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l += rs;
       FA_STAMP(6)
+      // the single P buffer is free once PV_{t-1} completed
+      if (t > 0 && pv_waited < t - 1) {
+        if (!mbar_wait_warp(&s.pv_done, (t - 1) & 1, p.status, kStatusTimeoutAttention, abort_flag)) {
+          ok = false;
+          break;
+        }
+        pv_waited = t - 1;
+      }
       FA_STAMP(7)
-      // P (bf16 pairs) over the first 64 columns of this tile's S buffer: this part's 32 words at
-      // column part * 32, where the PV MMA reads them
-      tmem_st_32x32b_x32(tmem + (t & 1) * 128 + lane_off + part * (kCols / 2),
-                         *reinterpret_cast<uint32_t(*)[32]>(pk));
-      tmem_st_wait();
+      // 128B-swizzled K-major store of this part of the row: 64-key swizzle atom cb / 64, 16-byte
+      // chunk (cb % 64) / 8 + c at that index ^ (row % 8)
+#pragma unroll
+      for (int c = 0; c < kCols / 8; ++c) {
+        const int chunk = (cb & 63) / 8 + c;
+        const uint4 v4 = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+        *reinterpret_cast<uint4*>(s.p + (cb >> 6) * kAtomBytes + r * 128 + ((chunk ^ (r & 7)) << 4)) = v4;
+      }
       FA_STAMP(8)
+      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.p_full);
